@@ -1,0 +1,294 @@
+/*
+ * orda.h -- C ABI of the B200 (sm_100a) ORDA distillation-loss library.
+ *
+ * This header is the drop-in boundary for the reference crate
+ * malcolmgreaves/orda-cutile-rs. Every type and entry point below names the
+ * reference item it replaces (path:line inside that crate). Plain C: no CUDA
+ * or torch types appear in any signature (streams are passed as void*).
+ *
+ * Two families of entry points:
+ *   - host-Mat entry (orda_distillation_loss): f32 host matrices in, callee
+ *     allocated f32 host gradients out, exactly the semantics of
+ *     `distillation_loss` (src/api.rs:188-422);
+ *   - device entry (orda_distillation_loss_device): bf16 device tensors,
+ *     fp32 device gradients, caller stream; the timed path.
+ *
+ * Status codes: 0 = Ok, non-zero = Err, with the message written to `err`
+ * (the reference returns `Result<_, String>`).
+ */
+#ifndef ORDA_H_
+#define ORDA_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ORDA_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define ORDA_API __attribute__((visibility("default")))
+#else
+#define ORDA_API
+#endif
+
+enum {
+  ORDA_OK = 0,
+  ORDA_ERR_INVALID = 1,   /* argument validation failed (src/api.rs:104-181) */
+  ORDA_ERR_BACKEND = 2,   /* backend unavailable (src/api.rs:197-207)       */
+  ORDA_ERR_CUDA = 3,      /* CUDA runtime / driver error                     */
+  ORDA_ERR_OOM = 4,       /* device allocation failed after the OOM ladder   */
+  ORDA_ERR_TIMEOUT = 5,   /* a bounded device wait expired                   */
+  ORDA_ERR_LABEL = 6      /* device-side label range check failed            */
+};
+
+/* Row-major f32 host matrix; replaces `Mat` (src/mat.rs:10-14). */
+typedef struct OrdaMatF32 {
+  const float* data;
+  size_t rows;
+  size_t cols;
+} OrdaMatF32;
+
+/* Callee-allocated f32 host matrix (output side of `Mat`). data == NULL
+ * encodes `None` for the optional gradients (src/api.rs:84-89). */
+typedef struct OrdaMatOut {
+  float* data;
+  size_t rows;
+  size_t cols;
+} OrdaMatOut;
+
+/* `TeacherMode` (src/teacher.rs:37-42). */
+typedef enum OrdaTeacherMode {
+  ORDA_TEACHER_TIED = 0,
+  ORDA_TEACHER_SEPARATE = 1,
+  ORDA_TEACHER_PRECOMPUTED = 2
+} OrdaTeacherMode;
+
+/* `Teacher::{Tied{hidden}, Separate{hidden,weight}, Precomputed{logits}}`
+ * (src/teacher.rs:11-32) as a tagged struct; unused members are ignored. */
+typedef struct OrdaTeacher {
+  OrdaTeacherMode mode;
+  OrdaMatF32 hidden; /* Tied, Separate   */
+  OrdaMatF32 weight; /* Separate         */
+  OrdaMatF32 logits; /* Precomputed      */
+} OrdaTeacher;
+
+/* `Reduction` (src/config.rs:11-17). */
+typedef enum OrdaReduction { ORDA_REDUCTION_MEAN = 0, ORDA_REDUCTION_SUM = 1 } OrdaReduction;
+
+/* `Backend` (src/config.rs:21-31). In this library Auto and Cuda select the
+ * B200 path; Cpu is rejected (the library ships no CPU path). */
+typedef enum OrdaBackend { ORDA_BACKEND_AUTO = 0, ORDA_BACKEND_CPU = 1, ORDA_BACKEND_CUDA = 2 } OrdaBackend;
+
+/* `Profile` (src/config.rs:35-42). */
+typedef enum OrdaProfile { ORDA_PROFILE_BALANCED = 0, ORDA_PROFILE_FAST = 1, ORDA_PROFILE_DEBUG = 2 } OrdaProfile;
+
+/* `KernelConfig` (src/config.rs:46-63). Option<T> fields carry a has_ flag. */
+typedef struct OrdaKernelConfig {
+  int32_t online_softmax;
+  int32_t fast_math;
+  int32_t quantize_grad_weight;
+  int32_t stochastic_rounding;
+  int32_t fp32_grad_weight_accumulation;
+  int32_t has_max_chunks;
+  size_t max_chunks;
+  size_t max_fused_size;
+  int32_t has_stochastic_seed;
+  uint64_t stochastic_seed;
+} OrdaKernelConfig;
+
+/* `ChunkSize::{Auto, Fixed(usize)}` (src/resolver.rs:10-16). */
+typedef enum OrdaChunkKind { ORDA_CHUNK_AUTO = 0, ORDA_CHUNK_FIXED = 1 } OrdaChunkKind;
+typedef struct OrdaChunkSize {
+  OrdaChunkKind kind;
+  size_t fixed_rows;
+} OrdaChunkSize;
+
+/* `ChunkPlan` (src/resolver.rs:40-45). */
+typedef struct OrdaChunkPlan {
+  size_t chunk_size;
+  size_t num_chunks;
+} OrdaChunkPlan;
+
+/* `LossOptions` (src/api.rs:25-47); `teacher_ce_weight: Option<f32>`. */
+typedef struct OrdaLossOptions {
+  float student_ce_weight;
+  int32_t has_teacher_ce_weight;
+  float teacher_ce_weight;
+  float kd_weight;
+  float temperature;
+  int64_t ignore_index;
+  float label_smoothing;
+  OrdaReduction reduction;
+  OrdaChunkSize chunk_size;
+  OrdaKernelConfig config;
+  OrdaBackend backend;
+} OrdaLossOptions;
+
+/* `DistillationLossOutput` (src/api.rs:71-92). Gradients are allocated by
+ * the library and released by orda_output_free(). */
+typedef struct OrdaOutput {
+  float loss;
+  float student_ce;
+  float teacher_ce;
+  float kl;
+  OrdaMatOut grad_student_hidden;
+  OrdaMatOut grad_weight;
+  OrdaMatOut grad_teacher_hidden; /* data == NULL: None */
+  OrdaMatOut grad_teacher_weight; /* data == NULL: None */
+  OrdaChunkPlan chunk_plan;
+} OrdaOutput;
+
+/* ---------------------------------------------------------------------------
+ * Configuration helpers (pure host logic, no device needed)
+ * ------------------------------------------------------------------------- */
+
+/* `LossOptions::default()` (src/api.rs:49-64). */
+ORDA_API void orda_loss_options_default(OrdaLossOptions* out);
+/* `KernelConfig::from_profile` (src/config.rs:81-93); Default = Balanced. */
+ORDA_API void orda_kernel_config_from_profile(OrdaProfile profile, OrdaKernelConfig* out);
+/* `KernelConfig::validate` (src/config.rs:106-119). */
+ORDA_API int orda_kernel_config_validate(const OrdaKernelConfig* cfg, char* err, size_t err_len);
+/* `is_power_of_two` (src/config.rs:122-124). */
+ORDA_API int orda_is_power_of_two(size_t value);
+/* `Teacher::default_teacher_ce_weight` (src/teacher.rs:54-59). */
+ORDA_API float orda_default_teacher_ce_weight(OrdaTeacherMode mode);
+/* `is_available` (src/lib.rs:70-79): 1 iff an sm_100 device is present. */
+ORDA_API int orda_is_available(void);
+
+/* `chunks_from_raw` (src/resolver.rs:28-36). */
+ORDA_API size_t orda_chunks_from_raw(double raw);
+/* `resolve_chunk_size` (src/resolver.rs:53-99). has_v / has_max_chunks
+ * encode the Option arguments. bt must be > 0 (returns {0,0} otherwise). */
+ORDA_API void orda_resolve_chunk_size(size_t bt, OrdaChunkSize chunk_size, int has_v, size_t v,
+                             int has_max_chunks, size_t max_chunks, OrdaChunkPlan* out);
+/* `default_max_chunks_limit` (src/resolver.rs:103-105). */
+ORDA_API size_t orda_default_max_chunks_limit(size_t bt);
+/* `chunk_doubling_schedule` (src/resolver.rs:114-126). Writes up to out_cap
+ * entries and returns the full schedule length. */
+ORDA_API size_t orda_chunk_doubling_schedule(size_t bt, size_t start, size_t limit, size_t* out, size_t out_cap);
+
+/* OOM retry ladder around `chunk_doubling_schedule` (src/resolver.rs:107-126,
+ * the upstream dispatcher's `dynamic_chunk` loop that the reference documents
+ * but never wires). Calls try_alloc(num_chunks, chunk_size, user) for each
+ * rung, starting at `start`; the first rung returning 0 wins and is written
+ * to `out`. Returns ORDA_OK, or ORDA_ERR_OOM when every rung failed. The
+ * device entry uses this with its workspace allocator. */
+typedef int (*OrdaTryAllocFn)(size_t num_chunks, size_t chunk_size, void* user);
+ORDA_API int orda_chunk_retry(size_t bt, size_t start, size_t limit, OrdaTryAllocFn try_alloc, void* user,
+                     OrdaChunkPlan* out);
+
+/* `validate` (src/api.rs:104-181) on host matrices. On success writes
+ * (V, H, BT). Messages are identical to the reference's. */
+ORDA_API int orda_validate(const OrdaMatF32* student_hidden, const OrdaMatF32* weight, const int64_t* labels,
+                  size_t n_labels, const OrdaTeacher* teacher, const OrdaLossOptions* opts, size_t* v_out,
+                  size_t* h_out, size_t* bt_out, char* err, size_t err_len);
+
+/* ---------------------------------------------------------------------------
+ * Host-Mat entry: `distillation_loss` (src/api.rs:188-422)
+ * ------------------------------------------------------------------------- */
+
+/* Computes loss, components and gradients on the B200 with the reference's
+ * semantics. Inputs are f32 host matrices (pinned or pageable); they are
+ * rounded to bf16 on the device (tensor-core operand type). Gradients come
+ * back as library-allocated f32 host matrices; free them with
+ * orda_output_free(). Runs on device 0 on an internal stream, synchronously. */
+ORDA_API int orda_distillation_loss(const OrdaMatF32* student_hidden, const OrdaMatF32* weight, const int64_t* labels,
+                           size_t n_labels, const OrdaTeacher* teacher, const OrdaLossOptions* opts,
+                           OrdaOutput* out, char* err, size_t err_len);
+ORDA_API void orda_output_free(OrdaOutput* out);
+
+/* ---------------------------------------------------------------------------
+ * Device entry (replaces the GPU launcher src/cuda/launch.rs:51-158, which
+ * covered only the KL + CE step; this covers the whole chunk loop)
+ * ------------------------------------------------------------------------- */
+
+typedef struct OrdaContext OrdaContext;
+
+/* A context owns the device workspace (logits chunk, dlogits group, row
+ * statistics) and a device status word. Use one context per stream. */
+ORDA_API int orda_context_create(int device, OrdaContext** out, char* err, size_t err_len);
+ORDA_API void orda_context_destroy(OrdaContext* ctx);
+/* Synchronizes the context's last stream and reports asynchronous device
+ * failures (label out of range, bounded-wait timeout). */
+ORDA_API int orda_context_check(OrdaContext* ctx, char* err, size_t err_len);
+/* Bytes of device workspace currently held by the context. */
+ORDA_API size_t orda_context_workspace_bytes(const OrdaContext* ctx);
+/* Test hook for the OOM ladder: the next `count` workspace allocations fail
+ * as if cudaMalloc had returned cudaErrorMemoryAllocation. */
+ORDA_API void orda_context_inject_alloc_failures(OrdaContext* ctx, int count);
+
+/* Element type of a device matrix. Hidden states and weights are bf16 (the
+ * tensor-core operand type); Precomputed teacher logits may be bf16 or f32. */
+typedef enum OrdaDType { ORDA_DTYPE_BF16 = 0, ORDA_DTYPE_F32 = 1 } OrdaDType;
+
+/* Device matrix, row-major with leading dimension `ld` (elements).
+ * Requirements: data 16-byte aligned, ld * sizeof(elem) a multiple of 16,
+ * ld >= cols. */
+typedef struct OrdaDeviceMat {
+  const void* data;
+  size_t rows;
+  size_t cols;
+  size_t ld;
+  OrdaDType dtype;
+} OrdaDeviceMat;
+
+typedef struct OrdaDeviceTeacher {
+  OrdaTeacherMode mode;
+  OrdaDeviceMat hidden; /* Tied [BT,H], Separate [BT,H_t]          */
+  OrdaDeviceMat weight; /* Separate [V,H_t]                         */
+  OrdaDeviceMat logits; /* Precomputed [BT,V]                       */
+} OrdaDeviceTeacher;
+
+/* fp32 device outputs; leading dimensions in elements. */
+typedef struct OrdaDeviceOutputs {
+  float* grad_student_hidden; size_t ld_grad_student_hidden; /* [BT,H], required              */
+  float* grad_weight; size_t ld_grad_weight;                 /* [V,H], required               */
+  float* grad_teacher_hidden; size_t ld_grad_teacher_hidden; /* [BT,H_t] iff w_t>0, Tied|Sep  */
+  float* grad_teacher_weight; size_t ld_grad_teacher_weight; /* [V,H_t] iff w_t>0, Separate   */
+  int8_t* grad_weight_q;     /* optional [V,H] int8, ld = H, when quantize_grad_weight           */
+  float* grad_weight_scale;  /* optional [V] per-row scales, when quantize_grad_weight           */
+  float* scalars;            /* required device float[4]: loss, student_ce, teacher_ce, kl      */
+} OrdaDeviceOutputs;
+
+/* Sharding extras for data-parallel callers (rows split across ranks). */
+typedef struct OrdaShardOptions {
+  int64_t global_non_ignore; /* > 0: use this token count as the mean denominator */
+  int32_t skip_quantize;     /* 1: leave grad_W un-quantized (quantize after the reduction) */
+} OrdaShardOptions;
+
+/* The timed path. Enqueues everything on `stream` (a cudaStream_t; NULL =
+ * legacy default stream); no host synchronization. labels is a device int64
+ * array of length bt. `plan_out` (optional) receives the chunk plan used. */
+ORDA_API int orda_distillation_loss_device(OrdaContext* ctx, const OrdaDeviceMat* student_hidden,
+                                  const OrdaDeviceMat* weight, const int64_t* labels, size_t bt,
+                                  const OrdaDeviceTeacher* teacher, const OrdaLossOptions* opts,
+                                  const OrdaDeviceOutputs* out, const OrdaShardOptions* shard,
+                                  void* stream, OrdaChunkPlan* plan_out, char* err, size_t err_len);
+
+/* INT8 row-wise grad_W quantisation on the device: `quantize_grad_w` +
+ * `dequantize_grad_w(.., 1.0)` (src/quant.rs:157-202). grad_w [V,H] fp32 is
+ * overwritten with the dequantized values (target rows kept exact); q and
+ * scale (optional) receive the INT8 body and per-row scales. Bit-exact with
+ * the reference on the same fp32 input. */
+ORDA_API int orda_quantize_grad_w_device(OrdaContext* ctx, float* grad_w, size_t v, size_t h, size_t ld,
+                                const int64_t* labels, size_t bt, int64_t ignore_index, int stochastic,
+                                uint64_t seed, int8_t* q, float* scale, void* stream, char* err,
+                                size_t err_len);
+
+/* bf16 tensor-core GEMM used by the chunk loop, exposed for unit tests:
+ *   C[M,N] (fp32, ldc) = alpha * op(A) @ op(B) + (beta != 0 ? C : 0)
+ * a_kind: 0 = A stored [M,K] (K contiguous), 1 = A stored [K,M] (M contiguous)
+ * b_kind: 0 = B stored [N,K] (K contiguous), 1 = B stored [K,N] (N contiguous)
+ * A and B are bf16 device pointers with leading dimensions lda, ldb. */
+ORDA_API int orda_gemm_bf16_device(OrdaContext* ctx, const void* a, size_t lda, int a_kind, const void* b, size_t ldb,
+                          int b_kind, float* c, size_t ldc, size_t m, size_t n, size_t k, float alpha,
+                          float beta, void* stream, char* err, size_t err_len);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ORDA_H_ */

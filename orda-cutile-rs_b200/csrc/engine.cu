@@ -1,0 +1,851 @@
+// engine.cu -- the chunk-loop orchestrator and the C ABI entry points.
+//
+// Device flow of one `distillation_loss` call (src/api.rs:188-422), all
+// enqueued on the caller's stream with no host synchronisation:
+//   label pass      count non-ignored labels, range check, mean scale,
+//                   target-row flags for the quantiser
+//   for each chunk (the resolver's plan, src/resolver.rs:53-99):
+//     [teacher GEMM] teacher logits (Tied/Separate) -> fp32 chunk buffer
+//     student GEMM   student logits -> fp32 chunk buffer + online-softmax
+//                    records (own and paired-teacher statistics, KL term)
+//     row kernel     per-row NLL / KL, bf16 logit gradients into the group
+//                    buffer (the merged CE + KL gradient of src/api.rs:319-344)
+//   per group of chunks (all chunks when the dlogits of the whole batch fit
+//   the memory budget, which holds for every BASELINE configuration):
+//     dgrad GEMM     grad_hidden rows = mean_scale * dlogits @ W
+//     wgrad GEMM     grad_W (+)= mean_scale * dlogits^T @ hidden
+//                    (Tied: student and teacher rows as two K segments)
+//   finalize        deterministic f64 reduction of the per-row losses
+//   quantise        optional INT8 round trip of grad_W (src/quant.rs)
+// Deferring the backward GEMMs to a group turns the per-chunk K=chunk_size
+// wgrad (a read-modify-write of the fp32 grad_W per chunk) into one GEMM with
+// K = group rows; the loss and gradients are chunk-invariant
+// (tests/end_to_end.rs:230-278), so results do not depend on the grouping.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <memory>
+#include <mutex>
+#include <vector>
+
+#include "../../include/orda.h"
+#include "host_logic.h"
+#include "kernels.h"
+#include "ptx.cuh"
+
+struct OrdaContext {
+  int device = 0;
+  int num_sms = 148;
+  int* d_words = nullptr;  // [0] status, [1] n_non_ignore
+  float* d_mean_scale = nullptr;
+  void* ws = nullptr;
+  size_t ws_bytes = 0;
+  void* stage = nullptr;
+  size_t stage_bytes = 0;
+  int inject_fail = 0;
+  cudaStream_t last_stream = nullptr;
+  cudaStream_t own_stream = nullptr;
+  std::mutex mu;
+};
+
+namespace orda {
+namespace {
+
+size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+struct DevInputs {
+  MatRef hs, w, ht, wt;     // bf16
+  const void* t_logits = nullptr;
+  long long ld_t_logits = 0;
+  bool t_logits_bf16 = true;
+  const int64_t* labels = nullptr;
+  size_t bt = 0, h = 0, v = 0, ht_dim = 0;
+  OrdaTeacherMode mode = ORDA_TEACHER_TIED;
+};
+
+struct Flags {
+  float w_s, w_t, kd, temperature, alpha;
+  bool need_teacher, teacher_rows, teacher_grad, teacher_ce, pair, quant;
+};
+
+struct WsLayout {
+  size_t logits = 0, rec_own = 0, rec_own_t = 0, rec_pair = 0, dlog_s = 0, dlog_t = 0, nll_s = 0, nll_t = 0,
+         kl = 0, flags = 0, total = 0;
+  size_t ldv = 0, ldd = 0, parts = 0, cs = 0, group_rows = 0;
+};
+
+WsLayout make_layout(const DevInputs& in, const Flags& f, size_t cs, size_t group_rows) {
+  WsLayout L;
+  L.cs = cs;
+  L.group_rows = group_rows;
+  L.ldv = round_up(in.v, 8);
+  L.ldd = round_up(in.v, 8);
+  L.parts = (in.v + 127) / 128;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off = round_up(off + bytes, 256);
+    return o;
+  };
+  L.logits = take((f.teacher_rows ? 2 : 1) * cs * L.ldv * sizeof(float));
+  L.rec_own = take(cs * L.parts * 16);
+  L.rec_own_t = take(f.teacher_rows ? cs * L.parts * 16 : 0);
+  L.rec_pair = take(f.pair ? cs * L.parts * 32 : 0);
+  L.dlog_s = take(group_rows * L.ldd * 2);
+  L.dlog_t = take(f.teacher_grad ? group_rows * L.ldd * 2 : 0);
+  L.nll_s = take(in.bt * sizeof(float));
+  L.nll_t = take(in.bt * sizeof(float));
+  L.kl = take(in.bt * sizeof(double));
+  L.flags = take(f.quant ? in.v : 0);
+  L.total = off;
+  return L;
+}
+
+cudaError_t ensure_ws(OrdaContext* ctx, size_t bytes) {
+  if (ctx->inject_fail > 0) {
+    --ctx->inject_fail;
+    return cudaErrorMemoryAllocation;
+  }
+  if (ctx->ws_bytes >= bytes) return cudaSuccess;
+  if (ctx->ws) {
+    cudaFree(ctx->ws);
+    ctx->ws = nullptr;
+    ctx->ws_bytes = 0;
+  }
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess) {
+    cudaGetLastError();  // clear the sticky-free allocation error
+    return e;
+  }
+  ctx->ws = p;
+  ctx->ws_bytes = bytes;
+  return cudaSuccess;
+}
+
+struct AllocTry {
+  OrdaContext* ctx;
+  const DevInputs* in;
+  const Flags* f;
+  WsLayout layout;
+};
+
+// Workspace for a rung of the OOM ladder: the chunk buffers plus the dlogits
+// group buffer, whose depth (chunks per backward-GEMM group) is the largest
+// that keeps the group within 60% of the memory this call may use.
+int try_alloc_cb(size_t num_chunks, size_t chunk_size, void* user) {
+  AllocTry* t = static_cast<AllocTry*>(user);
+  size_t free_b = 0, total_b = 0;
+  cudaMemGetInfo(&free_b, &total_b);
+  const size_t avail = free_b + t->ctx->ws_bytes;
+  const WsLayout base = make_layout(*t->in, *t->f, chunk_size, 0);
+  const size_t per_chunk = chunk_size * base.ldd * 2 * (t->f->teacher_grad ? 2 : 1);
+  size_t g = num_chunks;
+  const size_t budget = avail > base.total ? static_cast<size_t>((avail - base.total) * 0.6) : 0;
+  if (per_chunk > 0) g = std::min(num_chunks, std::max<size_t>(1, budget / per_chunk));
+  const size_t group_rows = std::min(g * chunk_size, t->in->bt);
+  WsLayout L = make_layout(*t->in, *t->f, chunk_size, group_rows);
+  if (ensure_ws(t->ctx, L.total) != cudaSuccess) return 1;
+  t->layout = L;
+  return 0;
+}
+
+int cuda_fail(cudaError_t e, const char* what, char* err, size_t len) {
+  set_error(err, len, "CUDA error in %s: %s", what, cudaGetErrorString(e));
+  return ORDA_ERR_CUDA;
+}
+
+int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, const OrdaDeviceOutputs& out,
+               const OrdaShardOptions* shard, cudaStream_t st, OrdaChunkPlan* plan_out, char* err, size_t len) {
+  Flags f{};
+  f.w_s = o.student_ce_weight;
+  f.w_t = o.has_teacher_ce_weight ? o.teacher_ce_weight : orda_default_teacher_ce_weight(in.mode);
+  if (f.w_t < 0.0f) {
+    set_error(err, len, "teacher_ce_weight must be >= 0, got %s", fmt_f32(f.w_t).c_str());
+    return ORDA_ERR_INVALID;
+  }
+  f.kd = o.kd_weight;
+  f.temperature = o.temperature;
+  f.alpha = o.label_smoothing;
+  f.need_teacher = f.kd > 0.0f || f.w_t > 0.0f;
+  const bool live_teacher = in.mode == ORDA_TEACHER_TIED || in.mode == ORDA_TEACHER_SEPARATE;
+  f.teacher_rows = f.need_teacher && live_teacher;
+  f.teacher_grad = f.w_t > 0.0f && live_teacher;
+  f.teacher_ce = f.w_t > 0.0f;
+  f.pair = f.kd > 0.0f || (f.w_t > 0.0f && in.mode == ORDA_TEACHER_PRECOMPUTED);
+  f.quant = o.config.quantize_grad_weight != 0 && !(shard && shard->skip_quantize);
+
+  if (!out.grad_student_hidden || !out.grad_weight || !out.scalars) {
+    set_error(err, len, "grad_student_hidden, grad_weight and scalars outputs are required");
+    return ORDA_ERR_INVALID;
+  }
+  if (f.teacher_grad && !out.grad_teacher_hidden) {
+    set_error(err, len, "grad_teacher_hidden output is required (teacher CE weight > 0 with a live teacher)");
+    return ORDA_ERR_INVALID;
+  }
+  if (f.teacher_grad && in.mode == ORDA_TEACHER_SEPARATE && !out.grad_teacher_weight) {
+    set_error(err, len, "grad_teacher_weight output is required (Separate teacher with teacher CE weight > 0)");
+    return ORDA_ERR_INVALID;
+  }
+
+  const size_t bt = in.bt, v = in.v, h = in.h, ht = in.ht_dim;
+  OrdaChunkPlan plan = resolve_chunk_size(bt, o.chunk_size, true, v, o.config.has_max_chunks != 0,
+                                          o.config.max_chunks);
+  const size_t limit = o.config.has_max_chunks ? o.config.max_chunks : default_max_chunks_limit(bt);
+  AllocTry at{ctx, &in, &f, {}};
+  OrdaChunkPlan used{};
+  // Rung 0 is the resolver's plan itself (a Fixed chunk size keeps its row
+  // count); after an allocation failure the ladder doubles the chunk count
+  // along chunk_doubling_schedule, as the upstream dispatcher does.
+  bool have = try_alloc_cb(plan.num_chunks, plan.chunk_size, &at) == 0;
+  if (have) used = plan;
+  if (!have) {
+    for (size_t nc : chunk_doubling_schedule(bt, plan.num_chunks, std::max(limit, plan.num_chunks))) {
+      if (nc <= plan.num_chunks) continue;
+      const size_t cs_r = ceil_div(bt, nc);
+      if (try_alloc_cb(nc, cs_r, &at) == 0) {
+        used = OrdaChunkPlan{cs_r, nc};
+        have = true;
+        break;
+      }
+    }
+  }
+  if (!have) {
+    set_error(err, len, "device workspace allocation failed for every chunk count of the OOM ladder");
+    return ORDA_ERR_OOM;
+  }
+  const WsLayout& L = at.layout;
+  if (plan_out) *plan_out = used;
+
+  uint8_t* ws = static_cast<uint8_t*>(ctx->ws);
+  float* logits = reinterpret_cast<float*>(ws + L.logits);
+  float* logits_t = logits + L.cs * L.ldv;
+  float* rec_own = reinterpret_cast<float*>(ws + L.rec_own);
+  float* rec_own_t = reinterpret_cast<float*>(ws + L.rec_own_t);
+  float* rec_pair = reinterpret_cast<float*>(ws + L.rec_pair);
+  uint16_t* dlog_s = reinterpret_cast<uint16_t*>(ws + L.dlog_s);
+  uint16_t* dlog_t = reinterpret_cast<uint16_t*>(ws + L.dlog_t);
+  float* nll_s = reinterpret_cast<float*>(ws + L.nll_s);
+  float* nll_t = reinterpret_cast<float*>(ws + L.nll_t);
+  double* kl_rows = reinterpret_cast<double*>(ws + L.kl);
+  uint8_t* tflags = f.quant ? ws + L.flags : nullptr;
+  int* status = ctx->d_words;
+
+  cudaError_t e;
+  if ((e = cudaMemsetAsync(ctx->d_words, 0, 2 * sizeof(int), st)) != cudaSuccess) return cuda_fail(e, "memset", err, len);
+  if (tflags && (e = cudaMemsetAsync(tflags, 0, v, st)) != cudaSuccess) return cuda_fail(e, "memset", err, len);
+  const long long denom_override = shard ? shard->global_non_ignore : 0;
+  launch_label_prep(in.labels, static_cast<long long>(bt), static_cast<long long>(v), o.ignore_index,
+                    o.reduction == ORDA_REDUCTION_SUM, denom_override, ctx->d_words + 1, ctx->d_mean_scale, tflags,
+                    status, st);
+
+  const float inv_t = 1.0f / f.temperature;
+  const char* why = nullptr;
+  const size_t cs = used.chunk_size;
+  const size_t group_rows = L.group_rows;
+  for (size_t g0 = 0; g0 < bt; g0 += group_rows) {
+    const size_t g1 = std::min(g0 + group_rows, bt);
+    for (size_t s = g0; s < g1; s += cs) {
+      const size_t n = std::min(cs, g1 - s);
+      // ---- teacher logits (Tied / Separate)
+      if (f.teacher_rows) {
+        GemmDesc gd;
+        const MatRef& tw = in.mode == ORDA_TEACHER_TIED ? in.w : in.wt;
+        const size_t kdim = in.mode == ORDA_TEACHER_TIED ? h : ht;
+        gd.a[0] = MatRef{static_cast<const uint16_t*>(in.ht.ptr) + s * in.ht.ld, static_cast<long long>(n),
+                         static_cast<long long>(kdim), in.ht.ld};
+        gd.b[0] = tw;
+        gd.k_seg[0] = static_cast<long long>(kdim);
+        gd.M = static_cast<long long>(n);
+        gd.N = static_cast<long long>(v);
+        gd.epi = Epi::Logits;
+        gd.status = status;
+        EpiArgs& ea = gd.args;
+        ea.logits = logits_t;
+        ea.ldl = static_cast<long long>(L.ldv);
+        ea.rec_own = rec_own_t;
+        ea.n_parts = static_cast<int>(L.parts);
+        ea.inv_t = inv_t;
+        ea.own_d1 = f.teacher_ce;
+        ea.own_sx = f.teacher_ce && f.alpha > 0.0f;
+        if ((e = gemm_launch(gd, ctx->num_sms, st, &why)) != cudaSuccess)
+          return cuda_fail(e, why ? why : "teacher logits GEMM", err, len);
+      }
+      // ---- student logits + statistics
+      {
+        GemmDesc gd;
+        gd.a[0] = MatRef{static_cast<const uint16_t*>(in.hs.ptr) + s * in.hs.ld, static_cast<long long>(n),
+                         static_cast<long long>(h), in.hs.ld};
+        gd.b[0] = in.w;
+        gd.k_seg[0] = static_cast<long long>(h);
+        gd.M = static_cast<long long>(n);
+        gd.N = static_cast<long long>(v);
+        gd.epi = Epi::Logits;
+        gd.status = status;
+        EpiArgs& ea = gd.args;
+        ea.logits = logits;
+        ea.ldl = static_cast<long long>(L.ldv);
+        ea.rec_own = rec_own;
+        ea.rec_pair = rec_pair;
+        ea.n_parts = static_cast<int>(L.parts);
+        ea.inv_t = inv_t;
+        ea.own_d1 = 1;
+        ea.own_dT = f.kd > 0.0f;
+        ea.own_sx = f.alpha > 0.0f;
+        ea.pair = f.pair;
+        if (f.pair) {
+          if (live_teacher) {
+            ea.pair_src = logits_t;
+            ea.ld_pair = static_cast<long long>(L.ldv);
+            ea.pair_is_bf16 = 0;
+          } else {
+            const size_t esz = in.t_logits_bf16 ? 2 : 4;
+            ea.pair_src = static_cast<const uint8_t*>(in.t_logits) + s * in.ld_t_logits * esz;
+            ea.ld_pair = in.ld_t_logits;
+            ea.pair_is_bf16 = in.t_logits_bf16;
+            ea.pair_d1 = f.teacher_ce;
+            ea.pair_sx = f.teacher_ce && f.alpha > 0.0f;
+          }
+        }
+        if ((e = gemm_launch(gd, ctx->num_sms, st, &why)) != cudaSuccess)
+          return cuda_fail(e, why ? why : "student logits GEMM", err, len);
+      }
+      // ---- row pass: losses and logit gradients
+      {
+        RowArgs r{};
+        r.n = static_cast<int>(n);
+        r.v = static_cast<int>(v);
+        r.n_parts = static_cast<int>(L.parts);
+        r.logits_s = logits;
+        r.ldl = static_cast<long long>(L.ldv);
+        if (live_teacher) {
+          r.teacher = logits_t;
+          r.ld_teacher = static_cast<long long>(L.ldv);
+          r.teacher_is_bf16 = 0;
+        } else {
+          const size_t esz = in.t_logits_bf16 ? 2 : 4;
+          r.teacher = static_cast<const uint8_t*>(in.t_logits) + s * in.ld_t_logits * esz;
+          r.ld_teacher = in.ld_t_logits;
+          r.teacher_is_bf16 = in.t_logits_bf16;
+        }
+        r.rec_own = rec_own;
+        r.rec_own_t = rec_own_t;
+        r.rec_pair = rec_pair;
+        r.labels = in.labels + s;
+        r.ignore_index = o.ignore_index;
+        r.w_s = f.w_s;
+        r.w_t = f.w_t;
+        r.kd = f.kd;
+        r.temperature = f.temperature;
+        r.inv_t = inv_t;
+        r.alpha = f.alpha;
+        r.need_kl = f.kd > 0.0f;
+        r.teacher_ce = f.teacher_ce;
+        r.teacher_ce_from_own = live_teacher;
+        r.teacher_grad = f.teacher_grad;
+        r.dlog_s = dlog_s + (s - g0) * L.ldd;
+        r.dlog_t = f.teacher_grad ? dlog_t + (s - g0) * L.ldd : nullptr;
+        r.ldd = static_cast<long long>(L.ldd);
+        r.nll_s_rows = nll_s + s;
+        r.nll_t_rows = nll_t + s;
+        r.kl_rows = kl_rows + s;
+        launch_rows(r, st);
+        if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(e, "row kernel", err, len);
+      }
+    }
+    const long long rows_g = static_cast<long long>(g1 - g0);
+    const long long vv = static_cast<long long>(v);
+    // ---- dgrad: grad_h rows = mean_scale * dlogits @ W
+    auto dgrad = [&](const uint16_t* dl, const MatRef& wmat, long long ncols, float* outp, size_t ldo) -> int {
+      GemmDesc gd;
+      gd.a[0] = MatRef{dl, rows_g, vv, static_cast<long long>(L.ldd)};
+      gd.b_mn_major = true;
+      gd.b[0] = MatRef{wmat.ptr, vv, ncols, wmat.ld};
+      gd.k_seg[0] = vv;
+      gd.M = rows_g;
+      gd.N = ncols;
+      gd.raster_n_fastest = true;
+      gd.status = status;
+      gd.args.out0 = outp + g0 * ldo;
+      gd.args.ld0 = static_cast<long long>(ldo);
+      gd.args.alpha_ptr = ctx->d_mean_scale;
+      cudaError_t ee = gemm_launch(gd, ctx->num_sms, st, &why);
+      if (ee != cudaSuccess) return cuda_fail(ee, why ? why : "dgrad GEMM", err, len);
+      return ORDA_OK;
+    };
+    if (int rc = dgrad(dlog_s, in.w, static_cast<long long>(h), out.grad_student_hidden, out.ld_grad_student_hidden))
+      return rc;
+    if (f.teacher_grad) {
+      const MatRef& tw = in.mode == ORDA_TEACHER_TIED ? in.w : in.wt;
+      const long long tn = static_cast<long long>(in.mode == ORDA_TEACHER_TIED ? h : ht);
+      if (int rc = dgrad(dlog_t, tw, tn, out.grad_teacher_hidden, out.ld_grad_teacher_hidden)) return rc;
+    }
+    // ---- wgrad: grad_W (+)= mean_scale * dlogits^T @ hidden
+    {
+      GemmDesc gd;
+      gd.a_mn_major = true;
+      gd.b_mn_major = true;
+      gd.a[0] = MatRef{dlog_s, rows_g, vv, static_cast<long long>(L.ldd)};
+      gd.b[0] = MatRef{static_cast<const uint16_t*>(in.hs.ptr) + g0 * in.hs.ld, rows_g, static_cast<long long>(h),
+                       in.hs.ld};
+      gd.k_seg[0] = rows_g;
+      if (f.teacher_grad && in.mode == ORDA_TEACHER_TIED) {
+        gd.nseg = 2;
+        gd.a[1] = MatRef{dlog_t, rows_g, vv, static_cast<long long>(L.ldd)};
+        gd.b[1] = MatRef{static_cast<const uint16_t*>(in.ht.ptr) + g0 * in.ht.ld, rows_g, static_cast<long long>(h),
+                         in.ht.ld};
+        gd.k_seg[1] = rows_g;
+      }
+      gd.M = vv;
+      gd.N = static_cast<long long>(h);
+      gd.raster_n_fastest = true;
+      gd.status = status;
+      gd.args.out0 = out.grad_weight;
+      gd.args.ld0 = static_cast<long long>(out.ld_grad_weight);
+      gd.args.alpha_ptr = ctx->d_mean_scale;
+      gd.args.beta = g0 > 0 ? 1.0f : 0.0f;
+      if ((e = gemm_launch(gd, ctx->num_sms, st, &why)) != cudaSuccess)
+        return cuda_fail(e, why ? why : "wgrad GEMM", err, len);
+    }
+    if (f.teacher_grad && in.mode == ORDA_TEACHER_SEPARATE) {
+      GemmDesc gd;
+      gd.a_mn_major = true;
+      gd.b_mn_major = true;
+      gd.a[0] = MatRef{dlog_t, rows_g, vv, static_cast<long long>(L.ldd)};
+      gd.b[0] = MatRef{static_cast<const uint16_t*>(in.ht.ptr) + g0 * in.ht.ld, rows_g, static_cast<long long>(ht),
+                       in.ht.ld};
+      gd.k_seg[0] = rows_g;
+      gd.M = vv;
+      gd.N = static_cast<long long>(ht);
+      gd.raster_n_fastest = true;
+      gd.status = status;
+      gd.args.out0 = out.grad_teacher_weight;
+      gd.args.ld0 = static_cast<long long>(out.ld_grad_teacher_weight);
+      gd.args.alpha_ptr = ctx->d_mean_scale;
+      gd.args.beta = g0 > 0 ? 1.0f : 0.0f;
+      if ((e = gemm_launch(gd, ctx->num_sms, st, &why)) != cudaSuccess)
+        return cuda_fail(e, why ? why : "teacher wgrad GEMM", err, len);
+    }
+  }
+  launch_finalize(nll_s, nll_t, kl_rows, static_cast<long long>(bt), ctx->d_mean_scale, f.w_s, f.w_t, f.kd,
+                  out.scalars, st);
+  if (f.quant) {
+    const uint64_t seed = o.config.has_stochastic_seed ? o.config.stochastic_seed : 0;
+    launch_quant(out.grad_weight, static_cast<long long>(v), static_cast<long long>(h),
+                 static_cast<long long>(out.ld_grad_weight), tflags, o.config.stochastic_rounding, seed,
+                 out.grad_weight_q, out.grad_weight_scale, st);
+  }
+  if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(e, "kernel launch", err, len);
+  ctx->last_stream = st;
+  return ORDA_OK;
+}
+
+// --------------------------------------------------------------- helpers
+bool device_is_sm100(int dev) {
+  cudaDeviceProp p;
+  if (cudaGetDeviceProperties(&p, dev) != cudaSuccess) return false;
+  return p.major == 10;
+}
+
+int check_status(OrdaContext* ctx, char* err, size_t len) {
+  int words[2] = {0, 0};
+  cudaError_t e = cudaStreamSynchronize(ctx->last_stream);
+  if (e != cudaSuccess) return cuda_fail(e, "stream synchronize", err, len);
+  e = cudaMemcpy(words, ctx->d_words, sizeof words, cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(e, "status read", err, len);
+  if (words[0] == DEV_LABEL_RANGE) {
+    set_error(err, len, "a label is out of range [0, V) and != ignore_index (device label check)");
+    return ORDA_ERR_LABEL;
+  }
+  if (words[0] != DEV_OK) {
+    set_error(err, len, "a bounded device wait expired (status 0x%x); results are invalid", words[0]);
+    return ORDA_ERR_TIMEOUT;
+  }
+  return ORDA_OK;
+}
+
+std::mutex g_default_mu;
+OrdaContext* g_default_ctx[64] = {nullptr};
+
+}  // namespace
+}  // namespace orda
+
+using namespace orda;
+
+extern "C" {
+
+int orda_is_available(void) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || n <= 0) {
+    cudaGetLastError();
+    return 0;
+  }
+  return device_is_sm100(0) ? 1 : 0;
+}
+
+int orda_context_create(int device, OrdaContext** out, char* err, size_t err_len) {
+  *out = nullptr;
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n) {
+    cudaGetLastError();
+    set_error(err, err_len, "no CUDA device %d available (this library has no CPU path)", device);
+    return ORDA_ERR_BACKEND;
+  }
+  if (!device_is_sm100(device)) {
+    set_error(err, err_len, "device %d is not an sm_100 (B200-class) GPU", device);
+    return ORDA_ERR_BACKEND;
+  }
+  cudaError_t e = cudaSetDevice(device);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice", err, err_len);
+  std::unique_ptr<OrdaContext> ctx(new OrdaContext());
+  ctx->device = device;
+  cudaDeviceGetAttribute(&ctx->num_sms, cudaDevAttrMultiProcessorCount, device);
+  if ((e = cudaMalloc(&ctx->d_words, 4 * sizeof(int))) != cudaSuccess) return cuda_fail(e, "cudaMalloc", err, err_len);
+  if ((e = cudaMalloc(&ctx->d_mean_scale, 4 * sizeof(float))) != cudaSuccess)
+    return cuda_fail(e, "cudaMalloc", err, err_len);
+  cudaMemset(ctx->d_words, 0, 4 * sizeof(int));
+  *out = ctx.release();
+  return ORDA_OK;
+}
+
+void orda_context_destroy(OrdaContext* ctx) {
+  if (!ctx) return;
+  cudaSetDevice(ctx->device);
+  cudaDeviceSynchronize();
+  cudaFree(ctx->ws);
+  cudaFree(ctx->stage);
+  cudaFree(ctx->d_words);
+  cudaFree(ctx->d_mean_scale);
+  if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
+  delete ctx;
+}
+
+int orda_context_check(OrdaContext* ctx, char* err, size_t err_len) {
+  if (!ctx) return ORDA_ERR_INVALID;
+  cudaSetDevice(ctx->device);
+  return check_status(ctx, err, err_len);
+}
+
+size_t orda_context_workspace_bytes(const OrdaContext* ctx) { return ctx ? ctx->ws_bytes : 0; }
+
+void orda_context_inject_alloc_failures(OrdaContext* ctx, int count) {
+  if (ctx) ctx->inject_fail = count;
+}
+
+static bool dev_mat_ok(const OrdaDeviceMat& m, bool need_bf16) {
+  if (need_bf16 && m.dtype != ORDA_DTYPE_BF16) return false;
+  const size_t esz = m.dtype == ORDA_DTYPE_BF16 ? 2 : 4;
+  if (!m.data) return false;
+  if ((reinterpret_cast<uintptr_t>(m.data) & 15) != 0) return false;
+  if ((m.ld * esz) % 16 != 0 || m.ld < m.cols) return false;
+  return true;
+}
+
+int orda_distillation_loss_device(OrdaContext* ctx, const OrdaDeviceMat* student_hidden, const OrdaDeviceMat* weight,
+                                  const int64_t* labels, size_t bt, const OrdaDeviceTeacher* teacher,
+                                  const OrdaLossOptions* opts, const OrdaDeviceOutputs* out,
+                                  const OrdaShardOptions* shard, void* stream, OrdaChunkPlan* plan_out, char* err,
+                                  size_t err_len) {
+  if (!ctx || !student_hidden || !weight || !labels || !teacher || !opts || !out) {
+    set_error(err, err_len, "null argument");
+    return ORDA_ERR_INVALID;
+  }
+  std::lock_guard<std::mutex> lock(ctx->mu);
+  const Shape2 sh{student_hidden->rows, student_hidden->cols}, w{weight->rows, weight->cols};
+  const Shape2 th{teacher->hidden.rows, teacher->hidden.cols}, tw{teacher->weight.rows, teacher->weight.cols},
+      tl{teacher->logits.rows, teacher->logits.cols};
+  size_t v = 0, h = 0, bt_chk = 0;
+  if (int rc = validate_shapes(sh, w, bt, teacher->mode, th, tw, tl, *opts, &v, &h, &bt_chk, err, err_len)) return rc;
+  if (int rc = validate_scalars_and_teacher(bt_chk, h, v, teacher->mode, th, tw, tl, *opts, err, err_len)) return rc;
+  if (opts->backend == ORDA_BACKEND_CPU) {
+    set_error(err, err_len, "Backend::Cpu is not available: this library is the B200 path and has no CPU backend");
+    return ORDA_ERR_BACKEND;
+  }
+  if (!dev_mat_ok(*student_hidden, true) || !dev_mat_ok(*weight, true)) {
+    set_error(err, err_len, "student_hidden and weight must be bf16, 16-byte aligned, with ld*2 a multiple of 16");
+    return ORDA_ERR_INVALID;
+  }
+  DevInputs in;
+  in.bt = bt;
+  in.h = h;
+  in.v = v;
+  in.mode = teacher->mode;
+  in.labels = labels;
+  in.hs = MatRef{student_hidden->data, static_cast<long long>(bt), static_cast<long long>(h),
+                 static_cast<long long>(student_hidden->ld)};
+  in.w = MatRef{weight->data, static_cast<long long>(v), static_cast<long long>(h), static_cast<long long>(weight->ld)};
+  in.ht_dim = h;
+  if (teacher->mode == ORDA_TEACHER_TIED || teacher->mode == ORDA_TEACHER_SEPARATE) {
+    if (!dev_mat_ok(teacher->hidden, true)) {
+      set_error(err, err_len, "teacher hidden must be bf16, 16-byte aligned, with ld*2 a multiple of 16");
+      return ORDA_ERR_INVALID;
+    }
+    in.ht_dim = teacher->hidden.cols;
+    in.ht = MatRef{teacher->hidden.data, static_cast<long long>(bt), static_cast<long long>(in.ht_dim),
+                   static_cast<long long>(teacher->hidden.ld)};
+  }
+  if (teacher->mode == ORDA_TEACHER_SEPARATE) {
+    if (!dev_mat_ok(teacher->weight, true)) {
+      set_error(err, err_len, "teacher weight must be bf16, 16-byte aligned, with ld*2 a multiple of 16");
+      return ORDA_ERR_INVALID;
+    }
+    in.wt = MatRef{teacher->weight.data, static_cast<long long>(v), static_cast<long long>(in.ht_dim),
+                   static_cast<long long>(teacher->weight.ld)};
+  }
+  if (teacher->mode == ORDA_TEACHER_PRECOMPUTED) {
+    if (!dev_mat_ok(teacher->logits, false)) {
+      set_error(err, err_len, "teacher logits must be 16-byte aligned with ld*elem a multiple of 16");
+      return ORDA_ERR_INVALID;
+    }
+    in.t_logits = teacher->logits.data;
+    in.ld_t_logits = static_cast<long long>(teacher->logits.ld);
+    in.t_logits_bf16 = teacher->logits.dtype == ORDA_DTYPE_BF16;
+  }
+  cudaSetDevice(ctx->device);
+  return run_device(ctx, in, *opts, *out, shard, static_cast<cudaStream_t>(stream), plan_out, err, err_len);
+}
+
+int orda_quantize_grad_w_device(OrdaContext* ctx, float* grad_w, size_t v, size_t h, size_t ld, const int64_t* labels,
+                                size_t bt, int64_t ignore_index, int stochastic, uint64_t seed, int8_t* q, float* scale,
+                                void* stream, char* err, size_t err_len) {
+  if (!ctx || !grad_w || (bt > 0 && !labels) || ld < h) {
+    set_error(err, err_len, "invalid argument");
+    return ORDA_ERR_INVALID;
+  }
+  std::lock_guard<std::mutex> lock(ctx->mu);
+  cudaSetDevice(ctx->device);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // target-row flags live in the context workspace
+  if (ensure_ws(ctx, round_up(v, 256)) != cudaSuccess) {
+    set_error(err, err_len, "device workspace allocation failed");
+    return ORDA_ERR_OOM;
+  }
+  uint8_t* flags = static_cast<uint8_t*>(ctx->ws);
+  cudaError_t e = cudaMemsetAsync(flags, 0, v, st);
+  if (e != cudaSuccess) return cuda_fail(e, "memset", err, err_len);
+  launch_target_flags(labels, static_cast<long long>(bt), static_cast<long long>(v), ignore_index, flags, st);
+  launch_quant(grad_w, static_cast<long long>(v), static_cast<long long>(h), static_cast<long long>(ld), flags,
+               stochastic, seed, q, scale, st);
+  if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(e, "quantise", err, err_len);
+  ctx->last_stream = st;
+  return ORDA_OK;
+}
+
+int orda_gemm_bf16_device(OrdaContext* ctx, const void* a, size_t lda, int a_kind, const void* b, size_t ldb, int b_kind,
+                          float* c, size_t ldc, size_t m, size_t n, size_t k, float alpha, float beta, void* stream,
+                          char* err, size_t err_len) {
+  if (!ctx || !a || !b || !c || k == 0) {
+    set_error(err, err_len, "invalid argument (null pointer or k == 0)");
+    return ORDA_ERR_INVALID;
+  }
+  std::lock_guard<std::mutex> lock(ctx->mu);
+  cudaSetDevice(ctx->device);
+  GemmDesc gd;
+  gd.a_mn_major = a_kind == 1;
+  gd.b_mn_major = b_kind == 1;
+  gd.a[0] = a_kind == 1 ? MatRef{a, static_cast<long long>(k), static_cast<long long>(m), static_cast<long long>(lda)}
+                        : MatRef{a, static_cast<long long>(m), static_cast<long long>(k), static_cast<long long>(lda)};
+  gd.b[0] = b_kind == 1 ? MatRef{b, static_cast<long long>(k), static_cast<long long>(n), static_cast<long long>(ldb)}
+                        : MatRef{b, static_cast<long long>(n), static_cast<long long>(k), static_cast<long long>(ldb)};
+  gd.k_seg[0] = static_cast<long long>(k);
+  gd.M = static_cast<long long>(m);
+  gd.N = static_cast<long long>(n);
+  gd.raster_n_fastest = m > n;
+  gd.status = ctx->d_words;
+  gd.args.out0 = c;
+  gd.args.ld0 = static_cast<long long>(ldc);
+  gd.args.alpha = alpha;
+  gd.args.beta = beta;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemsetAsync(ctx->d_words, 0, sizeof(int), st);
+  if (e != cudaSuccess) return cuda_fail(e, "memset", err, err_len);
+  const char* why = nullptr;
+  e = gemm_launch(gd, ctx->num_sms, st, &why);
+  if (e != cudaSuccess) return cuda_fail(e, why ? why : "GEMM", err, err_len);
+  ctx->last_stream = st;
+  return ORDA_OK;
+}
+
+// ------------------------------------------------------------ host-Mat entry
+
+int orda_distillation_loss(const OrdaMatF32* student_hidden, const OrdaMatF32* weight, const int64_t* labels,
+                           size_t n_labels, const OrdaTeacher* teacher, const OrdaLossOptions* opts, OrdaOutput* out,
+                           char* err, size_t err_len) {
+  if (!student_hidden || !weight || !teacher || !opts || !out) {
+    set_error(err, err_len, "null argument");
+    return ORDA_ERR_INVALID;
+  }
+  std::memset(out, 0, sizeof *out);
+  size_t v = 0, h = 0, bt = 0;
+  if (int rc = orda_validate(student_hidden, weight, labels, n_labels, teacher, opts, &v, &h, &bt, err, err_len))
+    return rc;
+  if (opts->backend == ORDA_BACKEND_CPU) {
+    set_error(err, err_len, "Backend::Cpu is not available: this library is the B200 path and has no CPU backend");
+    return ORDA_ERR_BACKEND;
+  }
+  const float w_t = opts->has_teacher_ce_weight ? opts->teacher_ce_weight : orda_default_teacher_ce_weight(teacher->mode);
+  if (w_t < 0.0f) {
+    set_error(err, err_len, "teacher_ce_weight must be >= 0, got %s", fmt_f32(w_t).c_str());
+    return ORDA_ERR_INVALID;
+  }
+  if (!orda_is_available()) {
+    set_error(err, err_len,
+              opts->backend == ORDA_BACKEND_CUDA
+                  ? "Backend::Cuda requested but no sm_100 CUDA device is available"
+                  : "Backend::Auto found no sm_100 CUDA device (this library has no CPU path)");
+    return ORDA_ERR_BACKEND;
+  }
+  int dev = 0;
+  cudaGetDevice(&dev);
+  OrdaContext* ctx = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_default_mu);
+    if (dev < 0 || dev >= 64) dev = 0;
+    if (!g_default_ctx[dev]) {
+      if (int rc = orda_context_create(dev, &g_default_ctx[dev], err, err_len)) return rc;
+    }
+    ctx = g_default_ctx[dev];
+  }
+  std::lock_guard<std::mutex> lock(ctx->mu);
+  cudaSetDevice(ctx->device);
+  if (!ctx->own_stream) cudaStreamCreateWithFlags(&ctx->own_stream, cudaStreamNonBlocking);
+  cudaStream_t st = ctx->own_stream;
+
+  const OrdaTeacherMode mode = teacher->mode;
+  const bool live = mode == ORDA_TEACHER_TIED || mode == ORDA_TEACHER_SEPARATE;
+  const size_t ht = mode == ORDA_TEACHER_SEPARATE ? teacher->hidden.cols : h;
+  const bool tgrad = w_t > 0.0f && live;
+  const size_t ldh = round_up(h, 8), ldht = round_up(ht, 8), ldtl = round_up(v, 4);
+
+  // staging layout
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off = round_up(off + bytes, 256);
+    return o;
+  };
+  const size_t o_hs = take(bt * ldh * 2), o_w = take(v * ldh * 2);
+  const size_t o_ht = take(live ? bt * ldht * 2 : 0), o_wt = take(mode == ORDA_TEACHER_SEPARATE ? v * ldht * 2 : 0);
+  const size_t o_tl = take(mode == ORDA_TEACHER_PRECOMPUTED ? bt * ldtl * 4 : 0);
+  const size_t o_lab = take(bt * 8);
+  const size_t o_ghs = take(bt * h * 4), o_gw = take(v * h * 4);
+  const size_t o_ght = take(tgrad ? bt * ht * 4 : 0), o_gwt = take(tgrad && mode == ORDA_TEACHER_SEPARATE ? v * ht * 4 : 0);
+  const size_t o_sc = take(4 * sizeof(float));
+  size_t tmp_elems = std::max({bt * h, v * h, live ? bt * ht : size_t{0}, mode == ORDA_TEACHER_SEPARATE ? v * ht : size_t{0}});
+  const size_t o_tmp = take(tmp_elems * 4);
+  if (ctx->stage_bytes < off) {
+    cudaFree(ctx->stage);
+    ctx->stage = nullptr;
+    ctx->stage_bytes = 0;
+    cudaError_t e = cudaMalloc(&ctx->stage, off);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      set_error(err, err_len, "device staging allocation of %zu bytes failed", off);
+      return ORDA_ERR_OOM;
+    }
+    ctx->stage_bytes = off;
+  }
+  uint8_t* S = static_cast<uint8_t*>(ctx->stage);
+  float* tmp = reinterpret_cast<float*>(S + o_tmp);
+  cudaError_t e;
+  auto upload_bf16 = [&](const OrdaMatF32& m, size_t ld, size_t o) -> cudaError_t {
+    cudaError_t ee = cudaMemcpyAsync(tmp, m.data, m.rows * m.cols * 4, cudaMemcpyHostToDevice, st);
+    if (ee != cudaSuccess) return ee;
+    launch_f32_to_bf16(tmp, static_cast<long long>(m.rows), static_cast<long long>(m.cols),
+                       reinterpret_cast<uint16_t*>(S + o), static_cast<long long>(ld), st);
+    return cudaGetLastError();
+  };
+  if ((e = upload_bf16(*student_hidden, ldh, o_hs)) != cudaSuccess) return cuda_fail(e, "upload", err, err_len);
+  if ((e = upload_bf16(*weight, ldh, o_w)) != cudaSuccess) return cuda_fail(e, "upload", err, err_len);
+  if (live && (e = upload_bf16(teacher->hidden, ldht, o_ht)) != cudaSuccess) return cuda_fail(e, "upload", err, err_len);
+  if (mode == ORDA_TEACHER_SEPARATE && (e = upload_bf16(teacher->weight, ldht, o_wt)) != cudaSuccess)
+    return cuda_fail(e, "upload", err, err_len);
+  if (mode == ORDA_TEACHER_PRECOMPUTED) {
+    e = cudaMemcpy2DAsync(S + o_tl, ldtl * 4, teacher->logits.data, v * 4, v * 4, bt, cudaMemcpyHostToDevice, st);
+    if (e != cudaSuccess) return cuda_fail(e, "upload", err, err_len);
+  }
+  if ((e = cudaMemcpyAsync(S + o_lab, labels, bt * 8, cudaMemcpyHostToDevice, st)) != cudaSuccess)
+    return cuda_fail(e, "upload", err, err_len);
+
+  OrdaDeviceOutputs dout{};
+  dout.grad_student_hidden = reinterpret_cast<float*>(S + o_ghs);
+  dout.ld_grad_student_hidden = h;
+  dout.grad_weight = reinterpret_cast<float*>(S + o_gw);
+  dout.ld_grad_weight = h;
+  if (tgrad) {
+    dout.grad_teacher_hidden = reinterpret_cast<float*>(S + o_ght);
+    dout.ld_grad_teacher_hidden = ht;
+  }
+  if (tgrad && mode == ORDA_TEACHER_SEPARATE) {
+    dout.grad_teacher_weight = reinterpret_cast<float*>(S + o_gwt);
+    dout.ld_grad_teacher_weight = ht;
+  }
+  dout.scalars = reinterpret_cast<float*>(S + o_sc);
+
+  DevInputs in;
+  in.bt = bt;
+  in.h = h;
+  in.v = v;
+  in.ht_dim = ht;
+  in.mode = mode;
+  in.labels = reinterpret_cast<const int64_t*>(S + o_lab);
+  in.hs = MatRef{S + o_hs, static_cast<long long>(bt), static_cast<long long>(h), static_cast<long long>(ldh)};
+  in.w = MatRef{S + o_w, static_cast<long long>(v), static_cast<long long>(h), static_cast<long long>(ldh)};
+  if (live) in.ht = MatRef{S + o_ht, static_cast<long long>(bt), static_cast<long long>(ht), static_cast<long long>(ldht)};
+  if (mode == ORDA_TEACHER_SEPARATE)
+    in.wt = MatRef{S + o_wt, static_cast<long long>(v), static_cast<long long>(ht), static_cast<long long>(ldht)};
+  if (mode == ORDA_TEACHER_PRECOMPUTED) {
+    in.t_logits = S + o_tl;
+    in.ld_t_logits = static_cast<long long>(ldtl);
+    in.t_logits_bf16 = false;
+  }
+  OrdaChunkPlan plan{};
+  if (int rc = run_device(ctx, in, *opts, dout, nullptr, st, &plan, err, err_len)) return rc;
+
+  // download into library-owned host buffers
+  auto dl = [&](float* dsrc, size_t rows, size_t cols, OrdaMatOut& m) -> cudaError_t {
+    m.rows = rows;
+    m.cols = cols;
+    m.data = static_cast<float*>(std::malloc(std::max<size_t>(rows * cols, 1) * 4));
+    if (!m.data) return cudaErrorMemoryAllocation;
+    return cudaMemcpyAsync(m.data, dsrc, rows * cols * 4, cudaMemcpyDeviceToHost, st);
+  };
+  float sc[4] = {0, 0, 0, 0};
+  e = dl(dout.grad_student_hidden, bt, h, out->grad_student_hidden);
+  if (e == cudaSuccess) e = dl(dout.grad_weight, v, h, out->grad_weight);
+  if (e == cudaSuccess && tgrad) e = dl(dout.grad_teacher_hidden, bt, ht, out->grad_teacher_hidden);
+  if (e == cudaSuccess && tgrad && mode == ORDA_TEACHER_SEPARATE)
+    e = dl(dout.grad_teacher_weight, v, ht, out->grad_teacher_weight);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(sc, dout.scalars, sizeof sc, cudaMemcpyDeviceToHost, st);
+  if (e != cudaSuccess) {
+    orda_output_free(out);
+    return cuda_fail(e, "download", err, err_len);
+  }
+  if (int rc = check_status(ctx, err, err_len)) {
+    orda_output_free(out);
+    return rc;
+  }
+  out->loss = sc[0];
+  out->student_ce = sc[1];
+  out->teacher_ce = sc[2];
+  out->kl = sc[3];
+  out->chunk_plan = plan;
+  return ORDA_OK;
+}
+
+void orda_output_free(OrdaOutput* out) {
+  if (!out) return;
+  std::free(out->grad_student_hidden.data);
+  std::free(out->grad_weight.data);
+  std::free(out->grad_teacher_hidden.data);
+  std::free(out->grad_teacher_weight.data);
+  out->grad_student_hidden.data = nullptr;
+  out->grad_weight.data = nullptr;
+  out->grad_teacher_hidden.data = nullptr;
+  out->grad_teacher_weight.data = nullptr;
+}
+
+}  // extern "C"

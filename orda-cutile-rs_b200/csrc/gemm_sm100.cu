@@ -1,0 +1,572 @@
+// gemm_sm100.cu -- persistent bf16 tensor-core GEMM for sm_100a.
+//
+// C[M,N] = op(A) @ op(B)^T with fp32 accumulation in TMEM.
+//   * TMA (cp.async.bulk.tensor, 128-byte swizzle) stages 128x64 A tiles and
+//     256x64 B tiles through a 4-deep shared-memory ring (48 KB per stage);
+//   * one thread issues tcgen05.mma (M=128, N=256, K=16) into one of two
+//     128x256 fp32 TMEM accumulators (all 512 TMEM columns), so the epilogue
+//     of tile i overlaps the main loop of tile i+1;
+//   * eight epilogue warps read the accumulator with tcgen05.ld (each warp
+//     owns one 32-lane TMEM quadrant and one 128-column half);
+//   * one CTA per SM walks the tile list (persistent scheduling).
+// Operands may be K-major ([rows, K] row-major) or MN-major ([K, rows]),
+// which covers the three GEMMs of the distillation loss without transposes:
+//   logits = h @ W^T      (A K-major, B K-major)
+//   grad_h = dlogits @ W  (A K-major, B MN-major)
+//   grad_W = dlogits^T @ h (A MN-major, B MN-major)
+// Epilogues: plain scaled store, or the logits epilogue that writes fp32
+// logits and per-row online-softmax statistics (max, sum exp(x-m),
+// sum exp((x-m)/T), sum x) together with the paired teacher statistics and
+// the KL cross term, so the loss never needs a separate reduction pass.
+//
+// No TMA multicast is used anywhere (the same kernels serve multi-GPU runs).
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdio>
+#include <mutex>
+
+#include "kernels.h"
+#include "ptx.cuh"
+
+namespace orda {
+
+namespace {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BK = 64;
+constexpr int STAGES = 4;
+constexpr int A_STAGE_BYTES = BM * BK * 2;  // 16 KB
+constexpr int B_STAGE_BYTES = BN * BK * 2;  // 32 KB
+constexpr int STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
+constexpr int NUM_THREADS = 384;  // warp 0 TMA, 1 MMA, 2 TMEM, 3 idle, 4..11 epilogue
+constexpr int EPI_WARP0 = 4;
+constexpr int NUM_EPI_WARPS = 8;
+constexpr int TMEM_COLS = 512;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+constexpr float LOG2E = 1.4426950408889634f;
+
+struct KParams {
+  int M, N;
+  int m_blocks, n_blocks, num_tiles;
+  int raster_n_fastest;
+  int nseg;
+  int seg_kblocks[2];
+  int* status;
+  EpiArgs e;
+};
+
+__device__ __forceinline__ void tile_coords(const KParams& p, int tile, int& mb, int& nb) {
+  if (p.raster_n_fastest) {
+    nb = tile % p.n_blocks;
+    mb = tile / p.n_blocks;
+  } else {
+    mb = tile % p.m_blocks;
+    nb = tile / p.m_blocks;
+  }
+}
+
+__device__ __forceinline__ float bf16_bits_to_f32(uint16_t b) { return __uint_as_float(static_cast<uint32_t>(b) << 16); }
+
+// ------------------------------------------------------------- epilogues
+
+// Plain store: dst = alpha * acc (+ beta * dst).
+__device__ __forceinline__ void epi_store_chunk(const KParams& p, long long grow, int col0, int nvalid,
+                                                const uint32_t (&r)[32], float alpha) {
+  const EpiArgs& e = p.e;
+  float* dst;
+  if (grow < e.split_row) dst = e.out0 + grow * e.ld0 + col0;
+  else dst = e.out1 + (grow - e.split_row) * e.ld1 + col0;
+  const bool vec = nvalid == 32 && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0);
+  if (vec) {
+#pragma unroll
+    for (int j = 0; j < 32; j += 4) {
+      float4 o;
+      o.x = alpha * __uint_as_float(r[j + 0]);
+      o.y = alpha * __uint_as_float(r[j + 1]);
+      o.z = alpha * __uint_as_float(r[j + 2]);
+      o.w = alpha * __uint_as_float(r[j + 3]);
+      if (e.beta != 0.0f) {
+        float4 old = *reinterpret_cast<const float4*>(dst + j);
+        o.x += e.beta * old.x;
+        o.y += e.beta * old.y;
+        o.z += e.beta * old.z;
+        o.w += e.beta * old.w;
+      }
+      *reinterpret_cast<float4*>(dst + j) = o;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      if (j < nvalid) {
+        float o = alpha * __uint_as_float(r[j]);
+        if (e.beta != 0.0f) o += e.beta * dst[j];
+        dst[j] = o;
+      }
+    }
+  }
+}
+
+struct OwnStats {
+  float m, d1, dT, sx;
+};
+struct PairStats {
+  float m, d1, dT, s, sx;
+};
+
+// Logits epilogue for one 32-column chunk of one row.
+__device__ __forceinline__ void epi_logits_chunk(const KParams& p, long long grow, bool row_ok, int col0,
+                                                 int nvalid, const uint32_t (&r)[32], OwnStats& os,
+                                                 PairStats& ps) {
+  const EpiArgs& e = p.e;
+  float v[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+
+  // fp32 logits store
+  if (row_ok) {
+    float* dst = e.logits + grow * e.ldl + col0;
+    if (nvalid == 32) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (j < nvalid) dst[j] = v[j];
+    }
+  }
+
+  const float inv_t = e.inv_t;
+  const float lt = LOG2E * inv_t;
+
+  // own online-softmax statistics
+  float cmax = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < 32; ++j)
+    if (j < nvalid) cmax = fmaxf(cmax, v[j]);
+  if (cmax > os.m) {
+    if (os.m != -INFINITY) {
+      const float dm = os.m - cmax;
+      os.d1 *= exp2f(dm * LOG2E);
+      os.dT *= exp2f(dm * lt);
+    }
+    os.m = cmax;
+  }
+  {
+    float a1 = 0.f, aT = 0.f, ax = 0.f;
+    const float m = os.m;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      if (j < nvalid) {
+        const float dx = v[j] - m;
+        if (e.own_d1) a1 += exp2f(dx * LOG2E);
+        if (e.own_dT) aT += exp2f(dx * lt);
+        ax += v[j];
+      }
+    }
+    os.d1 += a1;
+    os.dT += aT;
+    os.sx += ax;
+  }
+
+  if (!e.pair) return;
+  // paired teacher values for the same (row, columns)
+  float t[32];
+  if (row_ok) {
+    if (e.pair_is_bf16) {
+      const uint16_t* src = static_cast<const uint16_t*>(e.pair_src) + grow * e.ld_pair + col0;
+      if (nvalid == 32 && ((reinterpret_cast<uintptr_t>(src) & 15) == 0)) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 8) {
+          uint4 q = *reinterpret_cast<const uint4*>(src + j);
+          t[j + 0] = __uint_as_float(q.x << 16);
+          t[j + 1] = __uint_as_float(q.x & 0xFFFF0000u);
+          t[j + 2] = __uint_as_float(q.y << 16);
+          t[j + 3] = __uint_as_float(q.y & 0xFFFF0000u);
+          t[j + 4] = __uint_as_float(q.z << 16);
+          t[j + 5] = __uint_as_float(q.z & 0xFFFF0000u);
+          t[j + 6] = __uint_as_float(q.w << 16);
+          t[j + 7] = __uint_as_float(q.w & 0xFFFF0000u);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) t[j] = j < nvalid ? bf16_bits_to_f32(src[j]) : 0.f;
+      }
+    } else {
+      const float* src = static_cast<const float*>(e.pair_src) + grow * e.ld_pair + col0;
+      if (nvalid == 32 && ((reinterpret_cast<uintptr_t>(src) & 15) == 0)) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+          float4 q = *reinterpret_cast<const float4*>(src + j);
+          t[j] = q.x;
+          t[j + 1] = q.y;
+          t[j + 2] = q.z;
+          t[j + 3] = q.w;
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) t[j] = j < nvalid ? src[j] : 0.f;
+      }
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) t[j] = 0.f;
+  }
+  float tmax = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < 32; ++j)
+    if (j < nvalid) tmax = fmaxf(tmax, t[j]);
+  if (tmax > ps.m) {
+    if (ps.m != -INFINITY) {
+      const float dm = ps.m - tmax;
+      const float fT = exp2f(dm * lt);
+      ps.dT *= fT;
+      ps.s *= fT;
+      ps.d1 *= exp2f(dm * LOG2E);
+    }
+    ps.m = tmax;
+  }
+  {
+    float a1 = 0.f, aT = 0.f, as = 0.f, ax = 0.f;
+    const float m = ps.m;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      if (j < nvalid) {
+        const float dx = t[j] - m;
+        const float eT = exp2f(dx * lt);
+        aT += eT;
+        as += eT * ((t[j] - v[j]) * inv_t);
+        if (e.pair_d1) a1 += exp2f(dx * LOG2E);
+        ax += t[j];
+      }
+    }
+    ps.dT += aT;
+    ps.s += as;
+    ps.d1 += a1;
+    ps.sx += ax;
+  }
+}
+
+// ------------------------------------------------------------------ kernel
+
+template <bool A_MN, bool B_MN, int EPI>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap mapA0, const __grid_constant__ CUtensorMap mapA1,
+                const __grid_constant__ CUtensorMap mapB0, const __grid_constant__ CUtensorMap mapB1,
+                const __grid_constant__ KParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_STAGE_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], NUM_EPI_WARPS);
+    }
+    mbar_init(drain, 1);
+    fence_mbarrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&mapA0);
+    tma_prefetch_desc(&mapB0);
+    if (p.nseg > 1) {
+      tma_prefetch_desc(&mapA1);
+      tma_prefetch_desc(&mapB1);
+    }
+  }
+  if (warp == 2) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------- producer
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+      int mb, nb;
+      tile_coords(p, tile, mb, nb);
+      for (int seg = 0; seg < p.nseg && ok; ++seg) {
+        const CUtensorMap* ma = seg == 0 ? &mapA0 : &mapA1;
+        const CUtensorMap* mbm = seg == 0 ? &mapB0 : &mapB1;
+        for (int kb = 0; kb < p.seg_kblocks[seg]; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, p.status, DEV_TIMEOUT_PRODUCER)) {
+            ok = false;
+            break;
+          }
+          if (lane == 0) {
+            mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
+            uint8_t* a_dst = sA + stage * A_STAGE_BYTES;
+            uint8_t* b_dst = sB + stage * B_STAGE_BYTES;
+            if (!A_MN) {
+              tma_load_2d(a_dst, ma, &full[stage], kb * BK, mb * BM);
+            } else {
+#pragma unroll
+              for (int i = 0; i < BM / 64; ++i)
+                tma_load_2d(a_dst + i * (BK * 128), ma, &full[stage], mb * BM + i * 64, kb * BK);
+            }
+            if (!B_MN) {
+              tma_load_2d(b_dst, mbm, &full[stage], kb * BK, nb * BN);
+            } else {
+#pragma unroll
+              for (int i = 0; i < BN / 64; ++i)
+                tma_load_2d(b_dst + i * (BK * 128), mbm, &full[stage], nb * BN + i * 64, kb * BK);
+            }
+          }
+          __syncwarp();
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // --------------------------------------------------------------- MMA
+    constexpr uint32_t idesc = make_idesc_bf16_f32(BM, BN, A_MN, B_MN);
+    int stage = 0;
+    uint32_t phase = 0;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+      if (!mbar_wait(&tempty[acc], acc_phase ^ 1, p.status, DEV_TIMEOUT_MMA)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+      bool first = true;
+      for (int seg = 0; seg < p.nseg && ok; ++seg) {
+        for (int kb = 0; kb < p.seg_kblocks[seg]; ++kb) {
+          if (!mbar_wait(&full[stage], phase, p.status, DEV_TIMEOUT_MMA)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          if (lane == 0) {
+            const uint32_t a_base = smem_u32(sA + stage * A_STAGE_BYTES);
+            const uint32_t b_base = smem_u32(sB + stage * B_STAGE_BYTES);
+#pragma unroll
+            for (int k = 0; k < BK / 16; ++k) {
+              uint64_t ad, bd;
+              if (!A_MN) ad = make_smem_desc_sw128(a_base + k * 32, 16, 1024);
+              else ad = make_smem_desc_sw128(a_base + k * 2048, BK * 128, 1024);
+              if (!B_MN) bd = make_smem_desc_sw128(b_base + k * 32, 16, 1024);
+              else bd = make_smem_desc_sw128(b_base + k * 2048, BK * 128, 1024);
+              umma_bf16(d_tmem, ad, bd, idesc, (first && k == 0) ? 0u : 1u);
+            }
+            umma_commit(&empty[stage]);
+          }
+          __syncwarp();
+          first = false;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok) break;
+      if (lane == 0) umma_commit(&tfull[acc]);
+      __syncwarp();
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+    // Drain: every MMA this thread issued has completed before teardown.
+    if (lane == 0) umma_commit(drain);
+    __syncwarp();
+    mbar_wait(drain, 0, p.status, DEV_TIMEOUT_DRAIN);
+  } else if (warp >= EPI_WARP0) {
+    // ---------------------------------------------------------- epilogue
+    const int ew = warp - EPI_WARP0;
+    const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+    const int half = ew >> 2;   // which 128-column half of the tile
+    const int row_in_tile = quad * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
+      int mb, nb;
+      tile_coords(p, tile, mb, nb);
+      if (!mbar_wait(&tfull[acc], acc_phase, p.status, DEV_TIMEOUT_EPILOGUE)) break;
+      tc_fence_after();
+      const long long grow = static_cast<long long>(mb) * BM + row_in_tile;
+      const bool row_ok = grow < p.M;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
+                             static_cast<uint32_t>(acc * BN + half * 128);
+      if constexpr (EPI == static_cast<int>(Epi::Store)) {
+        const float alpha = p.e.alpha_ptr ? *p.e.alpha_ptr : p.e.alpha;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          const int col0 = nb * BN + half * 128 + c * 32;
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(t_row + c * 32, r);
+          tmem_ld_wait();
+          if (col0 < p.N && row_ok) {
+            const int nvalid = min(32, p.N - col0);
+            epi_store_chunk(p, grow, col0, nvalid, r, alpha);
+          }
+        }
+      } else {
+        OwnStats os{-INFINITY, 0.f, 0.f, 0.f};
+        PairStats ps{-INFINITY, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          const int col0 = nb * BN + half * 128 + c * 32;
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(t_row + c * 32, r);
+          tmem_ld_wait();
+          if (col0 < p.N) {
+            const int nvalid = min(32, p.N - col0);
+            epi_logits_chunk(p, grow, row_ok, col0, nvalid, r, os, ps);
+          }
+        }
+        const int part = nb * 2 + half;
+        if (row_ok && nb * BN + half * 128 < p.N) {
+          const long long ri = grow * p.e.n_parts + part;
+          reinterpret_cast<float4*>(p.e.rec_own)[ri] = make_float4(os.m, os.d1, os.dT, os.sx);
+          if (p.e.pair) {
+            float4* pr = reinterpret_cast<float4*>(p.e.rec_pair) + ri * 2;
+            pr[0] = make_float4(ps.m, ps.d1, ps.dT, ps.s);
+            pr[1] = make_float4(ps.sx, 0.f, 0.f, 0.f);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------- host side
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+
+bool get_encode() {
+  std::call_once(g_encode_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  return g_encode != nullptr;
+}
+
+// Encodes a 2-D bf16 map over a stored matrix (rows x cols, ld elements) with
+// a box of box_inner (along cols) x box_outer (along rows), 128-byte swizzle.
+bool encode_map(CUtensorMap* map, const MatRef& m, int box_inner, int box_outer) {
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(m.cols), static_cast<cuuint64_t>(m.rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(m.ld) * 2};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_inner), static_cast<cuuint32_t>(box_outer)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(m.ptr), dims, strides, box,
+                        estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+template <bool A_MN, bool B_MN, int EPI>
+cudaError_t launch_t(const CUtensorMap* maps, const KParams& kp, int grid, cudaStream_t stream) {
+  auto kern = gemm_kernel<A_MN, B_MN, EPI>;
+  static bool attr_done = false;  // per instantiation; attribute is per-function
+  if (!attr_done) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    attr_done = true;
+  }
+  kern<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(maps[0], maps[1], maps[2], maps[3], kp);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t gemm_launch(const GemmDesc& d, int num_sms, cudaStream_t stream, const char** why) {
+  if (why) *why = nullptr;
+  if (!get_encode()) {
+    if (why) *why = "cuTensorMapEncodeTiled entry point unavailable";
+    return cudaErrorNotSupported;
+  }
+  KParams kp{};
+  kp.M = static_cast<int>(d.M);
+  kp.N = static_cast<int>(d.N);
+  kp.m_blocks = static_cast<int>((d.M + BM - 1) / BM);
+  kp.n_blocks = static_cast<int>((d.N + BN - 1) / BN);
+  kp.num_tiles = kp.m_blocks * kp.n_blocks;
+  kp.raster_n_fastest = d.raster_n_fastest ? 1 : 0;
+  kp.nseg = d.nseg;
+  kp.status = d.status;
+  kp.e = d.args;
+  CUtensorMap maps[4];
+  for (int s = 0; s < 2; ++s) {
+    const int src = s < d.nseg ? s : 0;
+    kp.seg_kblocks[s] = s < d.nseg ? static_cast<int>((d.k_seg[s] + BK - 1) / BK) : 0;
+    const MatRef& a = d.a[src];
+    const MatRef& b = d.b[src];
+    for (const MatRef* m : {&a, &b}) {
+      if ((reinterpret_cast<uintptr_t>(m->ptr) & 15) != 0 || (m->ld * 2) % 16 != 0 || m->ld < m->cols) {
+        if (why) *why = "GEMM operand must be 16-byte aligned with ld*2 a multiple of 16";
+        return cudaErrorInvalidValue;
+      }
+    }
+    bool ok = d.a_mn_major ? encode_map(&maps[s], a, 64, BK) : encode_map(&maps[s], a, BK, BM);
+    ok = ok && (d.b_mn_major ? encode_map(&maps[2 + s], b, 64, BK) : encode_map(&maps[2 + s], b, BK, BN));
+    if (!ok) {
+      if (why) *why = "cuTensorMapEncodeTiled failed";
+      return cudaErrorInvalidValue;
+    }
+  }
+  if (kp.num_tiles == 0) return cudaSuccess;
+  const int grid = kp.num_tiles < num_sms ? kp.num_tiles : num_sms;
+  const int epi = static_cast<int>(d.epi);
+  if (epi == static_cast<int>(Epi::Logits)) {
+    if (d.a_mn_major || d.b_mn_major) {
+      if (why) *why = "logits epilogue requires K-major operands";
+      return cudaErrorInvalidValue;
+    }
+    return launch_t<false, false, 1>(maps, kp, grid, stream);
+  }
+  if (!d.a_mn_major && !d.b_mn_major) return launch_t<false, false, 0>(maps, kp, grid, stream);
+  if (!d.a_mn_major && d.b_mn_major) return launch_t<false, true, 0>(maps, kp, grid, stream);
+  if (d.a_mn_major && !d.b_mn_major) return launch_t<true, false, 0>(maps, kp, grid, stream);
+  return launch_t<true, true, 0>(maps, kp, grid, stream);
+}
+
+}  // namespace orda

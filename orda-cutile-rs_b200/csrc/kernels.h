@@ -1,0 +1,119 @@
+// kernels.h -- host-side launch interface of the sm_100a kernels.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace orda {
+
+// ---------------------------------------------------------------- GEMM
+// One operand segment: a bf16 matrix as stored in memory, rows x cols with
+// leading dimension ld (elements).
+struct MatRef {
+  const void* ptr = nullptr;
+  long long rows = 0;
+  long long cols = 0;
+  long long ld = 0;
+};
+
+enum class Epi : int { Store = 0, Logits = 1 };
+
+// Epilogue arguments. Store: out = alpha * acc (+ beta * out); rows below
+// split_row go to out0, the rest to out1 (row - split_row).
+// Logits: fp32 logits written to `logits` (ldl) plus per-(row, 128-column
+// part) online-softmax records (see rows.cu for the record layout).
+struct EpiArgs {
+  // Store
+  float* out0 = nullptr;
+  long long ld0 = 0;
+  float* out1 = nullptr;
+  long long ld1 = 0;
+  long long split_row = 1ll << 62;
+  float alpha = 1.0f;
+  const float* alpha_ptr = nullptr;  // device scalar overriding alpha
+  float beta = 0.0f;
+  // Logits
+  float* logits = nullptr;
+  long long ldl = 0;
+  float* rec_own = nullptr;   // float4 per (row, part)
+  float* rec_pair = nullptr;  // 8 floats per (row, part)
+  int n_parts = 0;
+  const void* pair_src = nullptr;  // teacher logits paired with this tile (same row/col)
+  long long ld_pair = 0;
+  int pair_is_bf16 = 0;
+  float inv_t = 1.0f;
+  int own_d1 = 0, own_dT = 0, own_sx = 0;
+  int pair = 0, pair_d1 = 0, pair_sx = 0;
+};
+
+struct GemmDesc {
+  bool a_mn_major = false;  // A stored [K, M] instead of [M, K]
+  bool b_mn_major = false;  // B stored [K, N] instead of [N, K]
+  int nseg = 1;             // K segments (stacked operands along K)
+  MatRef a[2];
+  MatRef b[2];
+  long long k_seg[2] = {0, 0};
+  long long M = 0, N = 0;
+  bool raster_n_fastest = false;
+  Epi epi = Epi::Store;
+  EpiArgs args;
+  int* status = nullptr;  // device status word
+};
+
+// Encodes the tensor maps and launches the persistent tcgen05 GEMM.
+// Returns cudaSuccess or the first error.
+cudaError_t gemm_launch(const GemmDesc& d, int num_sms, cudaStream_t stream, const char** why);
+
+// ------------------------------------------------------------ row kernels
+struct RowArgs {
+  int n;                  // rows in this chunk
+  int v;                  // vocabulary
+  int n_parts;            // record parts per row
+  const float* logits_s;  // [n, ldl] fp32 student logits
+  const void* teacher;    // teacher logits rows for this chunk (fp32 or bf16)
+  long long ld_teacher;
+  int teacher_is_bf16;
+  long long ldl;
+  const float* rec_own;   // [n] student own records
+  const float* rec_own_t; // [n] teacher own records (Tied/Separate teacher CE stats)
+  const float* rec_pair;  // [n] pair records (teacher KL stats, S)
+  const int64_t* labels;  // chunk labels
+  int64_t ignore_index;
+  float w_s, w_t, kd, temperature, inv_t, alpha;
+  int need_kl;            // kd > 0
+  int teacher_ce;         // w_t > 0 (teacher CE reported)
+  int teacher_ce_from_own;  // Tied/Separate: teacher CE stats from rec_own rows n..2n
+  int teacher_grad;       // write teacher dlogits rows
+  uint16_t* dlog_s;       // bf16 [n, ldd]
+  uint16_t* dlog_t;       // bf16 [n, ldd] (teacher_grad)
+  long long ldd;
+  float* nll_s_rows;      // [n]
+  float* nll_t_rows;      // [n]
+  double* kl_rows;        // [n] (KL * T^2, ignored -> 0)
+};
+void launch_rows(const RowArgs& a, cudaStream_t stream);
+
+// Label pass: counts non-ignored labels, checks the range [0, v), marks
+// target rows (for the quantiser) and writes the mean scale.
+void launch_label_prep(const int64_t* labels, long long bt, long long v, int64_t ignore_index, int reduction_sum,
+                       long long denom_override, int* n_non_ignore, float* mean_scale, uint8_t* target_flags,
+                       int* status, cudaStream_t stream);
+
+// Final deterministic reduction of per-row losses into the four scalars.
+void launch_finalize(const float* nll_s, const float* nll_t, const double* kl_rows, long long bt,
+                     const float* mean_scale, float w_s, float w_t, float kd, float* scalars, cudaStream_t stream);
+
+// f32 -> bf16 (round to nearest even) into a padded row-major buffer.
+void launch_f32_to_bf16(const float* src, long long rows, long long cols, uint16_t* dst, long long ld,
+                        cudaStream_t stream);
+
+// INT8 row-wise quantisation of grad_W (in place dequantised result).
+void launch_quant(float* grad_w, long long v, long long h, long long ld, const uint8_t* target_flags,
+                  int stochastic, uint64_t seed, int8_t* q, float* scale, cudaStream_t stream);
+
+// Marks target rows only (used by the stand-alone quantiser entry).
+void launch_target_flags(const int64_t* labels, long long bt, long long v, int64_t ignore_index,
+                         uint8_t* target_flags, cudaStream_t stream);
+
+}  // namespace orda

@@ -1,0 +1,100 @@
+// quant.cu -- fused INT8 row-wise grad_W quantisation (absmax + quantise +
+// dequantise in one kernel), bit-exact with src/quant.rs:
+//   s = max(amax, 1e-12) / 127            (IEEE f32 divide, row_scale :91-94)
+//   q = clamp(rne(x / s), -127, 127)      (IEEE divide; rne = round half even,
+//                                          round_half_even :48-63)
+//   stochastic: q = clamp(floor(x/s) + [frac > u_k], -127, 127) with u_k the
+//   k-th draw (k = r*H + c, row-major) of the SplitMix64 stream :18-44,120-144;
+//   draw k is computed directly from its index, so rows run in parallel.
+//   dequantised = q * s, target rows (labels) restored exactly (:157-202).
+// This file is compiled without fast-math, so '/' is the correctly rounded
+// divide; __fdiv_rn makes that explicit.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdint>
+
+#include "kernels.h"
+
+namespace orda {
+
+namespace {
+
+constexpr int QT = 256;
+
+__device__ __forceinline__ int8_t to_i8(float v) {
+  if (isnan(v)) return 0;  // Rust `as i8` maps NaN to 0
+  v = fminf(fmaxf(v, -127.0f), 127.0f);
+  return static_cast<int8_t>(v);
+}
+
+// u_k of the reference's SplitMix64 Rng::new(seed): the k-th call sees
+// state = seed + (k + 2) * golden (wrapping).
+__device__ __forceinline__ float splitmix_uniform(uint64_t seed, uint64_t k) {
+  const uint64_t golden = 0x9E3779B97F4A7C15ull;
+  uint64_t z = seed + (k + 2) * golden;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  z ^= z >> 31;
+  return static_cast<float>(z >> 40) * (1.0f / 16777216.0f);
+}
+
+__global__ void __launch_bounds__(QT) quant_kernel(float* grad_w, long long h, long long ld,
+                                                   const uint8_t* target_flags, int stochastic, uint64_t seed,
+                                                   int8_t* q, float* scale) {
+  __shared__ float sh[QT / 32];
+  const long long r = blockIdx.x;
+  float* row = grad_w + r * ld;
+
+  float amax = 0.0f;
+  const bool vec = (h % 4 == 0) && (ld % 4 == 0);
+  if (vec) {
+    for (long long c = threadIdx.x * 4; c < h; c += QT * 4) {
+      const float4 x = *reinterpret_cast<const float4*>(row + c);
+      amax = fmaxf(amax, fabsf(x.x));
+      amax = fmaxf(amax, fabsf(x.y));
+      amax = fmaxf(amax, fabsf(x.z));
+      amax = fmaxf(amax, fabsf(x.w));
+    }
+  } else {
+    for (long long c = threadIdx.x; c < h; c += QT) amax = fmaxf(amax, fabsf(row[c]));
+  }
+  for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+  if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = amax;
+  __syncthreads();
+  amax = sh[0];
+#pragma unroll
+  for (int w = 1; w < QT / 32; ++w) amax = fmaxf(amax, sh[w]);
+
+  const float s = __fdiv_rn(fmaxf(amax, 1e-12f), 127.0f);
+  if (scale && threadIdx.x == 0) scale[r] = s;
+  const bool keep = target_flags && target_flags[r];
+  int8_t* qrow = q ? q + r * h : nullptr;
+
+  for (long long c = threadIdx.x; c < h; c += QT) {
+    const float x = row[c];
+    const float scaled = __fdiv_rn(x, s);
+    int8_t qi;
+    if (!stochastic) {
+      qi = to_i8(rintf(scaled));
+    } else {
+      const float fl = floorf(scaled);
+      const float frac = scaled - fl;
+      const float u = splitmix_uniform(seed, static_cast<uint64_t>(r) * static_cast<uint64_t>(h) +
+                                                 static_cast<uint64_t>(c));
+      qi = to_i8(fl + (frac > u ? 1.0f : 0.0f));
+    }
+    if (qrow) qrow[c] = qi;
+    if (!keep) row[c] = static_cast<float>(qi) * s;
+  }
+}
+
+}  // namespace
+
+void launch_quant(float* grad_w, long long v, long long h, long long ld, const uint8_t* target_flags,
+                  int stochastic, uint64_t seed, int8_t* q, float* scale, cudaStream_t stream) {
+  if (v <= 0 || h <= 0) return;
+  quant_kernel<<<static_cast<unsigned>(v), QT, 0, stream>>>(grad_w, h, ld, target_flags, stochastic, seed, q, scale);
+}
+
+}  // namespace orda

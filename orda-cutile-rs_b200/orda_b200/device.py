@@ -1,0 +1,239 @@
+"""Device entry points of the C ABI for torch tensors (torch is used only for
+device memory and streams; every computation runs in liborda_b200.so).
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+
+from . import LossOptions, OrdaError, TeacherMode, ChunkPlan, _abi, _check
+from ._abi import load_library
+
+
+def _lib():
+    return load_library()
+
+
+class DeviceContext:
+    """Owns an `OrdaContext` (device workspace + status word)."""
+
+    def __init__(self, device: int = 0):
+        self.device = device
+        h = C.c_void_p()
+        buf = _abi.err_buf()
+        _check(_lib().orda_context_create(device, C.byref(h), buf, len(buf)), buf)
+        self.handle = h
+
+    def close(self) -> None:
+        if self.handle:
+            _lib().orda_context_destroy(self.handle)
+            self.handle = C.c_void_p()
+
+    def check(self) -> None:
+        buf = _abi.err_buf()
+        _check(_lib().orda_context_check(self.handle, buf, len(buf)), buf)
+
+    def workspace_bytes(self) -> int:
+        return int(_lib().orda_context_workspace_bytes(self.handle))
+
+    def inject_alloc_failures(self, count: int) -> None:
+        _lib().orda_context_inject_alloc_failures(self.handle, count)
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+
+def dev_mat(t: Optional[torch.Tensor]) -> _abi.OrdaDeviceMat:
+    m = _abi.OrdaDeviceMat()
+    if t is None:
+        return m
+    if t.dim() != 2 or t.stride(1) != 1:
+        raise ValueError("device matrices must be 2-D with unit column stride")
+    if t.dtype == torch.bfloat16:
+        m.dtype = _abi.DTYPE_BF16
+    elif t.dtype == torch.float32:
+        m.dtype = _abi.DTYPE_F32
+    else:
+        raise ValueError(f"unsupported dtype {t.dtype}")
+    m.data = t.data_ptr()
+    m.rows, m.cols = t.shape
+    m.ld = t.stride(0)
+    return m
+
+
+def _ptr(t: Optional[torch.Tensor]):
+    return None if t is None else t.data_ptr()
+
+
+def _stream(stream) -> int:
+    if stream is None:
+        return torch.cuda.current_stream().cuda_stream
+    if isinstance(stream, torch.cuda.Stream):
+        return stream.cuda_stream
+    return int(stream)
+
+
+@dataclass
+class DeviceLossResult:
+    scalars: torch.Tensor  # device float[4]: loss, student_ce, teacher_ce, kl
+    grad_student_hidden: torch.Tensor
+    grad_weight: torch.Tensor
+    grad_teacher_hidden: Optional[torch.Tensor]
+    grad_teacher_weight: Optional[torch.Tensor]
+    grad_weight_q: Optional[torch.Tensor]
+    grad_weight_scale: Optional[torch.Tensor]
+    chunk_plan: ChunkPlan
+
+
+def distillation_loss_device(
+    ctx: DeviceContext,
+    student_hidden: torch.Tensor,
+    weight: torch.Tensor,
+    labels: torch.Tensor,
+    teacher_mode: TeacherMode,
+    teacher_hidden: Optional[torch.Tensor] = None,
+    teacher_weight: Optional[torch.Tensor] = None,
+    teacher_logits: Optional[torch.Tensor] = None,
+    opts: Optional[LossOptions] = None,
+    out: Optional[dict] = None,
+    global_non_ignore: int = 0,
+    skip_quantize: bool = False,
+    want_int8: bool = False,
+    stream=None,
+) -> DeviceLossResult:
+    """`orda_distillation_loss_device`: bf16 device inputs, fp32 device grads."""
+    opts = opts or LossOptions()
+    dev = student_hidden.device
+    bt, h = student_hidden.shape
+    v = weight.shape[0]
+    w_t = opts.teacher_ce_weight
+    if w_t is None:
+        w_t = 1.0 if teacher_mode == TeacherMode.Tied else 0.0
+    live = teacher_mode in (TeacherMode.Tied, TeacherMode.Separate)
+    ht = teacher_hidden.shape[1] if teacher_mode == TeacherMode.Separate else h
+    out = dict(out or {})
+    f32 = dict(device=dev, dtype=torch.float32)
+    gsh = out.get("grad_student_hidden")
+    if gsh is None:
+        gsh = torch.empty(bt, h, **f32)
+    gw = out.get("grad_weight")
+    if gw is None:
+        gw = torch.empty(v, h, **f32)
+    gth = out.get("grad_teacher_hidden")
+    if gth is None and w_t > 0 and live:
+        gth = torch.empty(bt, ht, **f32)
+    gtw = out.get("grad_teacher_weight")
+    if gtw is None and w_t > 0 and teacher_mode == TeacherMode.Separate:
+        gtw = torch.empty(v, ht, **f32)
+    q = out.get("grad_weight_q")
+    sc = out.get("grad_weight_scale")
+    if want_int8 and opts.config.quantize_grad_weight:
+        if q is None:
+            q = torch.empty(v, h, device=dev, dtype=torch.int8)
+        if sc is None:
+            sc = torch.empty(v, **f32)
+    scal = out.get("scalars")
+    if scal is None:
+        scal = torch.empty(4, **f32)
+
+    t = _abi.OrdaDeviceTeacher()
+    t.mode = int(teacher_mode)
+    t.hidden = dev_mat(teacher_hidden)
+    t.weight = dev_mat(teacher_weight)
+    t.logits = dev_mat(teacher_logits)
+    o = _abi.OrdaDeviceOutputs()
+    o.grad_student_hidden = gsh.data_ptr()
+    o.ld_grad_student_hidden = gsh.stride(0)
+    o.grad_weight = gw.data_ptr()
+    o.ld_grad_weight = gw.stride(0)
+    if gth is not None:
+        o.grad_teacher_hidden = gth.data_ptr()
+        o.ld_grad_teacher_hidden = gth.stride(0)
+    if gtw is not None:
+        o.grad_teacher_weight = gtw.data_ptr()
+        o.ld_grad_teacher_weight = gtw.stride(0)
+    o.grad_weight_q = _ptr(q)
+    o.grad_weight_scale = _ptr(sc)
+    o.scalars = scal.data_ptr()
+    shard = _abi.OrdaShardOptions(int(global_non_ignore), int(skip_quantize))
+    plan = _abi.OrdaChunkPlan()
+    buf = _abi.err_buf()
+    rc = _lib().orda_distillation_loss_device(
+        ctx.handle,
+        C.byref(dev_mat(student_hidden)),
+        C.byref(dev_mat(weight)),
+        labels.data_ptr(),
+        labels.numel(),
+        C.byref(t),
+        C.byref(opts._c()),
+        C.byref(o),
+        C.byref(shard),
+        _stream(stream),
+        C.byref(plan),
+        buf,
+        len(buf),
+    )
+    _check(rc, buf)
+    return DeviceLossResult(
+        scalars=scal,
+        grad_student_hidden=gsh,
+        grad_weight=gw,
+        grad_teacher_hidden=gth,
+        grad_teacher_weight=gtw,
+        grad_weight_q=q,
+        grad_weight_scale=sc,
+        chunk_plan=ChunkPlan(int(plan.chunk_size), int(plan.num_chunks)),
+    )
+
+
+def gemm_bf16(
+    ctx: DeviceContext,
+    a: torch.Tensor,
+    a_kind: int,
+    b: torch.Tensor,
+    b_kind: int,
+    c: torch.Tensor,
+    m: int,
+    n: int,
+    k: int,
+    alpha: float = 1.0,
+    beta: float = 0.0,
+    stream=None,
+) -> torch.Tensor:
+    """`orda_gemm_bf16_device`: C = alpha * op(A) @ op(B) + beta * C."""
+    buf = _abi.err_buf()
+    rc = _lib().orda_gemm_bf16_device(
+        ctx.handle, a.data_ptr(), a.stride(0), a_kind, b.data_ptr(), b.stride(0), b_kind, c.data_ptr(), c.stride(0),
+        m, n, k, alpha, beta, _stream(stream), buf, len(buf),
+    )
+    _check(rc, buf)
+    return c
+
+
+def quantize_grad_w(
+    ctx: DeviceContext,
+    grad_w: torch.Tensor,
+    labels: torch.Tensor,
+    ignore_index: int = -100,
+    stochastic: bool = False,
+    seed: int = 0,
+    q: Optional[torch.Tensor] = None,
+    scale: Optional[torch.Tensor] = None,
+    stream=None,
+):
+    """`orda_quantize_grad_w_device`; grad_w is overwritten with the
+    dequantised values, q / scale receive the INT8 body and scales."""
+    v, h = grad_w.shape
+    buf = _abi.err_buf()
+    rc = _lib().orda_quantize_grad_w_device(
+        ctx.handle, grad_w.data_ptr(), v, h, grad_w.stride(0), labels.data_ptr(), labels.numel(), ignore_index,
+        int(stochastic), int(seed) & ((1 << 64) - 1), _ptr(q), _ptr(scale), _stream(stream), buf, len(buf),
+    )
+    _check(rc, buf)
+    return grad_w, q, scale
