@@ -1,0 +1,426 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 distillation loss (fwd + bwd) on BASELINE's metric
+configuration, printing one JSON line.
+
+Workload (the metric's config): Precomputed teacher
+logits, BT=8192 rows per GPU, H=4096, V=131072, bf16 inputs, kd=0.4, T=1.5,
+INT8 row-wise grad_W round trip; resolver plan 16 chunks x 512 rows. Synthetic
+seeded inputs (h ~ N(0,1), W ~ N(0,0.02), teacher logits ~ N(0,2) read as
+variance 2, labels uniform). A step is one `distillation_loss` call over the
+rank's rows. Inputs (W 1 GiB, teacher logits 2 GiB per GPU) are larger than
+the 126 MB L2, so no flush is needed between steps.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N>1 runs under torchrun (one rank per GPU, NCCL): rows are sharded across
+ranks (weak scaling, 8192 rows per GPU) with a reduce-scatter of grad_W.
+`--impl reference` times the reference's CPU path (the oracle restatement,
+all host threads) on a bounded row sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO / "orda-cutile-rs_b200"))
+sys.path.insert(0, str(REPO / "oracle"))
+
+METRIC = "distillation fwd+bwd tokens/sec at BT=8192,H=4096,V=131072; % bf16 tensor peak"
+CFG = dict(bt=8192, h=4096, v=131072, kd=0.4, temperature=1.5, teacher_std=2.0 ** 0.5, w_std=0.02)
+WORKLOAD = ("c4: Precomputed teacher logits, BT=8192 rows/GPU, H=4096, V=131072, bf16 inputs, "
+            "kd=0.4, T=1.5, INT8 grad_W round trip, chunks 16x512")
+
+
+def algorithmic_flops(bt, h, v):
+    """2*BT*V*(3*H_s) for the Precomputed teacher: logits, dgrad, wgrad."""
+    return 2.0 * bt * v * 3 * h
+
+
+def load_peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d["bf16_tflops"], d.get("bf16_tflops_sustained"), d["hbm_gbs"], "measured"
+    return 1590.0, 1400.0, 6650.0, "fallback"
+
+
+def host_cores():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+# ------------------------------------------------------------------ clocks
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id: str):
+        self.gpu_id = gpu_id
+        self.proc = None
+        self.f = None
+
+    def start(self):
+        try:
+            self.f = tempfile.TemporaryFile(mode="w+")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", self.gpu_id], stdout=self.f, stderr=subprocess.DEVNULL)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.f.seek(0)
+        rows = [r.split(",") for r in self.f.read().strip().splitlines() if r.count(",") >= 8]
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
+        smax = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].strip() == "Active"})
+        power = [float(r[3]) for r in rows if r[3].strip().replace(".", "").isdigit()]
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": reasons, "samples": len(rows), "power_w_max": max(power) if power else None}
+
+
+# ------------------------------------------------------------- CPU baselines
+
+def cpu_reference_sample(rows, nthreads, seed=77):
+    """Times the reference CPU path (oracle restatement of src/api.rs) on
+    `rows` rows of the workload (full H and V, Precomputed teacher, INT8
+    round trip). Returns seconds."""
+    import torch
+
+    import oracle
+    import orda_b200 as ob
+
+    gen = torch.Generator().manual_seed(seed)
+    h, v = CFG["h"], CFG["v"]
+    hs = torch.randn(rows, h, generator=gen).bfloat16().float().numpy()
+    w = (CFG["w_std"] * torch.randn(v, h, generator=gen)).bfloat16().float().numpy()
+    tl = (CFG["teacher_std"] * torch.randn(rows, v, generator=gen)).bfloat16().float().numpy()
+    labels = torch.randint(0, v, (rows,), generator=gen).tolist()
+    opts = ob.LossOptions(kd_weight=CFG["kd"], temperature=CFG["temperature"],
+                          config=ob.KernelConfig(quantize_grad_weight=True))
+    s, wm, t = ob.Mat.from_array(hs), ob.Mat.from_array(w), ob.Teacher.Precomputed(ob.Mat.from_array(tl))
+    t0 = time.perf_counter()
+    out = oracle.distillation_loss(s, wm, labels, t, opts, nthreads=nthreads)
+    dt = time.perf_counter() - t0
+    assert np.isfinite(out.loss)
+    return dt
+
+
+def extrapolate(samples, bt=8192, chunk_rows=512):
+    """Least-squares fit t = a*rows + b over (rows, seconds) samples of one
+    reference call each (one chunk per call), then the reference's own plan
+    for the full workload: 16 chunks x 512 rows -> T = 16 * (a*512 + b).
+    b holds the per-call O(V*H) work (grad_W-sized zero/add/scale/quantise
+    passes); at full size the per-row GEMM term a dominates."""
+    r = np.array([x for x, _ in samples], dtype=np.float64)
+    t = np.array([y for _, y in samples], dtype=np.float64)
+    a, b = np.polyfit(r, t, 1)
+    a = max(a, 1e-12)
+    b = max(b, 0.0)
+    chunks = bt // chunk_rows
+    total = chunks * (a * chunk_rows + b)
+    return bt / total, a, b, total
+
+
+def cpu_baseline_line(nthreads, rows_pair, reps=1):
+    samples = []
+    for _ in range(reps):
+        for rows in rows_pair:
+            samples.append((rows, cpu_reference_sample(rows, nthreads, seed=200 + len(samples))))
+    value, a, b, total = extrapolate(samples)
+    desc = (f"reference CPU path (oracle restatement), {nthreads} thread(s): calls of "
+            f"{'/'.join(str(x) for x in rows_pair)} rows at full H=4096, V=131072 (Precomputed, INT8 round trip) "
+            f"timed {', '.join(f'{t:.1f}s' for _, t in samples)}; fit t = {a:.3f} s/row + {b:.2f} s/call, "
+            f"extrapolated to the 16 x 512-row plan ({total / 3600:.2f} h for 8192 rows)")
+    return value, desc, samples
+
+
+def run_reference_arm(args):
+    """--impl reference: the reference's CPU path with all host threads."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    cores = host_cores()
+    # Two sample sizes: 1 row (mostly the per-call O(V*H) passes) and the
+    # smallest power of two whose call takes about twice as long, so the
+    # per-row GEMM term is resolved by the fit.
+    t1 = cpu_reference_sample(1, cores)
+    rows = 2
+    t = cpu_reference_sample(rows, cores)
+    while t < 2.0 * t1 and t < 30.0 and rows < 512:
+        rows *= 2
+        t = cpu_reference_sample(rows, cores)
+    for _ in range(max(0, args.warmup - 2)):
+        cpu_reference_sample(rows, cores)
+    samples = []
+    for i in range(max(2, args.steps)):
+        r = 1 if i % 2 == 0 else rows
+        samples.append((r, cpu_reference_sample(r, cores, seed=100 + i)))
+    value, a, b, total = extrapolate(samples)
+    per = statistics.mean(t for _, t in samples)
+    sample = (f"per step one reference call on 1 or {rows} of 8192 rows (alternating), full H=4096 and "
+              f"V=131072, Precomputed teacher, INT8 round trip; fit t = {a:.4f} s/row + {b:.2f} s/call, "
+              f"extrapolated to the reference's 16 x 512-row plan ({total / 3600:.2f} h for 8192 rows)")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": per * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32 (CPU reference path: f32 GEMMs, f64 softmax)",
+        "data": "synthetic", "config": {"workload": WORKLOAD, "sample_rows_per_step": [rows, 2 * rows]},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# --------------------------------------------------------------- our arm
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    import orda_b200 as ob
+    from orda_b200 import shard
+    from orda_b200.device import DeviceContext, distillation_loss_device, quantize_grad_w
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        print(f"warning: --gpus {args.gpus} but WORLD_SIZE {world}", file=sys.stderr)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+
+    bt, h, v = CFG["bt"], CFG["h"], CFG["v"]
+    gen = torch.Generator(device=dev).manual_seed(1000 + rank)
+    wgen = torch.Generator(device=dev).manual_seed(7)
+    hs = torch.randn(bt, h, generator=gen, device=dev).bfloat16()
+    w = (CFG["w_std"] * torch.randn(v, h, generator=wgen, device=dev)).bfloat16()
+    tl = torch.empty(bt, v, device=dev, dtype=torch.bfloat16)
+    for r0 in range(0, bt, 1024):  # generate in slabs to bound the fp32 temporary
+        tl[r0:r0 + 1024] = (CFG["teacher_std"] * torch.randn(min(1024, bt - r0), v, generator=gen, device=dev))
+    labels = torch.randint(0, v, (bt,), generator=gen, device=dev)
+    opts = ob.LossOptions(kd_weight=CFG["kd"], temperature=CFG["temperature"],
+                          config=ob.KernelConfig(quantize_grad_weight=True))
+    out = {"grad_student_hidden": torch.empty(bt, h, device=dev), "grad_weight": torch.empty(v, h, device=dev),
+           "scalars": torch.empty(4, device=dev)}
+    q = torch.empty(v // world, h, device=dev, dtype=torch.int8)
+    qs = torch.empty(v // world, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    ctx = DeviceContext(local)
+    n_global = bt * world if world == 1 else shard.global_non_ignore(labels, -100)
+
+    def step():
+        if world == 1:
+            out["grad_weight_q"], out["grad_weight_scale"] = q, qs
+            return distillation_loss_device(ctx, hs, w, labels, ob.TeacherMode.Precomputed, teacher_logits=tl,
+                                            opts=opts, out=out, want_int8=True, stream=stream)
+
+        def compute(n):
+            r = distillation_loss_device(ctx, hs, w, labels, ob.TeacherMode.Precomputed, teacher_logits=tl,
+                                         opts=opts, out=out, global_non_ignore=n, skip_quantize=True,
+                                         stream=stream)
+            return r.scalars, r.grad_student_hidden, r.grad_weight
+
+        def quant(sl, shifted):
+            quantize_grad_w(ctx, sl, shifted, -100, False, 0, q, qs, stream=stream)
+
+        return shard.row_sharded_step(compute, labels, -100, n_global, quantize=quant)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    ctx.check()
+
+    # ---------------- timed region
+    sampler = None
+    if rank == 0 and not args.no_clocks:
+        uuid = getattr(torch.cuda.get_device_properties(dev), "uuid", None)
+        sampler = ClockSampler(f"GPU-{uuid}" if uuid is not None else str(local))
+        sampler.start()
+        time.sleep(0.3)
+    ctx.reset_timing()
+    ctx.enable_timing(True)
+    launches0 = ctx.launch_count()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms_total = ev0.elapsed_time(ev1)
+    phases = ctx.phase_times()
+    ctx.enable_timing(False)
+    launches = ctx.launch_count() - launches0
+    clocks = sampler.stop() if sampler else None
+    ctx.check()
+    if world > 1:
+        t = torch.tensor([ms_total], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_total = float(t.item())
+    ms_step = ms_total / args.steps
+    tokens = bt * world
+    value = tokens / (ms_step / 1e3)
+
+    # ---------------- roofline of the dominant kernel family (tcgen05 GEMM)
+    peak, peak_sus, hbm, peak_kind = load_peaks()
+    gemm_ms = sum(phases[p][0] for p in ("logits_gemm", "dgrad_gemm", "wgrad_gemm")) / args.steps
+    gemm_launches = sum(phases[p][1] for p in ("logits_gemm", "dgrad_gemm", "wgrad_gemm")) / args.steps
+    flops = algorithmic_flops(bt, h, v)
+    achieved = flops / (gemm_ms / 1e3) / 1e12
+    traffic = None
+    tfile = REPO / "profiles" / "gemm_traffic.json"
+    if tfile.exists():
+        traffic = json.loads(tfile.read_text()).get("bytes_per_step")
+    roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                "traffic": traffic, "kernel": "gemm_kernel (tcgen05, 3 layouts)",
+                "launches_per_step": gemm_launches, "gemm_ms_per_step": gemm_ms,
+                "peak_kind": f"{peak_kind} burst bf16 (MEASURED_PEAKS.json bf16_tflops)",
+                "frac_of_sustained": achieved / peak_sus if peak_sus else None}
+    step_tflops = flops * world / (ms_step / 1e3) / 1e12 / world
+
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "global_batch": tokens, "seq_len": None, "rows_per_gpu": bt,
+                   "parallelism": "rows sharded, grad_W reduce-scatter" if world > 1 else "single GPU",
+                   "l2": "inputs larger than L2 (W 1 GiB, teacher logits 2 GiB per GPU); no flush"},
+        "step_tflops_per_gpu": step_tflops, "step_frac_of_peak": step_tflops / peak,
+        "phases_ms_per_step": {k: v_[0] / args.steps for k, v_ in phases.items()},
+        "roofline": roofline, "gpu_launches": int(launches), "clocks": clocks,
+    }
+
+    # ---------------- e2e through the host-Mat C ABI (HOST buffers)
+    if not args.no_e2e:
+        line["e2e"] = e2e_measure(args, ob, hs, w, tl, labels, opts, rank, world, dist)
+    else:
+        line["e2e"] = None
+
+    # ---------------- CPU baseline (rank 0, N=1 only)
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        val, desc, _ = cpu_baseline_line(1, (1, args.cpu_rows))
+        line["cpu_baseline"] = {"value": val, "unit": "tokens/s", "cores": 1, "kind": "port", "sample": desc}
+    else:
+        line["cpu_baseline"] = None
+
+    ctx.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+def e2e_measure(args, ob, hs, w, tl, labels, opts, rank, world, dist):
+    """The reference-facing host entry (orda_distillation_loss) with pinned
+    f32 host inputs; every step copies the inputs host->device and the
+    gradients device->host inside the call."""
+    import torch
+
+    from orda_b200 import _abi
+
+    lib = ob.load_library()
+    hs_h = hs.float().cpu().pin_memory()
+    w_h = w.float().cpu().pin_memory()
+    tl_h = torch.empty(tl.shape, dtype=torch.float32, pin_memory=True)
+    for r0 in range(0, tl.shape[0], 1024):
+        tl_h[r0:r0 + 1024].copy_(tl[r0:r0 + 1024].float())
+    lab_h = labels.cpu().contiguous()
+    s, wm = ob.Mat.from_array(hs_h.numpy()), ob.Mat.from_array(w_h.numpy())
+    t = ob.Teacher.Precomputed(ob.Mat.from_array(tl_h.numpy()))
+    sc, wc, tc, oc = s._c(), wm._c(), t._c(), opts._c()
+    lab_p = C.cast(lab_h.data_ptr(), C.POINTER(C.c_int64))
+    buf = _abi.err_buf()
+
+    def call():
+        o = _abi.OrdaOutput()
+        rc = lib.orda_distillation_loss(C.byref(sc), C.byref(wc), lab_p, lab_h.numel(), C.byref(tc), C.byref(oc),
+                                        C.byref(o), buf, len(buf))
+        if rc:
+            raise ob.OrdaError(rc, buf.value.decode())
+        loss = o.loss
+        lib.orda_output_free(C.byref(o))
+        return loss
+
+    call()  # warm-up (allocates the staging buffers)
+    if world > 1:
+        dist.barrier()
+    times = []
+    for _ in range(args.e2e_steps):
+        t0 = time.perf_counter()
+        call()
+        times.append(time.perf_counter() - t0)
+    per = statistics.mean(times)
+    if world > 1:
+        tt = torch.tensor([per], device="cuda", dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        per = float(tt.item())
+    bt, h, v = CFG["bt"], CFG["h"], CFG["v"]
+    h2d = bt * h * 4 + v * h * 4 + bt * v * 4 + bt * 8
+    d2h = bt * h * 4 + v * h * 4 + 16
+    return {"value": bt * world / per, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "ms_per_step": per * 1e3, "api": "orda_distillation_loss (f32 host Mats, pinned inputs)",
+            "scope": "per-rank local shard" if world > 1 else "full"}
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--e2e-steps", type=int, default=2)
+    ap.add_argument("--cpu-rows", type=int, default=3)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-clocks", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        print("note: at least 3 warm-up steps are required for a valid number; using 3", file=sys.stderr)
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference_arm(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -216,6 +216,20 @@ ORDA_API void orda_context_destroy(OrdaContext* ctx);
 ORDA_API int orda_context_check(OrdaContext* ctx, char* err, size_t err_len);
 /* Bytes of device workspace currently held by the context. */
 ORDA_API size_t orda_context_workspace_bytes(const OrdaContext* ctx);
+/* Phase timing: when enabled, the device entry records CUDA events around
+ * each kernel phase on the stream it launches on. Phases:
+ *   0 logits GEMMs (teacher + student, fused statistics epilogue)
+ *   1 row kernel (losses + bf16 logit gradients)
+ *   2 dgrad GEMMs   3 wgrad GEMMs   4 INT8 quantiser   5 label pass + finalize
+ * orda_context_phase_times synchronizes, adds the elapsed milliseconds and
+ * kernel-launch counts accumulated since the last reset into the outputs
+ * (arrays of ORDA_NUM_PHASES entries) and returns ORDA_NUM_PHASES. */
+#define ORDA_NUM_PHASES 6
+ORDA_API void orda_context_enable_timing(OrdaContext* ctx, int enable);
+ORDA_API int orda_context_phase_times(OrdaContext* ctx, double* ms_out, uint64_t* launches_out);
+ORDA_API void orda_context_reset_timing(OrdaContext* ctx);
+/* Total kernels this context has launched (all calls, timing on or off). */
+ORDA_API uint64_t orda_context_launch_count(const OrdaContext* ctx);
 /* Test hook for the OOM ladder: the next `count` workspace allocations fail
  * as if cudaMalloc had returned cudaErrorMemoryAllocation. */
 ORDA_API void orda_context_inject_alloc_failures(OrdaContext* ctx, int count);

@@ -29,6 +29,7 @@
 #include <cstring>
 #include <memory>
 #include <mutex>
+#include <optional>
 #include <vector>
 
 #include "../../include/orda.h"
@@ -49,6 +50,18 @@ struct OrdaContext {
   cudaStream_t last_stream = nullptr;
   cudaStream_t own_stream = nullptr;
   std::mutex mu;
+  // phase timing (see orda_context_enable_timing)
+  bool timing = false;
+  struct PhaseEvents {
+    int phase;
+    cudaEvent_t begin, end;
+    int launches;
+  };
+  std::vector<PhaseEvents> pending;
+  std::vector<cudaEvent_t> event_pool;
+  double phase_ms[ORDA_NUM_PHASES] = {};
+  uint64_t phase_launches[ORDA_NUM_PHASES] = {};
+  uint64_t launches = 0;
 };
 
 namespace orda {
@@ -153,6 +166,42 @@ int try_alloc_cb(size_t num_chunks, size_t chunk_size, void* user) {
   return 0;
 }
 
+// Records the span of one kernel phase on the launch stream when timing is
+// enabled; counts kernel launches always.
+struct Phase {
+  OrdaContext* ctx;
+  int phase;
+  cudaStream_t st;
+  cudaEvent_t begin = nullptr;
+  int n = 0;
+  Phase(OrdaContext* c, int p, cudaStream_t s) : ctx(c), phase(p), st(s) {
+    if (ctx->timing) {
+      begin = take_event(ctx);
+      cudaEventRecord(begin, st);
+    }
+  }
+  void launched(int k = 1) {
+    n += k;
+    ctx->launches += static_cast<uint64_t>(k);
+  }
+  ~Phase() {
+    if (!ctx->timing || !begin) return;
+    cudaEvent_t end = take_event(ctx);
+    cudaEventRecord(end, st);
+    ctx->pending.push_back({phase, begin, end, n});
+  }
+  static cudaEvent_t take_event(OrdaContext* c) {
+    if (!c->event_pool.empty()) {
+      cudaEvent_t e = c->event_pool.back();
+      c->event_pool.pop_back();
+      return e;
+    }
+    cudaEvent_t e = nullptr;
+    cudaEventCreate(&e);
+    return e;
+  }
+};
+
 int cuda_fail(cudaError_t e, const char* what, char* err, size_t len) {
   set_error(err, len, "CUDA error in %s: %s", what, cudaGetErrorString(e));
   return ORDA_ERR_CUDA;
@@ -238,9 +287,13 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
   if ((e = cudaMemsetAsync(ctx->d_words, 0, 2 * sizeof(int), st)) != cudaSuccess) return cuda_fail(e, "memset", err, len);
   if (tflags && (e = cudaMemsetAsync(tflags, 0, v, st)) != cudaSuccess) return cuda_fail(e, "memset", err, len);
   const long long denom_override = shard ? shard->global_non_ignore : 0;
-  launch_label_prep(in.labels, static_cast<long long>(bt), static_cast<long long>(v), o.ignore_index,
-                    o.reduction == ORDA_REDUCTION_SUM, denom_override, ctx->d_words + 1, ctx->d_mean_scale, tflags,
-                    status, st);
+  {
+    Phase ph_prep(ctx, 5, st);
+    ph_prep.launched();
+    launch_label_prep(in.labels, static_cast<long long>(bt), static_cast<long long>(v), o.ignore_index,
+                      o.reduction == ORDA_REDUCTION_SUM, denom_override, ctx->d_words + 1, ctx->d_mean_scale,
+                      tflags, status, st);
+  }
 
   const float inv_t = 1.0f / f.temperature;
   const char* why = nullptr;
@@ -250,8 +303,11 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
     const size_t g1 = std::min(g0 + group_rows, bt);
     for (size_t s = g0; s < g1; s += cs) {
       const size_t n = std::min(cs, g1 - s);
+      std::optional<Phase> ph_fwd;
+      ph_fwd.emplace(ctx, 0, st);
       // ---- teacher logits (Tied / Separate)
       if (f.teacher_rows) {
+        ph_fwd->launched();
         GemmDesc gd;
         const MatRef& tw = in.mode == ORDA_TEACHER_TIED ? in.w : in.wt;
         const size_t kdim = in.mode == ORDA_TEACHER_TIED ? h : ht;
@@ -276,6 +332,7 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
       }
       // ---- student logits + statistics
       {
+        ph_fwd->launched();
         GemmDesc gd;
         gd.a[0] = MatRef{static_cast<const uint16_t*>(in.hs.ptr) + s * in.hs.ld, static_cast<long long>(n),
                          static_cast<long long>(h), in.hs.ld};
@@ -313,8 +370,11 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
         if ((e = gemm_launch(gd, ctx->num_sms, st, &why)) != cudaSuccess)
           return cuda_fail(e, why ? why : "student logits GEMM", err, len);
       }
+      ph_fwd.reset();
       // ---- row pass: losses and logit gradients
       {
+        Phase ph_rows(ctx, 1, st);
+        ph_rows.launched();
         RowArgs r{};
         r.n = static_cast<int>(n);
         r.v = static_cast<int>(v);
@@ -360,6 +420,8 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
     const long long vv = static_cast<long long>(v);
     // ---- dgrad: grad_h rows = mean_scale * dlogits @ W
     auto dgrad = [&](const uint16_t* dl, const MatRef& wmat, long long ncols, float* outp, size_t ldo) -> int {
+      Phase ph(ctx, 2, st);
+      ph.launched();
       GemmDesc gd;
       gd.a[0] = MatRef{dl, rows_g, vv, static_cast<long long>(L.ldd)};
       gd.b_mn_major = true;
@@ -385,6 +447,8 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
     }
     // ---- wgrad: grad_W (+)= mean_scale * dlogits^T @ hidden
     {
+      Phase ph(ctx, 3, st);
+      ph.launched();
       GemmDesc gd;
       gd.a_mn_major = true;
       gd.b_mn_major = true;
@@ -411,6 +475,8 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
         return cuda_fail(e, why ? why : "wgrad GEMM", err, len);
     }
     if (f.teacher_grad && in.mode == ORDA_TEACHER_SEPARATE) {
+      Phase ph(ctx, 3, st);
+      ph.launched();
       GemmDesc gd;
       gd.a_mn_major = true;
       gd.b_mn_major = true;
@@ -430,9 +496,15 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
         return cuda_fail(e, why ? why : "teacher wgrad GEMM", err, len);
     }
   }
-  launch_finalize(nll_s, nll_t, kl_rows, static_cast<long long>(bt), ctx->d_mean_scale, f.w_s, f.w_t, f.kd,
+  {
+    Phase ph(ctx, 5, st);
+    ph.launched();
+    launch_finalize(nll_s, nll_t, kl_rows, static_cast<long long>(bt), ctx->d_mean_scale, f.w_s, f.w_t, f.kd,
                   out.scalars, st);
+  }
   if (f.quant) {
+    Phase ph(ctx, 4, st);
+    ph.launched();
     const uint64_t seed = o.config.has_stochastic_seed ? o.config.stochastic_seed : 0;
     launch_quant(out.grad_weight, static_cast<long long>(v), static_cast<long long>(h),
                  static_cast<long long>(out.ld_grad_weight), tflags, o.config.stochastic_rounding, seed,
@@ -520,6 +592,11 @@ void orda_context_destroy(OrdaContext* ctx) {
   cudaFree(ctx->d_words);
   cudaFree(ctx->d_mean_scale);
   if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
+  for (auto& pe : ctx->pending) {
+    cudaEventDestroy(pe.begin);
+    cudaEventDestroy(pe.end);
+  }
+  for (cudaEvent_t e : ctx->event_pool) cudaEventDestroy(e);
   delete ctx;
 }
 
@@ -627,6 +704,7 @@ int orda_quantize_grad_w_device(OrdaContext* ctx, float* grad_w, size_t v, size_
   cudaError_t e = cudaMemsetAsync(flags, 0, v, st);
   if (e != cudaSuccess) return cuda_fail(e, "memset", err, err_len);
   launch_target_flags(labels, static_cast<long long>(bt), static_cast<long long>(v), ignore_index, flags, st);
+  ctx->launches += 2;
   launch_quant(grad_w, static_cast<long long>(v), static_cast<long long>(h), static_cast<long long>(ld), flags,
                stochastic, seed, q, scale, st);
   if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(e, "quantise", err, err_len);
@@ -663,11 +741,54 @@ int orda_gemm_bf16_device(OrdaContext* ctx, const void* a, size_t lda, int a_kin
   cudaError_t e = cudaMemsetAsync(ctx->d_words, 0, sizeof(int), st);
   if (e != cudaSuccess) return cuda_fail(e, "memset", err, err_len);
   const char* why = nullptr;
+  ctx->launches += 1;
   e = gemm_launch(gd, ctx->num_sms, st, &why);
   if (e != cudaSuccess) return cuda_fail(e, why ? why : "GEMM", err, err_len);
   ctx->last_stream = st;
   return ORDA_OK;
 }
+
+void orda_context_enable_timing(OrdaContext* ctx, int enable) {
+  if (ctx) ctx->timing = enable != 0;
+}
+
+int orda_context_phase_times(OrdaContext* ctx, double* ms_out, uint64_t* launches_out) {
+  if (!ctx) return 0;
+  std::lock_guard<std::mutex> lock(ctx->mu);
+  cudaSetDevice(ctx->device);
+  for (auto& pe : ctx->pending) {
+    cudaEventSynchronize(pe.end);
+    float ms = 0.0f;
+    if (cudaEventElapsedTime(&ms, pe.begin, pe.end) == cudaSuccess) ctx->phase_ms[pe.phase] += ms;
+    ctx->phase_launches[pe.phase] += static_cast<uint64_t>(pe.launches);
+    ctx->event_pool.push_back(pe.begin);
+    ctx->event_pool.push_back(pe.end);
+  }
+  ctx->pending.clear();
+  for (int i = 0; i < ORDA_NUM_PHASES; ++i) {
+    if (ms_out) ms_out[i] = ctx->phase_ms[i];
+    if (launches_out) launches_out[i] = ctx->phase_launches[i];
+  }
+  return ORDA_NUM_PHASES;
+}
+
+void orda_context_reset_timing(OrdaContext* ctx) {
+  if (!ctx) return;
+  std::lock_guard<std::mutex> lock(ctx->mu);
+  cudaSetDevice(ctx->device);
+  for (auto& pe : ctx->pending) {
+    cudaEventSynchronize(pe.end);
+    ctx->event_pool.push_back(pe.begin);
+    ctx->event_pool.push_back(pe.end);
+  }
+  ctx->pending.clear();
+  for (int i = 0; i < ORDA_NUM_PHASES; ++i) {
+    ctx->phase_ms[i] = 0.0;
+    ctx->phase_launches[i] = 0;
+  }
+}
+
+uint64_t orda_context_launch_count(const OrdaContext* ctx) { return ctx ? ctx->launches : 0; }
 
 // ------------------------------------------------------------ host-Mat entry
 

@@ -506,12 +506,9 @@ bool encode_map(CUtensorMap* map, const MatRef& m, int box_inner, int box_outer)
 template <bool A_MN, bool B_MN, int EPI>
 cudaError_t launch_t(const CUtensorMap* maps, const KParams& kp, int grid, cudaStream_t stream) {
   auto kern = gemm_kernel<A_MN, B_MN, EPI>;
-  static bool attr_done = false;  // per instantiation; attribute is per-function
-  if (!attr_done) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-    if (e != cudaSuccess) return e;
-    attr_done = true;
-  }
+  // Per device and cheap; set on every launch so any device/thread works.
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+  if (e != cudaSuccess) return e;
   kern<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(maps[0], maps[1], maps[2], maps[3], kp);
   return cudaGetLastError();
 }

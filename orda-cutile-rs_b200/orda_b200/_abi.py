@@ -26,6 +26,8 @@ BACKEND_AUTO, BACKEND_CPU, BACKEND_CUDA = 0, 1, 2
 PROFILE_BALANCED, PROFILE_FAST, PROFILE_DEBUG = 0, 1, 2
 CHUNK_AUTO, CHUNK_FIXED = 0, 1
 DTYPE_BF16, DTYPE_F32 = 0, 1
+NUM_PHASES = 6
+PHASE_NAMES = ("logits_gemm", "rows", "dgrad_gemm", "wgrad_gemm", "quant", "prep_finalize")
 
 
 class OrdaMatF32(C.Structure):
@@ -187,6 +189,10 @@ SIGNATURES = {
     "orda_context_check": (C.c_int, [C.c_void_p, C.c_char_p, C.c_size_t]),
     "orda_context_workspace_bytes": (C.c_size_t, [C.c_void_p]),
     "orda_context_inject_alloc_failures": (None, [C.c_void_p, C.c_int]),
+    "orda_context_enable_timing": (None, [C.c_void_p, C.c_int]),
+    "orda_context_phase_times": (C.c_int, [C.c_void_p, C.POINTER(C.c_double), C.POINTER(C.c_uint64)]),
+    "orda_context_reset_timing": (None, [C.c_void_p]),
+    "orda_context_launch_count": (C.c_uint64, [C.c_void_p]),
     "orda_distillation_loss_device": (
         C.c_int,
         [

@@ -42,6 +42,23 @@ class DeviceContext:
     def inject_alloc_failures(self, count: int) -> None:
         _lib().orda_context_inject_alloc_failures(self.handle, count)
 
+    def enable_timing(self, on: bool = True) -> None:
+        _lib().orda_context_enable_timing(self.handle, int(on))
+
+    def reset_timing(self) -> None:
+        _lib().orda_context_reset_timing(self.handle)
+
+    def phase_times(self) -> dict:
+        """Milliseconds and kernel launches per phase since the last reset
+        (events recorded on the launch stream; synchronizes)."""
+        ms = (C.c_double * _abi.NUM_PHASES)()
+        n = (C.c_uint64 * _abi.NUM_PHASES)()
+        _lib().orda_context_phase_times(self.handle, ms, n)
+        return {name: (float(ms[i]), int(n[i])) for i, name in enumerate(_abi.PHASE_NAMES)}
+
+    def launch_count(self) -> int:
+        return int(_lib().orda_context_launch_count(self.handle))
+
     def __enter__(self):
         return self
 

@@ -1,0 +1,95 @@
+"""Row-sharded (data-parallel over tokens) distillation across GPUs.
+
+Each rank owns a contiguous block of the BT rows and a replica of W. Ranks
+compute their rows' loss terms and gradients with the global mean
+denominator (the token count of all ranks), so the per-rank scalar sums and
+grad_W partials add up to the single-GPU result. The only cross-rank traffic
+is one reduction of grad_W (reduce-scatter: rank r keeps vocabulary rows
+[r*V/N, (r+1)*V/N)), a 4-float all-reduce of the loss scalars and, for the
+INT8 round trip, an all-gather of the labels so every rank knows the target
+rows of its vocabulary slice. grad_hidden stays local.
+
+The collective flow is written against a `compute` callable so the same code
+drives the B200 path (NCCL, CUDA tensors) and the CPU tests (gloo, with the
+oracle as compute).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Callable, Optional
+
+import torch
+import torch.distributed as dist
+
+
+def shard_rows(bt_total: int, world: int, rank: int) -> tuple[int, int]:
+    """Contiguous row block of `rank` (the first bt_total % world ranks take
+    one extra row)."""
+    base, extra = divmod(bt_total, world)
+    start = rank * base + min(rank, extra)
+    return start, start + base + (1 if rank < extra else 0)
+
+
+def vocab_slice(v: int, world: int, rank: int) -> tuple[int, int]:
+    """Vocabulary rows of grad_W owned by `rank` after the reduce-scatter."""
+    if v % world:
+        raise ValueError(f"V={v} must be divisible by the world size {world} for the reduce-scatter")
+    n = v // world
+    return rank * n, (rank + 1) * n
+
+
+def global_non_ignore(labels_local: torch.Tensor, ignore_index: int, group=None) -> int:
+    cnt = (labels_local != ignore_index).sum().to(torch.int64).reshape(1)
+    dist.all_reduce(cnt, group=group)
+    return int(cnt.item())
+
+
+@dataclass
+class ShardResult:
+    scalars: torch.Tensor          # global [loss, student_ce, teacher_ce, kl]
+    grad_student_hidden: torch.Tensor  # local rows
+    grad_weight_slice: torch.Tensor    # this rank's vocabulary slice of grad_W
+    vocab_range: tuple[int, int]
+
+
+def reduce_grad_weight(grad_w: torch.Tensor, group=None) -> torch.Tensor:
+    """Sum of grad_W over ranks, returning this rank's vocabulary slice."""
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    v0, v1 = vocab_slice(grad_w.shape[0], world, rank)
+    if dist.get_backend(group) == "nccl":
+        out = torch.empty(v1 - v0, grad_w.shape[1], dtype=grad_w.dtype, device=grad_w.device)
+        dist.reduce_scatter_tensor(out, grad_w, group=group)
+        return out
+    dist.all_reduce(grad_w, group=group)
+    return grad_w[v0:v1]
+
+
+def row_sharded_step(
+    compute: Callable[[int], tuple[torch.Tensor, torch.Tensor, torch.Tensor]],
+    labels_local: torch.Tensor,
+    ignore_index: int,
+    n_global: int,
+    quantize: Optional[Callable[[torch.Tensor, torch.Tensor], None]] = None,
+    group=None,
+) -> ShardResult:
+    """One row-sharded step.
+
+    compute(n_global) -> (scalars[4], grad_student_hidden, grad_weight) runs
+    the local rows with the global denominator. quantize(grad_w_slice,
+    labels_shifted) applies the INT8 round trip to the reduced slice, with
+    labels shifted so the slice's first row is 0.
+    """
+    scalars, gsh, gw = compute(n_global)
+    dist.all_reduce(scalars, group=group)
+    sl = reduce_grad_weight(gw, group)
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    v0, v1 = vocab_slice(gw.shape[0], world, rank)
+    if quantize is not None:
+        gathered = [torch.empty_like(labels_local) for _ in range(world)]
+        dist.all_gather(gathered, labels_local, group=group)
+        labels_all = torch.cat(gathered)
+        shifted = torch.where(labels_all == ignore_index, torch.full_like(labels_all, -1), labels_all - v0)
+        quantize(sl, shifted)
+    return ShardResult(scalars=scalars, grad_student_hidden=gsh, grad_weight_slice=sl, vocab_range=(v0, v1))

@@ -1,0 +1,335 @@
+"""Parity of the B200 path with the CPU oracle (the reference's CPU path
+restated), through the C ABI, on the same seeded inputs.
+
+Inputs are rounded to bf16 first (the tensor-core operand type) and the same
+values are given to both sides as f32.
+
+Stated tolerances:
+  * loss and the three components: |gpu - ref| <= 1e-4 * |ref| + 1e-6
+  * gradients: relative L2 error <= 1e-2 (the logit gradients are bf16
+    operands of the backward GEMMs); max-abs error is reported on failure
+  * INT8 grad_W quantisation: bit-exact on the same fp32 grad_W.
+"""
+from __future__ import annotations
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import bf16_round, rel_l2
+
+pytestmark = pytest.mark.gpu
+
+LOSS_RTOL = 1e-4
+LOSS_ATOL = 1e-6
+GRAD_REL_L2 = 1e-2
+NT = os.cpu_count() or 1
+
+
+def assert_parity(gpu, ref, what=""):
+    for name in ("loss", "student_ce", "teacher_ce", "kl"):
+        a, b = getattr(gpu, name), getattr(ref, name)
+        assert abs(a - b) <= LOSS_RTOL * abs(b) + LOSS_ATOL, f"{what} {name}: gpu {a!r} ref {b!r}"
+    for name in ("grad_student_hidden", "grad_weight", "grad_teacher_hidden", "grad_teacher_weight"):
+        a, b = getattr(gpu, name), getattr(ref, name)
+        assert (a is None) == (b is None), f"{what} {name} presence differs"
+        if a is None:
+            continue
+        assert a.shape() == b.shape()
+        e = rel_l2(a.a, b.a)
+        mx = float(np.max(np.abs(a.a.astype(np.float64) - b.a))) if a.a.size else 0.0
+        assert e <= GRAD_REL_L2, f"{what} {name}: rel L2 {e:.3e} (max abs {mx:.3e})"
+    assert gpu.chunk_plan == ref.chunk_plan
+
+
+def lcg_mat(ob, oracle, rows, cols, seed, scale):
+    return ob.Mat.from_array(bf16_round(oracle.lcg_fill(rows * cols, seed, scale).reshape(rows, cols)))
+
+
+def randn_mat(ob, rows, cols, gen, std=1.0):
+    return ob.Mat.from_array(bf16_round((torch.randn(rows, cols, generator=gen) * std).numpy()))
+
+
+# --------------------------------------------------------- small exact cases
+
+def test_tied_small_matches_oracle(ob, oracle):
+    """Shapes and options of tests/end_to_end.rs:89-128 (Tied, smoothing,
+    ignored rows, teacher CE)."""
+    bt, h, v = 6, 5, 7
+    s = lcg_mat(ob, oracle, bt, h, 1, 0.3)
+    w = lcg_mat(ob, oracle, v, h, 2, 0.2)
+    th = lcg_mat(ob, oracle, bt, h, 3, 0.3)
+    labs = oracle.e2e_labels(bt, v, 4, -100)
+    t = ob.Teacher.Tied(th)
+    opts = ob.LossOptions(kd_weight=0.5, temperature=1.5, teacher_ce_weight=1.0, label_smoothing=0.1)
+    assert_parity(ob.distillation_loss(s, w, labs, t, opts), oracle.distillation_loss(s, w, labs, t, opts), "tied")
+
+
+def test_separate_small_matches_oracle(ob, oracle):
+    """tests/end_to_end.rs:130-178 shapes (Separate teacher, H_t != H)."""
+    bt, h, ht, v = 6, 5, 4, 7
+    s = lcg_mat(ob, oracle, bt, h, 11, 0.3)
+    w = lcg_mat(ob, oracle, v, h, 12, 0.2)
+    th = lcg_mat(ob, oracle, bt, ht, 13, 0.3)
+    tw = lcg_mat(ob, oracle, v, ht, 14, 0.2)
+    labs = oracle.e2e_labels(bt, v, None, -100)
+    t = ob.Teacher.Separate(th, tw)
+    opts = ob.LossOptions(kd_weight=0.5, temperature=1.5, teacher_ce_weight=0.7)
+    assert_parity(ob.distillation_loss(s, w, labs, t, opts), oracle.distillation_loss(s, w, labs, t, opts), "sep")
+
+
+def test_precomputed_small_matches_oracle(ob, oracle):
+    """tests/end_to_end.rs:180-204 shapes; also with a teacher CE weight
+    (reported, no teacher gradient)."""
+    bt, h, v = 6, 5, 7
+    s = lcg_mat(ob, oracle, bt, h, 21, 0.3)
+    w = lcg_mat(ob, oracle, v, h, 22, 0.2)
+    tl = ob.Mat.from_array(oracle.lcg_fill(bt * v, 23, 0.5).reshape(bt, v))
+    labs = oracle.e2e_labels(bt, v, 5, -100)
+    t = ob.Teacher.Precomputed(tl)
+    for opts in (ob.LossOptions(kd_weight=0.5, temperature=1.5),
+                 ob.LossOptions(kd_weight=0.5, temperature=1.5, teacher_ce_weight=0.3, label_smoothing=0.2)):
+        g = ob.distillation_loss(s, w, labs, t, opts)
+        assert g.grad_teacher_hidden is None and g.grad_teacher_weight is None
+        assert_parity(g, oracle.distillation_loss(s, w, labs, t, opts), "pre")
+
+
+def test_pure_student_ce(ob, oracle):
+    """tests/end_to_end.rs:206-228: kd = 0, w_t = 0."""
+    bt, h, v = 8, 4, 6
+    s = lcg_mat(ob, oracle, bt, h, 31, 0.3)
+    w = lcg_mat(ob, oracle, v, h, 32, 0.2)
+    labs = oracle.e2e_labels(bt, v, None, -100)
+    t = ob.Teacher.Tied(ob.Mat.zeros(bt, h))
+    opts = ob.LossOptions(kd_weight=0.0, teacher_ce_weight=0.0)
+    g = ob.distillation_loss(s, w, labs, t, opts)
+    assert g.teacher_ce == 0.0 and g.kl == 0.0
+    assert_parity(g, oracle.distillation_loss(s, w, labs, t, opts), "ce")
+
+
+def test_all_rows_ignored(ob, oracle):
+    """Every label equals ignore_index: zero loss and zero gradients, mean
+    denominator clamped to 1 (src/api.rs:225-230)."""
+    bt, h, v = 5, 16, 40
+    gen = torch.Generator().manual_seed(3)
+    s, w, th = randn_mat(ob, bt, h, gen), randn_mat(ob, v, h, gen, 0.1), randn_mat(ob, bt, h, gen)
+    labs = [-100] * bt
+    t = ob.Teacher.Tied(th)
+    opts = ob.LossOptions(kd_weight=0.4, temperature=1.5)
+    g = ob.distillation_loss(s, w, labs, t, opts)
+    assert g.loss == 0.0 and g.kl == 0.0
+    assert np.all(g.grad_weight.a == 0.0) and np.all(g.grad_student_hidden.a == 0.0)
+    assert_parity(g, oracle.distillation_loss(s, w, labs, t, opts), "ignored")
+
+
+# ----------------------------------------------------------------- c1 config
+
+@pytest.fixture(scope="module")
+def c1(ob):
+    """Tied, BT=256, H=512, V=8192, h_t = h_s + N(0,0.1),
+    W ~ N(0, 0.02), labels uniform, kd=0.4, T=1.5, fixed seed."""
+    gen = torch.Generator().manual_seed(20261201)
+    bt, h, v = 256, 512, 8192
+    hs = torch.randn(bt, h, generator=gen)
+    ht = hs + 0.1 * torch.randn(bt, h, generator=gen)
+    w = 0.02 * torch.randn(v, h, generator=gen)
+    labs = torch.randint(0, v, (bt,), generator=gen).tolist()
+    return (ob.Mat.from_array(bf16_round(hs.numpy())), ob.Mat.from_array(bf16_round(w.numpy())), labs,
+            ob.Teacher.Tied(ob.Mat.from_array(bf16_round(ht.numpy()))))
+
+
+@pytest.mark.parametrize("chunk", [None, 64])
+def test_c1_matches_oracle(ob, oracle, c1, chunk):
+    s, w, labs, t = c1
+    cs = ob.ChunkSize.Auto() if chunk is None else ob.ChunkSize.Fixed(chunk)
+    opts = ob.LossOptions(kd_weight=0.4, temperature=1.5, chunk_size=cs)
+    g = ob.distillation_loss(s, w, labs, t, opts)
+    r = oracle.distillation_loss(s, w, labs, t, opts, nthreads=NT)
+    assert_parity(g, r, f"c1 chunk={chunk}")
+    assert g.chunk_plan == (ob.ChunkPlan(256, 1) if chunk is None else ob.ChunkPlan(64, 4))
+
+
+def test_c1_chunk_invariance_on_gpu(ob, c1):
+    """tests/end_to_end.rs:230-278 on the GPU: single chunk vs 4 chunks vs 256
+    chunks give identical results (the backward GEMMs run once per group)."""
+    s, w, labs, t = c1
+    outs = [ob.distillation_loss(s, w, labs, t, ob.LossOptions(kd_weight=0.4, temperature=1.5,
+                                                               chunk_size=ob.ChunkSize.Fixed(c)))
+            for c in (256, 64, 1)]
+    for o in outs[1:]:
+        assert abs(o.loss - outs[0].loss) <= 1e-6 * abs(outs[0].loss)
+        assert rel_l2(o.grad_weight.a, outs[0].grad_weight.a) < 1e-6
+        assert rel_l2(o.grad_student_hidden.a, outs[0].grad_student_hidden.a) < 1e-6
+
+
+def test_c1_sum_is_mean_times_count(ob, c1):
+    """tests/end_to_end.rs:313-358 on the GPU."""
+    s, w, labs, t = c1
+    labs = [(-100 if i % 4 == 0 else y) for i, y in enumerate(labs)]
+    n_valid = sum(1 for y in labs if y != -100)
+    mean = ob.distillation_loss(s, w, labs, t, ob.LossOptions(kd_weight=0.4, temperature=1.5))
+    summ = ob.distillation_loss(s, w, labs, t, ob.LossOptions(kd_weight=0.4, temperature=1.5,
+                                                              reduction=ob.Reduction.Sum))
+    assert abs(summ.loss - mean.loss * n_valid) <= 1e-5 * abs(summ.loss)
+    assert rel_l2(summ.grad_weight.a, mean.grad_weight.a * n_valid) < 1e-5
+
+
+def test_c1_device_entry_matches_host_entry(ob, c1):
+    """The timed device entry and the reference-facing host entry agree."""
+    from orda_b200.device import DeviceContext, distillation_loss_device
+
+    s, w, labs, t = c1
+    opts = ob.LossOptions(kd_weight=0.4, temperature=1.5)
+    host = ob.distillation_loss(s, w, labs, t, opts)
+    with DeviceContext(0) as ctx:
+        d = distillation_loss_device(
+            ctx, torch.from_numpy(s.a).cuda().bfloat16(), torch.from_numpy(w.a).cuda().bfloat16(),
+            torch.tensor(labs, dtype=torch.int64, device="cuda"), ob.TeacherMode.Tied,
+            teacher_hidden=torch.from_numpy(t.hidden.a).cuda().bfloat16(), opts=opts)
+        torch.cuda.synchronize()
+        ctx.check()
+        sc = d.scalars.cpu().numpy()
+    assert np.allclose(sc, [host.loss, host.student_ce, host.teacher_ce, host.kl], rtol=1e-6, atol=0)
+    assert rel_l2(d.grad_weight.cpu().numpy(), host.grad_weight.a) < 1e-6
+    assert rel_l2(d.grad_student_hidden.cpu().numpy(), host.grad_student_hidden.a) < 1e-6
+    assert rel_l2(d.grad_teacher_hidden.cpu().numpy(), host.grad_teacher_hidden.a) < 1e-6
+
+
+def test_oom_ladder_on_device(ob, c1):
+    """An injected workspace-allocation failure moves the device entry to the
+    next rung of the chunk-doubling schedule; results are unchanged."""
+    from orda_b200.device import DeviceContext, distillation_loss_device
+
+    s, w, labs, t = c1
+    opts = ob.LossOptions(kd_weight=0.4, temperature=1.5)
+    args = (torch.from_numpy(s.a).cuda().bfloat16(), torch.from_numpy(w.a).cuda().bfloat16(),
+            torch.tensor(labs, dtype=torch.int64, device="cuda"), ob.TeacherMode.Tied)
+    kw = dict(teacher_hidden=torch.from_numpy(t.hidden.a).cuda().bfloat16(), opts=opts)
+    with DeviceContext(0) as ctx:
+        a = distillation_loss_device(ctx, *args, **kw)
+        torch.cuda.synchronize()
+        ctx.inject_alloc_failures(1)
+        b = distillation_loss_device(ctx, *args, **kw)
+        torch.cuda.synchronize()
+        ctx.check()
+        ctx.inject_alloc_failures(10)
+        with pytest.raises(ob.OrdaError, match="OOM ladder"):
+            distillation_loss_device(ctx, *args, **kw)
+        ctx.inject_alloc_failures(0)
+    assert a.chunk_plan == ob.ChunkPlan(256, 1)
+    assert b.chunk_plan == ob.ChunkPlan(128, 2)
+    assert torch.allclose(a.scalars, b.scalars, rtol=1e-6, atol=0)
+    assert rel_l2(b.grad_weight.cpu().numpy(), a.grad_weight.cpu().numpy()) < 1e-6
+
+
+def test_device_label_range_error(ob):
+    """Out-of-range labels on the device entry are reported by the device
+    label check (no out-of-bounds access; the rows are skipped)."""
+    from orda_b200.device import DeviceContext, distillation_loss_device
+
+    bt, h, v = 16, 64, 256
+    gen = torch.Generator(device="cuda").manual_seed(1)
+    hs = torch.randn(bt, h, generator=gen, device="cuda").bfloat16()
+    w = (0.02 * torch.randn(v, h, generator=gen, device="cuda")).bfloat16()
+    labs = torch.randint(0, v, (bt,), generator=gen, device="cuda")
+    labs[3] = v + 5
+    with DeviceContext(0) as ctx:
+        distillation_loss_device(ctx, hs, w, labs, ob.TeacherMode.Tied, teacher_hidden=hs,
+                                 opts=ob.LossOptions(kd_weight=0.4))
+        torch.cuda.synchronize()
+        with pytest.raises(ob.OrdaError, match="out of range"):
+            ctx.check()
+
+
+# ------------------------------------------------------- BASELINE subsets
+
+def _subset_case(ob, cfg, rows, gen):
+    if cfg == "c2":
+        bt, h, v = rows, 4096, 32000
+        hs = torch.randn(bt, h, generator=gen)
+        ht = hs + 0.1 * torch.randn(bt, h, generator=gen)
+        w = 0.02 * torch.randn(v, h, generator=gen)
+        labs = torch.randint(0, v, (bt,), generator=gen).tolist()
+        t = ob.Teacher.Tied(ob.Mat.from_array(bf16_round(ht.numpy())))
+        opts = ob.LossOptions(kd_weight=0.4, temperature=1.5)
+        return ob.Mat.from_array(bf16_round(hs.numpy())), ob.Mat.from_array(bf16_round(w.numpy())), labs, t, opts
+    if cfg == "c3":
+        bt, hs_d, ht_d, v = rows, 2048, 4096, 128256
+        hs = torch.randn(bt, hs_d, generator=gen)
+        ht = torch.randn(bt, ht_d, generator=gen)
+        ws = 0.02 * torch.randn(v, hs_d, generator=gen)
+        wt = 0.02 * torch.randn(v, ht_d, generator=gen)
+        labs = torch.randint(0, v, (bt,), generator=gen)
+        labs[torch.rand(bt, generator=gen) < 0.05] = -100
+        t = ob.Teacher.Separate(ob.Mat.from_array(bf16_round(ht.numpy())), ob.Mat.from_array(bf16_round(wt.numpy())))
+        opts = ob.LossOptions(kd_weight=0.5, temperature=2.0, label_smoothing=0.1)
+        return (ob.Mat.from_array(bf16_round(hs.numpy())), ob.Mat.from_array(bf16_round(ws.numpy())),
+                labs.tolist(), t, opts)
+    if cfg == "c4":
+        bt, h, v = rows, 4096, 131072
+        hs = torch.randn(bt, h, generator=gen)
+        w = 0.02 * torch.randn(v, h, generator=gen)
+        tl = np.sqrt(2.0) * torch.randn(bt, v, generator=gen)
+        labs = torch.randint(0, v, (bt,), generator=gen).tolist()
+        t = ob.Teacher.Precomputed(ob.Mat.from_array(bf16_round(tl.numpy())))
+        opts = ob.LossOptions(kd_weight=0.4, temperature=1.5, config=ob.KernelConfig(quantize_grad_weight=True))
+        return ob.Mat.from_array(bf16_round(hs.numpy())), ob.Mat.from_array(bf16_round(w.numpy())), labs, t, opts
+    raise ValueError(cfg)
+
+
+@pytest.mark.parametrize("cfg,rows", [("c2", 64), ("c3", 16), ("c4", 16)])
+def test_baseline_config_row_subsets_match_oracle(ob, oracle, cfg, rows):
+    """Full H and V of BASELINE configs c2-c4 on a row subset the oracle can
+    finish in seconds (c4 includes the INT8 grad_W round trip)."""
+    gen = torch.Generator().manual_seed(7 + rows)
+    s, w, labs, t, opts = _subset_case(ob, cfg, rows, gen)
+    g = ob.distillation_loss(s, w, labs, t, opts)
+    r = oracle.distillation_loss(s, w, labs, t, opts, nthreads=NT)
+    assert_parity(g, r, cfg)
+
+
+# ------------------------------------------------------------ INT8 parity
+
+@pytest.mark.parametrize("stochastic", [False, True])
+def test_quantizer_bit_exact_on_same_grad_w(ob, oracle, stochastic):
+    """`quantize_grad_w` + `dequantize_grad_w` (src/quant.rs:157-202) on the
+    GPU vs the oracle on the same fp32 grad_W: q, scales and the dequantised
+    matrix are bit-identical."""
+    from orda_b200.device import DeviceContext, quantize_grad_w
+
+    gen = torch.Generator().manual_seed(11)
+    v, h = 1000, 515
+    gw = (torch.randn(v, h, generator=gen) * torch.rand(v, 1, generator=gen) ** 3 * 1e-3).numpy()
+    gw[7, :] = 0.0  # amax = 0 -> scale from the 1e-12 floor
+    gw[9, 3] = 2.5e-3  # exact .5 ties after scaling are handled by rint
+    labels = torch.randint(0, v, (300,), generator=gen)
+    labels[::7] = -100
+    q_ref, s_ref, deq_ref = oracle.quantize_grad_w(gw, labels.numpy(), -100, stochastic=stochastic, seed=12345)
+    with DeviceContext(0) as ctx:
+        g = torch.from_numpy(gw).cuda()
+        q = torch.empty(v, h, dtype=torch.int8, device="cuda")
+        sc = torch.empty(v, device="cuda")
+        quantize_grad_w(ctx, g, labels.cuda(), -100, stochastic, 12345, q, sc)
+        torch.cuda.synchronize()
+        ctx.check()
+    assert np.array_equal(q.cpu().numpy(), q_ref)
+    assert np.array_equal(sc.cpu().numpy().view(np.uint32), s_ref.view(np.uint32))
+    assert np.array_equal(g.cpu().numpy().view(np.uint32), deq_ref.view(np.uint32))
+
+
+def test_end_to_end_int8_close_but_lossy(ob, oracle, c1):
+    """tests/end_to_end.rs:360-417 on the GPU: the loss is unchanged by the
+    INT8 round trip, grad_W changes slightly."""
+    s, w, labs, t = c1
+    exact = ob.distillation_loss(s, w, labs, t, ob.LossOptions(kd_weight=0.4, temperature=1.5))
+    quant = ob.distillation_loss(s, w, labs, t, ob.LossOptions(
+        kd_weight=0.4, temperature=1.5, config=ob.KernelConfig(quantize_grad_weight=True)))
+    assert abs(exact.loss - quant.loss) < 1e-6
+    d = np.abs(exact.grad_weight.a - quant.grad_weight.a)
+    assert 0.0 < d.max() < 0.05
+    # the GPU quantiser applied to the GPU's own fp32 grad_W equals the oracle
+    # quantiser on that same matrix
+    _q, _s, deq = oracle.quantize_grad_w(exact.grad_weight.a, labs, -100)
+    assert np.array_equal(deq.view(np.uint32), quant.grad_weight.a.view(np.uint32))
