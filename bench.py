@@ -80,7 +80,7 @@ class ClockSampler:
         try:
             self.f = tempfile.TemporaryFile(mode="w+")
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "50",
                  "-i", self.gpu_id], stdout=self.f, stderr=subprocess.DEVNULL)
         except (FileNotFoundError, OSError):
             self.proc = None
@@ -223,7 +223,7 @@ def run_ours(args):
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
 
-    bt, h, v = CFG["bt"], CFG["h"], CFG["v"]
+    bt, h, v = args.rows, CFG["h"], CFG["v"]
     gen = torch.Generator(device=dev).manual_seed(1000 + rank)
     wgen = torch.Generator(device=dev).manual_seed(7)
     hs = torch.randn(bt, h, generator=gen, device=dev).bfloat16()
@@ -320,7 +320,8 @@ def run_ours(args):
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "global_batch": tokens, "seq_len": None, "rows_per_gpu": bt,
+        "config": {"workload": WORKLOAD if bt == CFG["bt"] else f"{WORKLOAD} [profiling size: {bt} rows]",
+                   "global_batch": tokens, "seq_len": None, "rows_per_gpu": bt,
                    "parallelism": "rows sharded, grad_W reduce-scatter" if world > 1 else "single GPU",
                    "l2": "inputs larger than L2 (W 1 GiB, teacher logits 2 GiB per GPU); no flush"},
         "step_tflops_per_gpu": step_tflops, "step_frac_of_peak": step_tflops / peak,
@@ -394,7 +395,7 @@ def e2e_measure(args, ob, hs, w, tl, labels, opts, rank, world, dist):
         tt = torch.tensor([per], device="cuda", dtype=torch.float64)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         per = float(tt.item())
-    bt, h, v = CFG["bt"], CFG["h"], CFG["v"]
+    bt, h, v = hs.shape[0], CFG["h"], CFG["v"]
     h2d = bt * h * 4 + v * h * 4 + bt * v * 4 + bt * 8
     d2h = bt * h * 4 + v * h * 4 + 16
     return {"value": bt * world / per, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
@@ -405,10 +406,12 @@ def e2e_measure(args, ob, hs, w, tl, labels, opts, rank, world, dist):
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--e2e-steps", type=int, default=2)
+    ap.add_argument("--rows", type=int, default=CFG["bt"],
+                    help="rows per GPU (default 8192, the metric's config; smaller values are for profiling only)")
     ap.add_argument("--cpu-rows", type=int, default=3)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")

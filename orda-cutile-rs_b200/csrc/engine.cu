@@ -86,7 +86,7 @@ struct Flags {
 
 struct WsLayout {
   size_t logits = 0, rec_own = 0, rec_own_t = 0, rec_pair = 0, dlog_s = 0, dlog_t = 0, nll_s = 0, nll_t = 0,
-         kl = 0, flags = 0, total = 0;
+         kl = 0, flags = 0, row_const = 0, total = 0;
   size_t ldv = 0, ldd = 0, parts = 0, cs = 0, group_rows = 0;
 };
 
@@ -113,6 +113,7 @@ WsLayout make_layout(const DevInputs& in, const Flags& f, size_t cs, size_t grou
   L.nll_t = take(in.bt * sizeof(float));
   L.kl = take(in.bt * sizeof(double));
   L.flags = take(f.quant ? in.v : 0);
+  L.row_const = take(cs * kRowConstBytes);
   L.total = off;
   return L;
 }
@@ -280,6 +281,7 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
   float* nll_s = reinterpret_cast<float*>(ws + L.nll_s);
   float* nll_t = reinterpret_cast<float*>(ws + L.nll_t);
   double* kl_rows = reinterpret_cast<double*>(ws + L.kl);
+  void* row_const = ws + L.row_const;
   uint8_t* tflags = f.quant ? ws + L.flags : nullptr;
   int* status = ctx->d_words;
 
@@ -374,7 +376,7 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
       // ---- row pass: losses and logit gradients
       {
         Phase ph_rows(ctx, 1, st);
-        ph_rows.launched();
+        ph_rows.launched(kRowLaunches);
         RowArgs r{};
         r.n = static_cast<int>(n);
         r.v = static_cast<int>(v);
@@ -412,6 +414,7 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
         r.nll_s_rows = nll_s + s;
         r.nll_t_rows = nll_t + s;
         r.kl_rows = kl_rows + s;
+        r.row_const = row_const;
         launch_rows(r, st);
         if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(e, "row kernel", err, len);
       }

@@ -91,7 +91,12 @@ struct RowArgs {
   float* nll_s_rows;      // [n]
   float* nll_t_rows;      // [n]
   double* kl_rows;        // [n] (KL * T^2, ignored -> 0)
+  void* row_const;        // [n] x 32 B scratch: per-row constants (stats -> gradient kernel)
 };
+// Two launches: the per-row statistics kernel and the elementwise gradient
+// kernel.
+constexpr int kRowLaunches = 2;
+constexpr size_t kRowConstBytes = 32;
 void launch_rows(const RowArgs& a, cudaStream_t stream);
 
 // Label pass: counts non-ignored labels, checks the range [0, v), marks

@@ -86,183 +86,206 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
   return static_cast<uint32_t>(__bfloat16_as_ushort(ha)) | (static_cast<uint32_t>(__bfloat16_as_ushort(hb)) << 16);
 }
 
+// Per-row constants handed from the statistics kernel to the gradient
+// kernel (lse terms pre-multiplied by log2(e) for exp2).
 struct RowConst {
-  float c_s1, c_sT, c_tT, c_t1;  // lse * log2(e) terms
-  float ws, wt, kdT, eps, one_minus_a;
+  float c_s1, c_sT, c_tT, c_t1;
   int y;
   int ignored;
+  int pad0, pad1;
 };
 
-__global__ void __launch_bounds__(ROW_THREADS) rows_kernel(const RowArgs a) {
+// ---- kernel 1: merge the records of one row, evaluate its losses, write
+// its constants. One CTA per row.
+__global__ void __launch_bounds__(ROW_THREADS) row_stats_kernel(const RowArgs a) {
   __shared__ Acc sh[ROW_THREADS / 32];
-  __shared__ RowConst rc;
   const int i = blockIdx.x;
   const int P = a.n_parts;
   const double inv_t = static_cast<double>(a.inv_t);
+  const bool want_pair = a.need_kl || (a.teacher_ce && !a.teacher_ce_from_own);
+  const bool want_tow = a.teacher_ce && a.teacher_ce_from_own;
 
-  // ---- 1. merge the statistics records of this row
   Acc own = acc_empty(), pr = acc_empty(), tow = acc_empty();
   for (int p = threadIdx.x; p < P; p += blockDim.x) {
     own = acc_merge(own, load_own(a.rec_own, static_cast<long long>(i) * P + p), inv_t);
-    if (a.need_kl || (a.teacher_ce && !a.teacher_ce_from_own))
-      pr = acc_merge(pr, load_pair(a.rec_pair, static_cast<long long>(i) * P + p), inv_t);
-    if (a.teacher_ce && a.teacher_ce_from_own)
-      tow = acc_merge(tow, load_own(a.rec_own_t, static_cast<long long>(i) * P + p), inv_t);
+    if (want_pair) pr = acc_merge(pr, load_pair(a.rec_pair, static_cast<long long>(i) * P + p), inv_t);
+    if (want_tow) tow = acc_merge(tow, load_own(a.rec_own_t, static_cast<long long>(i) * P + p), inv_t);
   }
   own = block_merge(own, inv_t, sh);
-  if (a.need_kl || (a.teacher_ce && !a.teacher_ce_from_own)) pr = block_merge(pr, inv_t, sh);
-  if (a.teacher_ce && a.teacher_ce_from_own) tow = block_merge(tow, inv_t, sh);
+  if (want_pair) pr = block_merge(pr, inv_t, sh);
+  if (want_tow) tow = block_merge(tow, inv_t, sh);
+  if (threadIdx.x != 0) return;
 
-  // ---- 2. per-row loss terms (double), as the reference defines them
-  if (threadIdx.x == 0) {
-    const int64_t y64 = a.labels[i];
-    int ignored = y64 == a.ignore_index;
-    if (!ignored && (y64 < 0 || y64 >= a.v)) ignored = 1;  // range errors are reported by the label pass
-    const int y = ignored ? 0 : static_cast<int>(y64);
-    const double alpha = static_cast<double>(a.alpha);
-    const double vd = static_cast<double>(a.v);
-    const float* xs = a.logits_s + static_cast<long long>(i) * a.ldl;
-
-    const double lse_s1 = own.m + log(own.d1);
-    double nll_s = 0.0;
-    if (!ignored) {
-      const double x_y = static_cast<double>(xs[y]);
-      nll_s = alpha > 0.0 ? lse_s1 - (1.0 - alpha) * x_y - (alpha / vd) * own.sx : lse_s1 - x_y;
-    }
-    a.nll_s_rows[i] = static_cast<float>(nll_s);
-
-    double lse_sT = 0.0, lse_tT = 0.0;
-    if (a.need_kl) {
-      lse_sT = own.m * inv_t + log(own.dT);
-      lse_tT = pr.m * inv_t + log(pr.dT);
-      // KL = sum p_t (log p_t - log p_s) = S / d_t + lse_s^T - lse_t^T
-      const double kl = pr.s / pr.dT + lse_sT - lse_tT;
-      const double t_sq = static_cast<double>(a.temperature * a.temperature);
-      a.kl_rows[i] = ignored ? 0.0 : kl * t_sq;
-    } else {
-      a.kl_rows[i] = 0.0;
-    }
-
-    double lse_t1 = 0.0;
-    if (a.teacher_ce) {
-      const Acc& ts = a.teacher_ce_from_own ? tow : pr;
-      lse_t1 = ts.m + log(ts.d1);
-      double nll_t = 0.0;
-      if (!ignored) {
-        double t_y;
-        if (a.teacher_is_bf16) {
-          const uint16_t b = static_cast<const uint16_t*>(a.teacher)[static_cast<long long>(i) * a.ld_teacher + y];
-          t_y = static_cast<double>(__uint_as_float(static_cast<uint32_t>(b) << 16));
-        } else {
-          t_y = static_cast<double>(static_cast<const float*>(a.teacher)[static_cast<long long>(i) * a.ld_teacher + y]);
-        }
-        nll_t = alpha > 0.0 ? lse_t1 - (1.0 - alpha) * t_y - (alpha / vd) * ts.sx : lse_t1 - t_y;
-      }
-      a.nll_t_rows[i] = static_cast<float>(nll_t);
-    } else {
-      a.nll_t_rows[i] = 0.0f;
-    }
-
-    rc.c_s1 = static_cast<float>(lse_s1 * static_cast<double>(LOG2E_F));
-    rc.c_sT = static_cast<float>(lse_sT * static_cast<double>(LOG2E_F));
-    rc.c_tT = static_cast<float>(lse_tT * static_cast<double>(LOG2E_F));
-    rc.c_t1 = static_cast<float>(lse_t1 * static_cast<double>(LOG2E_F));
-    rc.ws = a.w_s;
-    rc.wt = a.w_t;
-    rc.kdT = a.need_kl ? a.kd * a.temperature : 0.0f;
-    rc.eps = static_cast<float>(alpha / vd);
-    rc.one_minus_a = static_cast<float>(1.0 - alpha);
-    rc.y = y;
-    rc.ignored = ignored;
-  }
-  __syncthreads();
-
-  // ---- 3. one streaming pass writing the bf16 logit gradients
-  const RowConst c = rc;
+  const int64_t y64 = a.labels[i];
+  int ignored = y64 == a.ignore_index;
+  if (!ignored && (y64 < 0 || y64 >= a.v)) ignored = 1;  // range errors are reported by the label pass
+  const int y = ignored ? 0 : static_cast<int>(y64);
+  const double alpha = static_cast<double>(a.alpha);
+  const double vd = static_cast<double>(a.v);
   const float* xs = a.logits_s + static_cast<long long>(i) * a.ldl;
-  uint16_t* gs = a.dlog_s + static_cast<long long>(i) * a.ldd;
-  uint16_t* gt = a.teacher_grad ? a.dlog_t + static_cast<long long>(i) * a.ldd : nullptr;
-  const bool want_t = a.need_kl || a.teacher_grad;
-  const float l1 = LOG2E_F, lT = LOG2E_F * a.inv_t;
-  const int V = a.v;
 
-  auto teacher_at = [&](int j) -> float {
-    if (a.teacher_is_bf16) {
-      const uint16_t b = static_cast<const uint16_t*>(a.teacher)[static_cast<long long>(i) * a.ld_teacher + j];
-      return __uint_as_float(static_cast<uint32_t>(b) << 16);
-    }
-    return static_cast<const float*>(a.teacher)[static_cast<long long>(i) * a.ld_teacher + j];
-  };
+  const double lse_s1 = own.m + log(own.d1);
+  double nll_s = 0.0;
+  if (!ignored) {
+    const double x_y = static_cast<double>(xs[y]);
+    nll_s = alpha > 0.0 ? lse_s1 - (1.0 - alpha) * x_y - (alpha / vd) * own.sx : lse_s1 - x_y;
+  }
+  a.nll_s_rows[i] = static_cast<float>(nll_s);
 
-  auto grads = [&](int j, float x, float t, float& g_s, float& g_t) {
-    float g = c.ws * (exp2f(fmaf(x, l1, -c.c_s1)) - c.eps);
-    if (c.kdT != 0.0f) g += c.kdT * (exp2f(fmaf(x, lT, -c.c_sT)) - exp2f(fmaf(t, lT, -c.c_tT)));
-    if (j == c.y) g -= c.ws * c.one_minus_a;
-    float h = 0.0f;
-    if (gt) {
-      h = c.wt * (exp2f(fmaf(t, l1, -c.c_t1)) - c.eps);
-      if (j == c.y) h -= c.wt * c.one_minus_a;
-    }
-    if (c.ignored) {
-      g = 0.0f;
-      h = 0.0f;
-    }
-    g_s = g;
-    g_t = h;
-  };
+  double lse_sT = 0.0, lse_tT = 0.0;
+  if (a.need_kl) {
+    lse_sT = own.m * inv_t + log(own.dT);
+    lse_tT = pr.m * inv_t + log(pr.dT);
+    // KL = sum p_t (log p_t - log p_s) = S / d_t + lse_s^T - lse_t^T
+    const double kl = pr.s / pr.dT + lse_sT - lse_tT;
+    const double t_sq = static_cast<double>(a.temperature * a.temperature);
+    a.kl_rows[i] = ignored ? 0.0 : kl * t_sq;
+  } else {
+    a.kl_rows[i] = 0.0;
+  }
 
-  const int vec_end = (V / 8) * 8;
-  for (int j0 = threadIdx.x * 8; j0 < vec_end; j0 += blockDim.x * 8) {
-    const float4 x0 = *reinterpret_cast<const float4*>(xs + j0);
-    const float4 x1 = *reinterpret_cast<const float4*>(xs + j0 + 4);
-    const float x[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-    float t[8];
-    if (want_t) {
+  double lse_t1 = 0.0;
+  if (a.teacher_ce) {
+    const Acc& ts = a.teacher_ce_from_own ? tow : pr;
+    lse_t1 = ts.m + log(ts.d1);
+    double nll_t = 0.0;
+    if (!ignored) {
+      double t_y;
       if (a.teacher_is_bf16) {
-        const uint4 q = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.teacher) +
-                                                        static_cast<long long>(i) * a.ld_teacher + j0);
-        t[0] = __uint_as_float(q.x << 16);
-        t[1] = __uint_as_float(q.x & 0xFFFF0000u);
-        t[2] = __uint_as_float(q.y << 16);
-        t[3] = __uint_as_float(q.y & 0xFFFF0000u);
-        t[4] = __uint_as_float(q.z << 16);
-        t[5] = __uint_as_float(q.z & 0xFFFF0000u);
-        t[6] = __uint_as_float(q.w << 16);
-        t[7] = __uint_as_float(q.w & 0xFFFF0000u);
+        const uint16_t b = static_cast<const uint16_t*>(a.teacher)[static_cast<long long>(i) * a.ld_teacher + y];
+        t_y = static_cast<double>(__uint_as_float(static_cast<uint32_t>(b) << 16));
       } else {
-        const float* tp = static_cast<const float*>(a.teacher) + static_cast<long long>(i) * a.ld_teacher + j0;
-        const float4 t0 = *reinterpret_cast<const float4*>(tp);
-        const float4 t1 = *reinterpret_cast<const float4*>(tp + 4);
-        t[0] = t0.x; t[1] = t0.y; t[2] = t0.z; t[3] = t0.w;
-        t[4] = t1.x; t[5] = t1.y; t[6] = t1.z; t[7] = t1.w;
+        t_y = static_cast<double>(static_cast<const float*>(a.teacher)[static_cast<long long>(i) * a.ld_teacher + y]);
       }
-    } else {
-#pragma unroll
-      for (int k = 0; k < 8; ++k) t[k] = 0.0f;
+      nll_t = alpha > 0.0 ? lse_t1 - (1.0 - alpha) * t_y - (alpha / vd) * ts.sx : lse_t1 - t_y;
     }
-    float gsv[8], gtv[8];
+    a.nll_t_rows[i] = static_cast<float>(nll_t);
+  } else {
+    a.nll_t_rows[i] = 0.0f;
+  }
+
+  RowConst rc;
+  rc.c_s1 = static_cast<float>(lse_s1 * static_cast<double>(LOG2E_F));
+  rc.c_sT = static_cast<float>(lse_sT * static_cast<double>(LOG2E_F));
+  rc.c_tT = static_cast<float>(lse_tT * static_cast<double>(LOG2E_F));
+  rc.c_t1 = static_cast<float>(lse_t1 * static_cast<double>(LOG2E_F));
+  rc.y = y;
+  rc.ignored = ignored;
+  rc.pad0 = rc.pad1 = 0;
+  reinterpret_cast<RowConst*>(a.row_const)[i] = rc;
+}
+
+// Scalars shared by every element of the gradient pass.
+struct GradScalars {
+  float ws, wt, kdT, eps, ws_tgt, wt_tgt, l1, lT;
+};
+
+__device__ __forceinline__ void grad_elem(const GradScalars& g, const RowConst& c, bool want_kl, bool want_t,
+                                          int j, float x, float t, float& gs, float& gt) {
+  float s = g.ws * (exp2f(fmaf(x, g.l1, -c.c_s1)) - g.eps);
+  if (want_kl) s += g.kdT * (exp2f(fmaf(x, g.lT, -c.c_sT)) - exp2f(fmaf(t, g.lT, -c.c_tT)));
+  if (j == c.y) s -= g.ws_tgt;
+  float u = 0.0f;
+  if (want_t) {
+    u = g.wt * (exp2f(fmaf(t, g.l1, -c.c_t1)) - g.eps);
+    if (j == c.y) u -= g.wt_tgt;
+  }
+  if (c.ignored) {
+    s = 0.0f;
+    u = 0.0f;
+  }
+  gs = s;
+  gt = u;
+}
+
+__device__ __forceinline__ void load_teacher8(const RowArgs& a, long long row, int j0, float (&t)[8]) {
+  if (a.teacher_is_bf16) {
+    const uint4 q = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.teacher) +
+                                                         row * a.ld_teacher + j0));
+    t[0] = __uint_as_float(q.x << 16);
+    t[1] = __uint_as_float(q.x & 0xFFFF0000u);
+    t[2] = __uint_as_float(q.y << 16);
+    t[3] = __uint_as_float(q.y & 0xFFFF0000u);
+    t[4] = __uint_as_float(q.z << 16);
+    t[5] = __uint_as_float(q.z & 0xFFFF0000u);
+    t[6] = __uint_as_float(q.w << 16);
+    t[7] = __uint_as_float(q.w & 0xFFFF0000u);
+  } else {
+    const float* tp = static_cast<const float*>(a.teacher) + row * a.ld_teacher + j0;
+    const float4 t0 = __ldg(reinterpret_cast<const float4*>(tp));
+    const float4 t1 = __ldg(reinterpret_cast<const float4*>(tp + 4));
+    t[0] = t0.x; t[1] = t0.y; t[2] = t0.z; t[3] = t0.w;
+    t[4] = t1.x; t[5] = t1.y; t[6] = t1.z; t[7] = t1.w;
+  }
+}
+
+// ---- kernel 2: flat elementwise pass over the chunk's [n, V] logits,
+// 8 columns per thread per step (32 B fp32 student, 16/32 B teacher in;
+// 16 B bf16 gradient out per row kind), grid-stride so every SM stays busy.
+// Requires V % 8 == 0 and 16-byte aligned rows (checked by the launcher).
+__global__ void __launch_bounds__(256) row_grad_kernel_vec(const RowArgs a, const GradScalars g) {
+  const long long vecs_per_row = a.v / 8;
+  const long long total = static_cast<long long>(a.n) * vecs_per_row;
+  const bool want_kl = a.need_kl != 0;
+  const bool want_t = a.teacher_grad != 0;
+  const bool need_teacher = want_kl || want_t;
+  const RowConst* rcs = reinterpret_cast<const RowConst*>(a.row_const);
+  for (long long idx = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long row = idx / vecs_per_row;
+    const int j0 = static_cast<int>(idx - row * vecs_per_row) * 8;
+    const RowConst c = rcs[row];
+    const float* xs = a.logits_s + row * a.ldl + j0;
+    const float4 x0 = __ldg(reinterpret_cast<const float4*>(xs));
+    const float4 x1 = __ldg(reinterpret_cast<const float4*>(xs + 4));
+    const float x[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+    float t[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (need_teacher) load_teacher8(a, row, j0, t);
+    float gs[8], gt[8];
 #pragma unroll
-    for (int k = 0; k < 8; ++k) grads(j0 + k, x[k], t[k], gsv[k], gtv[k]);
+    for (int k = 0; k < 8; ++k) grad_elem(g, c, want_kl, want_t, j0 + k, x[k], t[k], gs[k], gt[k]);
     uint4 o;
-    o.x = pack_bf16x2(gsv[0], gsv[1]);
-    o.y = pack_bf16x2(gsv[2], gsv[3]);
-    o.z = pack_bf16x2(gsv[4], gsv[5]);
-    o.w = pack_bf16x2(gsv[6], gsv[7]);
-    *reinterpret_cast<uint4*>(gs + j0) = o;
-    if (gt) {
-      o.x = pack_bf16x2(gtv[0], gtv[1]);
-      o.y = pack_bf16x2(gtv[2], gtv[3]);
-      o.z = pack_bf16x2(gtv[4], gtv[5]);
-      o.w = pack_bf16x2(gtv[6], gtv[7]);
-      *reinterpret_cast<uint4*>(gt + j0) = o;
+    o.x = pack_bf16x2(gs[0], gs[1]);
+    o.y = pack_bf16x2(gs[2], gs[3]);
+    o.z = pack_bf16x2(gs[4], gs[5]);
+    o.w = pack_bf16x2(gs[6], gs[7]);
+    *reinterpret_cast<uint4*>(a.dlog_s + row * a.ldd + j0) = o;
+    if (want_t) {
+      o.x = pack_bf16x2(gt[0], gt[1]);
+      o.y = pack_bf16x2(gt[2], gt[3]);
+      o.z = pack_bf16x2(gt[4], gt[5]);
+      o.w = pack_bf16x2(gt[6], gt[7]);
+      *reinterpret_cast<uint4*>(a.dlog_t + row * a.ldd + j0) = o;
     }
   }
-  for (int j = vec_end + threadIdx.x; j < V; j += blockDim.x) {
-    const float t = want_t ? teacher_at(j) : 0.0f;
-    float g_s, g_t;
-    grads(j, xs[j], t, g_s, g_t);
-    gs[j] = __bfloat16_as_ushort(__float2bfloat16_rn(g_s));
-    if (gt) gt[j] = __bfloat16_as_ushort(__float2bfloat16_rn(g_t));
+}
+
+// Scalar fallback for vocabularies that are not a multiple of 8.
+__global__ void __launch_bounds__(256) row_grad_kernel_scalar(const RowArgs a, const GradScalars g) {
+  const long long total = static_cast<long long>(a.n) * a.v;
+  const bool want_kl = a.need_kl != 0;
+  const bool want_t = a.teacher_grad != 0;
+  const bool need_teacher = want_kl || want_t;
+  const RowConst* rcs = reinterpret_cast<const RowConst*>(a.row_const);
+  for (long long idx = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long row = idx / a.v;
+    const int j = static_cast<int>(idx - row * a.v);
+    const RowConst c = rcs[row];
+    const float x = a.logits_s[row * a.ldl + j];
+    float t = 0.0f;
+    if (need_teacher) {
+      if (a.teacher_is_bf16) {
+        const uint16_t b = static_cast<const uint16_t*>(a.teacher)[row * a.ld_teacher + j];
+        t = __uint_as_float(static_cast<uint32_t>(b) << 16);
+      } else {
+        t = static_cast<const float*>(a.teacher)[row * a.ld_teacher + j];
+      }
+    }
+    float gs, gt;
+    grad_elem(g, c, want_kl, want_t, j, x, t, gs, gt);
+    a.dlog_s[row * a.ldd + j] = __bfloat16_as_ushort(__float2bfloat16_rn(gs));
+    if (want_t) a.dlog_t[row * a.ldd + j] = __bfloat16_as_ushort(__float2bfloat16_rn(gt));
   }
 }
 
@@ -368,7 +391,31 @@ __global__ void f32_to_bf16_kernel(const float* src, long long rows, long long c
 
 void launch_rows(const RowArgs& a, cudaStream_t stream) {
   if (a.n <= 0) return;
-  rows_kernel<<<a.n, ROW_THREADS, 0, stream>>>(a);
+  row_stats_kernel<<<a.n, ROW_THREADS, 0, stream>>>(a);
+  GradScalars g;
+  g.ws = a.w_s;
+  g.wt = a.w_t;
+  g.kdT = a.need_kl ? a.kd * a.temperature : 0.0f;
+  const double alpha = static_cast<double>(a.alpha);
+  g.eps = static_cast<float>(alpha / static_cast<double>(a.v));
+  const float one_minus_a = static_cast<float>(1.0 - alpha);
+  g.ws_tgt = a.w_s * one_minus_a;
+  g.wt_tgt = a.w_t * one_minus_a;
+  g.l1 = LOG2E_F;
+  g.lT = LOG2E_F * a.inv_t;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const long long tsz = a.teacher_is_bf16 ? 2 : 4;
+  const bool vec = (a.v % 8 == 0) && (a.ldl % 4 == 0) && (a.ldd % 8 == 0) &&
+                   ((a.ld_teacher * tsz) % 16 == 0) && ((reinterpret_cast<uintptr_t>(a.teacher) & 15) == 0) &&
+                   ((reinterpret_cast<uintptr_t>(a.logits_s) & 15) == 0);
+  const long long work = vec ? static_cast<long long>(a.n) * (a.v / 8) : static_cast<long long>(a.n) * a.v;
+  long long blocks = (work + 255) / 256;
+  const long long cap = static_cast<long long>(sms) * 8;
+  if (blocks > cap) blocks = cap;
+  if (vec) row_grad_kernel_vec<<<static_cast<int>(blocks), 256, 0, stream>>>(a, g);
+  else row_grad_kernel_scalar<<<static_cast<int>(blocks), 256, 0, stream>>>(a, g);
 }
 
 void launch_label_prep(const int64_t* labels, long long bt, long long v, int64_t ignore_index, int reduction_sum,
