@@ -292,6 +292,22 @@ ORDA_API int orda_quantize_grad_w_device(OrdaContext* ctx, float* grad_w, size_t
                                 uint64_t seed, int8_t* q, float* scale, void* stream, char* err,
                                 size_t err_len);
 
+/* Allocation-free variant of orda_quantize_grad_w_device. It has no
+ * counterpart in the reference crate. It exists for callers that cannot call
+ * cudaMalloc (allocator hooks, out-of-memory handlers, runtimes that forbid
+ * device allocations after start-up): instead of a context workspace, its
+ * scratch (one flag byte per grad_W row) is a fixed device array inside the
+ * library, ORDA_NOALLOC_MAX_V bytes on every GPU that loads the library.
+ * Same arguments and results as orda_quantize_grad_w_device without the
+ * context; runs on the current device. V above ORDA_NOALLOC_MAX_V is rejected.
+ * All calls on a device share the array: calls that overlap on the GPU race,
+ * so order them. The first call on each device looks up the array's device
+ * address; make it before any CUDA stream capture. */
+#define ORDA_NOALLOC_MAX_V 262144
+ORDA_API int orda_quantize_grad_w_device_noalloc(float* grad_w, size_t v, size_t h, size_t ld, const int64_t* labels,
+                                                 size_t bt, int64_t ignore_index, int stochastic, uint64_t seed,
+                                                 int8_t* q, float* scale, void* stream, char* err, size_t err_len);
+
 /* bf16 tensor-core GEMM used by the chunk loop, exposed for unit tests:
  *   C[M,N] (fp32, ldc) = alpha * op(A) @ op(B) + (beta != 0 ? C : 0)
  * a_kind: 0 = A stored [M,K] (K contiguous), 1 = A stored [K,M] (M contiguous)

@@ -231,6 +231,25 @@ SIGNATURES = {
             C.c_size_t,
         ],
     ),
+    "orda_quantize_grad_w_device_noalloc": (
+        C.c_int,
+        [
+            C.c_void_p,
+            C.c_size_t,
+            C.c_size_t,
+            C.c_size_t,
+            C.c_void_p,
+            C.c_size_t,
+            C.c_int64,
+            C.c_int,
+            C.c_uint64,
+            C.c_void_p,
+            C.c_void_p,
+            C.c_void_p,
+            C.c_char_p,
+            C.c_size_t,
+        ],
+    ),
     "orda_gemm_bf16_device": (
         C.c_int,
         [
