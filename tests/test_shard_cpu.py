@@ -1,0 +1,143 @@
+"""Row-sharded data parallelism (orda_b200/shard.py) with world-size-2 gloo
+ranks on CPU.
+
+Each rank runs the oracle on its block of rows with the global mean
+denominator (what the device entry does with OrdaShardOptions), then the
+shard module's collectives combine the ranks: all-reduce of the scalars,
+reduction of grad_W to each rank's vocabulary slice, label all-gather for the
+INT8 round trip on the slice. The combined result must equal the single-rank
+oracle on the whole batch.
+"""
+from __future__ import annotations
+
+import os
+import socket
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+REPO = Path(__file__).resolve().parent.parent
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _problem():
+    sys.path.insert(0, str(REPO / "orda-cutile-rs_b200"))
+    sys.path.insert(0, str(REPO / "oracle"))
+    import oracle
+    import orda_b200 as ob
+
+    bt, h, v = 12, 8, 16
+    hs = oracle.lcg_fill(bt * h, 5, 0.5).reshape(bt, h)
+    ht = oracle.lcg_fill(bt * h, 6, 0.5).reshape(bt, h)
+    w = oracle.lcg_fill(v * h, 7, 0.4).reshape(v, h)
+    labels = oracle.e2e_labels(bt, v, 5, -100)
+    return bt, h, v, hs, ht, w, labels
+
+
+def _opts(ob, reduction, quant):
+    return ob.LossOptions(kd_weight=0.4, temperature=1.5, teacher_ce_weight=0.5, label_smoothing=0.05,
+                          reduction=reduction, config=ob.KernelConfig(quantize_grad_weight=quant))
+
+
+def _worker(rank, world, port, quant, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    sys.path.insert(0, str(REPO / "orda-cutile-rs_b200"))
+    sys.path.insert(0, str(REPO / "oracle"))
+    import oracle
+    import orda_b200 as ob
+    from orda_b200 import shard
+
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        bt, h, v, hs, ht, w, labels = _problem()
+        r0, r1 = shard.shard_rows(bt, world, rank)
+        lab_local = torch.tensor(labels[r0:r1], dtype=torch.int64)
+        n_global = shard.global_non_ignore(lab_local, -100)
+
+        def compute(n):
+            # local rows, Sum reduction, then the global mean scale (f32), which is
+            # what the device entry applies given global_non_ignore = n
+            out = oracle.distillation_loss(ob.Mat.from_array(hs[r0:r1]), ob.Mat.from_array(w), labels[r0:r1],
+                                           ob.Teacher.Tied(ob.Mat.from_array(ht[r0:r1])),
+                                           _opts(ob, ob.Reduction.Sum, False))
+            ms = np.float32(1.0) / np.float32(max(n, 1))
+            sc = torch.tensor([out.loss, out.student_ce, out.teacher_ce, out.kl], dtype=torch.float32) * float(ms)
+            return (sc, torch.from_numpy(out.grad_student_hidden.a * ms),
+                    torch.from_numpy(np.ascontiguousarray(out.grad_weight.a * ms)))
+
+        def quantize(sl, shifted):
+            _q, _s, deq = oracle.quantize_grad_w(sl.numpy(), shifted.numpy(), -100)
+            sl.copy_(torch.from_numpy(deq))
+
+        res = shard.row_sharded_step(compute, lab_local, -100, n_global, quantize=quantize if quant else None)
+        q.put((rank, res.scalars.numpy(), res.grad_student_hidden.numpy(), res.grad_weight_slice.numpy().copy(),
+               res.vocab_range, (r0, r1)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("quant", [False, True])
+def test_row_sharded_matches_single_rank(quant):
+    import torch.multiprocessing as mp
+
+    sys.path.insert(0, str(REPO / "orda-cutile-rs_b200"))
+    sys.path.insert(0, str(REPO / "oracle"))
+    import oracle
+    import orda_b200 as ob
+
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, quant, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = sorted([q.get(timeout=120) for _ in range(world)], key=lambda x: x[0])
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+
+    bt, h, v, hs, ht, w, labels = _problem()
+    full = oracle.distillation_loss(ob.Mat.from_array(hs), ob.Mat.from_array(w), labels,
+                                    ob.Teacher.Tied(ob.Mat.from_array(ht)), _opts(ob, ob.Reduction.Mean, quant))
+    sc = results[0][1]
+    assert np.allclose(sc, results[1][1])  # all-reduced on every rank
+    ref = np.array([full.loss, full.student_ce, full.teacher_ce, full.kl], np.float32)
+    assert np.allclose(sc, ref, rtol=1e-5, atol=1e-6), (sc, ref)
+    gh = np.concatenate([r[2] for r in results])
+    assert np.allclose(gh, full.grad_student_hidden.a, rtol=1e-5, atol=1e-7)
+    gw = np.concatenate([r[3] for r in results])
+    assert [r[4] for r in results] == [(0, v // 2), (v // 2, v)]
+    if quant:
+        # INT8 round trip on each reduced slice: error bounded by half a
+        # quantisation step of the full-batch result's rows
+        _q, s, _d = oracle.quantize_grad_w(full.grad_weight.a, labels, -100)
+        assert np.all(np.abs(gw - full.grad_weight.a) <= s[:, None] * 0.5 + 1e-6)
+    else:
+        assert np.allclose(gw, full.grad_weight.a, rtol=1e-5, atol=1e-7)
+
+
+def test_shard_rows_and_vocab_slices():
+    sys.path.insert(0, str(REPO / "orda-cutile-rs_b200"))
+    from orda_b200 import shard
+
+    assert [shard.shard_rows(10, 3, r) for r in range(3)] == [(0, 4), (4, 7), (7, 10)]
+    assert [shard.shard_rows(8192 * 8, 8, r) for r in (0, 7)] == [(0, 8192), (57344, 65536)]
+    assert shard.vocab_slice(131072, 8, 3) == (49152, 65536)
+    with pytest.raises(ValueError):
+        shard.vocab_slice(152065, 8, 0)
