@@ -279,8 +279,10 @@ def run_ours(args):
         dist.barrier()
     torch.cuda.synchronize()
     ev0.record(stream)
+    h0 = time.perf_counter()
     for _ in range(args.steps):
         step()
+    host_ms = (time.perf_counter() - h0) * 1e3 / args.steps
     ev1.record(stream)
     torch.cuda.synchronize()
     if world > 1:
@@ -326,6 +328,7 @@ def run_ours(args):
                    "l2": "inputs larger than L2 (W 1 GiB, teacher logits 2 GiB per GPU); no flush"},
         "step_tflops_per_gpu": step_tflops, "step_frac_of_peak": step_tflops / peak,
         "phases_ms_per_step": {k: v_[0] / args.steps for k, v_ in phases.items()},
+        "host_enqueue_ms_per_step": host_ms,
         "roofline": roofline, "gpu_launches": int(launches), "clocks": clocks,
     }
 

@@ -128,7 +128,8 @@ typedef struct OrdaLossOptions {
 } OrdaLossOptions;
 
 /* `DistillationLossOutput` (src/api.rs:71-92). Gradients are allocated by
- * the library and released by orda_output_free(). */
+ * the library (page-locked host memory from a reuse pool) and must be
+ * released with orda_output_free(), never free(). */
 typedef struct OrdaOutput {
   float loss;
   float student_ce;

@@ -24,6 +24,8 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <map>
+#include <unordered_map>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -81,13 +83,13 @@ struct DevInputs {
 
 struct Flags {
   float w_s, w_t, kd, temperature, alpha;
-  bool need_teacher, teacher_rows, teacher_grad, teacher_ce, pair, quant;
+  bool need_teacher, teacher_rows, teacher_grad, teacher_ce, quant;
 };
 
 struct WsLayout {
-  size_t logits = 0, rec_own = 0, rec_own_t = 0, rec_pair = 0, dlog_s = 0, dlog_t = 0, nll_s = 0, nll_t = 0,
-         kl = 0, flags = 0, row_const = 0, total = 0;
-  size_t ldv = 0, ldd = 0, parts = 0, cs = 0, group_rows = 0;
+  size_t logits = 0, rec_own = 0, rec_own_t = 0, dlog_s = 0, dlog_t = 0, nll_s = 0, nll_t = 0, kl_base = 0,
+         s_part = 0, flags = 0, row_const = 0, total = 0;
+  size_t ldv = 0, ldd = 0, parts = 0, parts_t = 0, nseg = 0, cs = 0, group_rows = 0;
 };
 
 WsLayout make_layout(const DevInputs& in, const Flags& f, size_t cs, size_t group_rows) {
@@ -97,6 +99,8 @@ WsLayout make_layout(const DevInputs& in, const Flags& f, size_t cs, size_t grou
   L.ldv = round_up(in.v, 8);
   L.ldd = round_up(in.v, 8);
   L.parts = (in.v + 127) / 128;
+  L.parts_t = f.teacher_rows ? L.parts : 1;  // teacher GEMM records, or one pre-pass record per row
+  L.nseg = f.kd > 0.0f ? (in.v + kGradSegCols - 1) / kGradSegCols : 0;
   size_t off = 0;
   auto take = [&](size_t bytes) {
     const size_t o = off;
@@ -105,13 +109,13 @@ WsLayout make_layout(const DevInputs& in, const Flags& f, size_t cs, size_t grou
   };
   L.logits = take((f.teacher_rows ? 2 : 1) * cs * L.ldv * sizeof(float));
   L.rec_own = take(cs * L.parts * 16);
-  L.rec_own_t = take(f.teacher_rows ? cs * L.parts * 16 : 0);
-  L.rec_pair = take(f.pair ? cs * L.parts * 32 : 0);
+  L.rec_own_t = take(f.need_teacher ? cs * L.parts_t * 16 : 0);
   L.dlog_s = take(group_rows * L.ldd * 2);
   L.dlog_t = take(f.teacher_grad ? group_rows * L.ldd * 2 : 0);
   L.nll_s = take(in.bt * sizeof(float));
   L.nll_t = take(in.bt * sizeof(float));
-  L.kl = take(in.bt * sizeof(double));
+  L.kl_base = take(in.bt * sizeof(double));
+  L.s_part = take(in.bt * L.nseg * sizeof(float));
   L.flags = take(f.quant ? in.v : 0);
   L.row_const = take(cs * kRowConstBytes);
   L.total = off;
@@ -152,6 +156,15 @@ struct AllocTry {
 // that keeps the group within 60% of the memory this call may use.
 int try_alloc_cb(size_t num_chunks, size_t chunk_size, void* user) {
   AllocTry* t = static_cast<AllocTry*>(user);
+  // Fast path (no device query): the held workspace already fits a group of
+  // every chunk.
+  {
+    const WsLayout full = make_layout(*t->in, *t->f, chunk_size, std::min(num_chunks * chunk_size, t->in->bt));
+    if (t->ctx->inject_fail <= 0 && t->ctx->ws_bytes >= full.total) {
+      t->layout = full;
+      return 0;
+    }
+  }
   size_t free_b = 0, total_b = 0;
   cudaMemGetInfo(&free_b, &total_b);
   const size_t avail = free_b + t->ctx->ws_bytes;
@@ -225,7 +238,6 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
   f.teacher_rows = f.need_teacher && live_teacher;
   f.teacher_grad = f.w_t > 0.0f && live_teacher;
   f.teacher_ce = f.w_t > 0.0f;
-  f.pair = f.kd > 0.0f || (f.w_t > 0.0f && in.mode == ORDA_TEACHER_PRECOMPUTED);
   f.quant = o.config.quantize_grad_weight != 0 && !(shard && shard->skip_quantize);
 
   if (!out.grad_student_hidden || !out.grad_weight || !out.scalars) {
@@ -275,14 +287,14 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
   float* logits_t = logits + L.cs * L.ldv;
   float* rec_own = reinterpret_cast<float*>(ws + L.rec_own);
   float* rec_own_t = reinterpret_cast<float*>(ws + L.rec_own_t);
-  float* rec_pair = reinterpret_cast<float*>(ws + L.rec_pair);
   uint16_t* dlog_s = reinterpret_cast<uint16_t*>(ws + L.dlog_s);
   uint16_t* dlog_t = reinterpret_cast<uint16_t*>(ws + L.dlog_t);
   float* nll_s = reinterpret_cast<float*>(ws + L.nll_s);
   float* nll_t = reinterpret_cast<float*>(ws + L.nll_t);
-  double* kl_rows = reinterpret_cast<double*>(ws + L.kl);
-  void* row_const = ws + L.row_const;
+  double* kl_base = reinterpret_cast<double*>(ws + L.kl_base);
+  float* s_part = reinterpret_cast<float*>(ws + L.s_part);
   uint8_t* tflags = f.quant ? ws + L.flags : nullptr;
+  void* row_const = ws + L.row_const;
   int* status = ctx->d_words;
 
   cudaError_t e;
@@ -301,40 +313,43 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
   const char* why = nullptr;
   const size_t cs = used.chunk_size;
   const size_t group_rows = L.group_rows;
+  const size_t t_esz = in.t_logits_bf16 ? 2 : 4;
   for (size_t g0 = 0; g0 < bt; g0 += group_rows) {
     const size_t g1 = std::min(g0 + group_rows, bt);
     for (size_t s = g0; s < g1; s += cs) {
       const size_t n = std::min(cs, g1 - s);
-      std::optional<Phase> ph_fwd;
-      ph_fwd.emplace(ctx, 0, st);
-      // ---- teacher logits (Tied / Separate)
-      if (f.teacher_rows) {
-        ph_fwd->launched();
-        GemmDesc gd;
-        const MatRef& tw = in.mode == ORDA_TEACHER_TIED ? in.w : in.wt;
-        const size_t kdim = in.mode == ORDA_TEACHER_TIED ? h : ht;
-        gd.a[0] = MatRef{static_cast<const uint16_t*>(in.ht.ptr) + s * in.ht.ld, static_cast<long long>(n),
-                         static_cast<long long>(kdim), in.ht.ld};
-        gd.b[0] = tw;
-        gd.k_seg[0] = static_cast<long long>(kdim);
-        gd.M = static_cast<long long>(n);
-        gd.N = static_cast<long long>(v);
-        gd.epi = Epi::Logits;
-        gd.status = status;
-        EpiArgs& ea = gd.args;
-        ea.logits = logits_t;
-        ea.ldl = static_cast<long long>(L.ldv);
-        ea.rec_own = rec_own_t;
-        ea.n_parts = static_cast<int>(L.parts);
-        ea.inv_t = inv_t;
-        ea.own_d1 = f.teacher_ce;
-        ea.own_sx = f.teacher_ce && f.alpha > 0.0f;
-        if ((e = gemm_launch(gd, ctx->num_sms, st, &why)) != cudaSuccess)
-          return cuda_fail(e, why ? why : "teacher logits GEMM", err, len);
-      }
-      // ---- student logits + statistics
+      const void* t_rows = live_teacher ? static_cast<const void*>(logits_t)
+                                        : static_cast<const void*>(static_cast<const uint8_t*>(in.t_logits) +
+                                                                   s * in.ld_t_logits * t_esz);
+      const long long t_ld = live_teacher ? static_cast<long long>(L.ldv) : in.ld_t_logits;
+      const int t_bf16 = live_teacher ? 0 : static_cast<int>(in.t_logits_bf16);
       {
-        ph_fwd->launched();
+        Phase ph_fwd(ctx, 0, st);
+        // ---- teacher logits + statistics (Tied / Separate)
+        if (f.teacher_rows) {
+          ph_fwd.launched();
+          GemmDesc gd;
+          const MatRef& tw = in.mode == ORDA_TEACHER_TIED ? in.w : in.wt;
+          const size_t kdim = in.mode == ORDA_TEACHER_TIED ? h : ht;
+          gd.a[0] = MatRef{static_cast<const uint16_t*>(in.ht.ptr) + s * in.ht.ld, static_cast<long long>(n),
+                           static_cast<long long>(kdim), in.ht.ld};
+          gd.b[0] = tw;
+          gd.k_seg[0] = static_cast<long long>(kdim);
+          gd.M = static_cast<long long>(n);
+          gd.N = static_cast<long long>(v);
+          gd.epi = Epi::Logits;
+          gd.status = status;
+          gd.args.logits = logits_t;
+          gd.args.ldl = static_cast<long long>(L.ldv);
+          gd.args.rec_own = rec_own_t;
+          gd.args.n_parts = static_cast<int>(L.parts);
+          gd.args.inv_t = inv_t;
+          gd.args.own_dT = f.kd > 0.0f;
+          if ((e = gemm_launch(gd, ctx->num_sms, st, &why)) != cudaSuccess)
+            return cuda_fail(e, why ? why : "teacher logits GEMM", err, len);
+        }
+        // ---- student logits + statistics
+        ph_fwd.launched();
         GemmDesc gd;
         gd.a[0] = MatRef{static_cast<const uint16_t*>(in.hs.ptr) + s * in.hs.ld, static_cast<long long>(n),
                          static_cast<long long>(h), in.hs.ld};
@@ -344,58 +359,35 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
         gd.N = static_cast<long long>(v);
         gd.epi = Epi::Logits;
         gd.status = status;
-        EpiArgs& ea = gd.args;
-        ea.logits = logits;
-        ea.ldl = static_cast<long long>(L.ldv);
-        ea.rec_own = rec_own;
-        ea.rec_pair = rec_pair;
-        ea.n_parts = static_cast<int>(L.parts);
-        ea.inv_t = inv_t;
-        ea.own_d1 = 1;
-        ea.own_dT = f.kd > 0.0f;
-        ea.own_sx = f.alpha > 0.0f;
-        ea.pair = f.pair;
-        if (f.pair) {
-          if (live_teacher) {
-            ea.pair_src = logits_t;
-            ea.ld_pair = static_cast<long long>(L.ldv);
-            ea.pair_is_bf16 = 0;
-          } else {
-            const size_t esz = in.t_logits_bf16 ? 2 : 4;
-            ea.pair_src = static_cast<const uint8_t*>(in.t_logits) + s * in.ld_t_logits * esz;
-            ea.ld_pair = in.ld_t_logits;
-            ea.pair_is_bf16 = in.t_logits_bf16;
-            ea.pair_d1 = f.teacher_ce;
-            ea.pair_sx = f.teacher_ce && f.alpha > 0.0f;
-          }
-        }
+        gd.args.logits = logits;
+        gd.args.ldl = static_cast<long long>(L.ldv);
+        gd.args.rec_own = rec_own;
+        gd.args.n_parts = static_cast<int>(L.parts);
+        gd.args.inv_t = inv_t;
+        gd.args.own_dT = f.kd > 0.0f;
         if ((e = gemm_launch(gd, ctx->num_sms, st, &why)) != cudaSuccess)
           return cuda_fail(e, why ? why : "student logits GEMM", err, len);
       }
-      ph_fwd.reset();
-      // ---- row pass: losses and logit gradients
+      // ---- row pass: teacher statistics (given logits), losses, logit gradients
       {
         Phase ph_rows(ctx, 1, st);
+        if (f.need_teacher && !live_teacher) {
+          ph_rows.launched();
+          launch_teacher_stats(t_rows, t_ld, t_bf16, static_cast<int>(n), static_cast<int>(v), inv_t, rec_own_t, st);
+        }
         ph_rows.launched(kRowLaunches);
         RowArgs r{};
         r.n = static_cast<int>(n);
         r.v = static_cast<int>(v);
         r.n_parts = static_cast<int>(L.parts);
+        r.n_parts_t = static_cast<int>(L.parts_t);
         r.logits_s = logits;
         r.ldl = static_cast<long long>(L.ldv);
-        if (live_teacher) {
-          r.teacher = logits_t;
-          r.ld_teacher = static_cast<long long>(L.ldv);
-          r.teacher_is_bf16 = 0;
-        } else {
-          const size_t esz = in.t_logits_bf16 ? 2 : 4;
-          r.teacher = static_cast<const uint8_t*>(in.t_logits) + s * in.ld_t_logits * esz;
-          r.ld_teacher = in.ld_t_logits;
-          r.teacher_is_bf16 = in.t_logits_bf16;
-        }
+        r.teacher = t_rows;
+        r.ld_teacher = t_ld;
+        r.teacher_is_bf16 = t_bf16;
         r.rec_own = rec_own;
         r.rec_own_t = rec_own_t;
-        r.rec_pair = rec_pair;
         r.labels = in.labels + s;
         r.ignore_index = o.ignore_index;
         r.w_s = f.w_s;
@@ -406,17 +398,19 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
         r.alpha = f.alpha;
         r.need_kl = f.kd > 0.0f;
         r.teacher_ce = f.teacher_ce;
-        r.teacher_ce_from_own = live_teacher;
         r.teacher_grad = f.teacher_grad;
         r.dlog_s = dlog_s + (s - g0) * L.ldd;
         r.dlog_t = f.teacher_grad ? dlog_t + (s - g0) * L.ldd : nullptr;
         r.ldd = static_cast<long long>(L.ldd);
         r.nll_s_rows = nll_s + s;
         r.nll_t_rows = nll_t + s;
-        r.kl_rows = kl_rows + s;
+        r.kl_base_rows = kl_base + s;
+        r.s_part = s_part + s * L.nseg;
+        r.nseg = static_cast<int>(L.nseg);
         r.row_const = row_const;
+        r.num_sms = ctx->num_sms;
         launch_rows(r, st);
-        if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(e, "row kernel", err, len);
+        if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(e, "row kernels", err, len);
       }
     }
     const long long rows_g = static_cast<long long>(g1 - g0);
@@ -502,8 +496,9 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
   {
     Phase ph(ctx, 5, st);
     ph.launched();
-    launch_finalize(nll_s, nll_t, kl_rows, static_cast<long long>(bt), ctx->d_mean_scale, f.w_s, f.w_t, f.kd,
-                  out.scalars, st);
+    const double t_sq = static_cast<double>(f.temperature * f.temperature);
+    launch_finalize(nll_s, nll_t, kl_base, s_part, static_cast<int>(L.nseg), t_sq, static_cast<long long>(bt),
+                    ctx->d_mean_scale, f.w_s, f.w_t, f.kd, out.scalars, st);
   }
   if (f.quant) {
     Phase ph(ctx, 4, st);
@@ -544,6 +539,53 @@ int check_status(OrdaContext* ctx, char* err, size_t len) {
 
 std::mutex g_default_mu;
 OrdaContext* g_default_ctx[64] = {nullptr};
+
+// Output buffers of the host-Mat entry: page-locked host memory recycled
+// through a pool, so the gradients come back at full PCIe bandwidth without
+// page faults on every call. orda_output_free returns a buffer to the pool;
+// at most kPinnedPoolCap bytes of free buffers are kept.
+constexpr size_t kPinnedPoolCap = size_t{16} << 30;
+std::mutex g_pinned_mu;
+std::multimap<size_t, void*> g_pinned_free;      // capacity -> buffer
+std::unordered_map<void*, size_t> g_pinned_cap;  // live and free buffers
+size_t g_pinned_free_bytes = 0;
+
+float* pinned_alloc(size_t bytes) {
+  bytes = std::max<size_t>(bytes, 256);
+  {
+    std::lock_guard<std::mutex> lock(g_pinned_mu);
+    auto it = g_pinned_free.lower_bound(bytes);
+    if (it != g_pinned_free.end() && it->first <= 2 * bytes) {
+      void* p = it->second;
+      g_pinned_free_bytes -= it->first;
+      g_pinned_free.erase(it);
+      return static_cast<float*>(p);
+    }
+  }
+  void* p = nullptr;
+  if (cudaHostAlloc(&p, bytes, cudaHostAllocDefault) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(g_pinned_mu);
+  g_pinned_cap[p] = bytes;
+  return static_cast<float*>(p);
+}
+
+void pinned_release(void* p) {
+  if (!p) return;
+  std::lock_guard<std::mutex> lock(g_pinned_mu);
+  auto it = g_pinned_cap.find(p);
+  if (it == g_pinned_cap.end()) return;
+  const size_t cap = it->second;
+  if (g_pinned_free_bytes + cap > kPinnedPoolCap) {
+    g_pinned_cap.erase(it);
+    cudaFreeHost(p);
+    return;
+  }
+  g_pinned_free.emplace(cap, p);
+  g_pinned_free_bytes += cap;
+}
 
 }  // namespace
 }  // namespace orda
@@ -933,7 +975,7 @@ int orda_distillation_loss(const OrdaMatF32* student_hidden, const OrdaMatF32* w
   auto dl = [&](float* dsrc, size_t rows, size_t cols, OrdaMatOut& m) -> cudaError_t {
     m.rows = rows;
     m.cols = cols;
-    m.data = static_cast<float*>(std::malloc(std::max<size_t>(rows * cols, 1) * 4));
+    m.data = pinned_alloc(std::max<size_t>(rows * cols, 1) * 4);
     if (!m.data) return cudaErrorMemoryAllocation;
     return cudaMemcpyAsync(m.data, dsrc, rows * cols * 4, cudaMemcpyDeviceToHost, st);
   };
@@ -962,10 +1004,10 @@ int orda_distillation_loss(const OrdaMatF32* student_hidden, const OrdaMatF32* w
 
 void orda_output_free(OrdaOutput* out) {
   if (!out) return;
-  std::free(out->grad_student_hidden.data);
-  std::free(out->grad_weight.data);
-  std::free(out->grad_teacher_hidden.data);
-  std::free(out->grad_teacher_weight.data);
+  pinned_release(out->grad_student_hidden.data);
+  pinned_release(out->grad_weight.data);
+  pinned_release(out->grad_teacher_hidden.data);
+  pinned_release(out->grad_teacher_weight.data);
   out->grad_student_hidden.data = nullptr;
   out->grad_weight.data = nullptr;
   out->grad_teacher_hidden.data = nullptr;

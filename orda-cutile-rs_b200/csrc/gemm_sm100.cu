@@ -15,9 +15,9 @@
 //   grad_h = dlogits @ W  (A K-major, B MN-major)
 //   grad_W = dlogits^T @ h (A MN-major, B MN-major)
 // Epilogues: plain scaled store, or the logits epilogue that writes fp32
-// logits and per-row online-softmax statistics (max, sum exp(x-m),
-// sum exp((x-m)/T), sum x) together with the paired teacher statistics and
-// the KL cross term, so the loss never needs a separate reduction pass.
+// logits and per-(row, 128-column part) online-softmax statistics (max,
+// sum exp(x-m), sum exp((x-m)/T), sum x) from the fp32 accumulators, so the
+// loss needs no separate reduction pass over the logits.
 //
 // No TMA multicast is used anywhere (the same kernels serve multi-GPU runs).
 #include <cuda.h>
@@ -27,6 +27,8 @@
 
 #include <cmath>
 #include <cstdio>
+#include <cstring>
+#include <atomic>
 #include <mutex>
 
 #include "kernels.h"
@@ -47,7 +49,11 @@ constexpr int NUM_THREADS = 384;  // warp 0 TMA, 1 MMA, 2 TMEM, 3 idle, 4..11 ep
 constexpr int EPI_WARP0 = 4;
 constexpr int NUM_EPI_WARPS = 8;
 constexpr int TMEM_COLS = 512;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+// Per epilogue warp: one 32 x 32 fp32 output chunk staged for a TMA store.
+constexpr int OUT_STAGE_BYTES = 32 * 32 * 4;
+constexpr int OUT_BYTES = NUM_EPI_WARPS * OUT_STAGE_BYTES;  // 32 KB
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + OUT_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+static_assert(SMEM_BYTES <= 232448, "shared memory over the sm_100 opt-in limit");
 constexpr float LOG2E = 1.4426950408889634f;
 
 struct KParams {
@@ -57,6 +63,9 @@ struct KParams {
   int nseg;
   int seg_kblocks[2];
   int* status;
+  int prefetch_b;  // L2 prefetch distance (k-blocks) for a K-major B operand; 0 = off
+  int tma_store;   // output written through the staging buffers + TMA
+  int tma_reduce;  // TMA reduce-add into the output (beta == 1)
   EpiArgs e;
 };
 
@@ -69,8 +78,6 @@ __device__ __forceinline__ void tile_coords(const KParams& p, int tile, int& mb,
     nb = tile / p.m_blocks;
   }
 }
-
-__device__ __forceinline__ float bf16_bits_to_f32(uint16_t b) { return __uint_as_float(static_cast<uint32_t>(b) << 16); }
 
 // ------------------------------------------------------------- epilogues
 
@@ -114,140 +121,85 @@ __device__ __forceinline__ void epi_store_chunk(const KParams& p, long long grow
 struct OwnStats {
   float m, d1, dT, sx;
 };
-struct PairStats {
-  float m, d1, dT, s, sx;
-};
 
-// Logits epilogue for one 32-column chunk of one row.
-__device__ __forceinline__ void epi_logits_chunk(const KParams& p, long long grow, bool row_ok, int col0,
-                                                 int nvalid, const uint32_t (&r)[32], OwnStats& os,
-                                                 PairStats& ps) {
-  const EpiArgs& e = p.e;
+// e^x as 2^(x * log2 e) with the PTX ex2.approx.ftz.f32 instruction (one
+// MUFU op); statistics sums of up to 128 terms tolerate its ~2^-22 relative
+// error (checked against the f64 oracle by the parity tests).
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ float max32(const float (&v)[32]) {
+  float m[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) m[k] = fmaxf(fmaxf(v[4 * k], v[4 * k + 1]), fmaxf(v[4 * k + 2], v[4 * k + 3]));
+#pragma unroll
+  for (int k = 0; k < 4; ++k) m[k] = fmaxf(m[k], m[k + 4]);
+  return fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3]));
+}
+
+// Online-softmax statistics of one 32-column chunk of one row. FULL: all 32
+// columns valid (no per-element masking).
+template <bool FULL, bool OWN_DT>
+__device__ __forceinline__ void logits_chunk(const EpiArgs& e, long long grow, bool row_ok, int col0, int nvalid,
+                                             const uint32_t (&r)[32], OwnStats& os) {
   float v[32];
 #pragma unroll
   for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+  const float lt = LOG2E * e.inv_t;
+  float vm[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) vm[j] = (FULL || j < nvalid) ? v[j] : -INFINITY;
+  const float m_new = fmaxf(os.m, max32(vm));
+  const float dm = os.m - m_new;  // -inf on the first chunk: factors 0
+  os.d1 *= fast_exp2(dm * LOG2E);
+  if (OWN_DT) os.dT *= fast_exp2(dm * lt);
+  os.m = m_new;
+  float a1[4] = {0.f, 0.f, 0.f, 0.f}, aT[4] = {0.f, 0.f, 0.f, 0.f}, ax[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    if (FULL || j < nvalid) {
+      const float u = v[j] - m_new;
+      a1[j & 3] += fast_exp2(u * LOG2E);
+      if (OWN_DT) aT[j & 3] += fast_exp2(u * lt);
+      ax[j & 3] += v[j];
+    }
+  }
+  os.d1 += (a1[0] + a1[1]) + (a1[2] + a1[3]);
+  if (OWN_DT) os.dT += (aT[0] + aT[1]) + (aT[2] + aT[3]);
+  os.sx += (ax[0] + ax[1]) + (ax[2] + ax[3]);
+}
 
-  // fp32 logits store
-  if (row_ok) {
-    float* dst = e.logits + grow * e.ldl + col0;
-    if (nvalid == 32) {
-#pragma unroll
-      for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-    } else {
-#pragma unroll
-      for (int j = 0; j < 32; ++j)
-        if (j < nvalid) dst[j] = v[j];
-    }
-  }
+template <bool OWN_DT>
+__device__ __forceinline__ void logits_chunk_any(const EpiArgs& e, long long grow, bool row_ok, int col0, int N,
+                                                 const uint32_t (&r)[32], OwnStats& os) {
+  const int nvalid = N - col0;
+  if (nvalid >= 32) logits_chunk<true, OWN_DT>(e, grow, row_ok, col0, 32, r, os);
+  else if (nvalid > 0) logits_chunk<false, OWN_DT>(e, grow, row_ok, col0, nvalid, r, os);
+}
 
-  const float inv_t = e.inv_t;
-  const float lt = LOG2E * inv_t;
-
-  // own online-softmax statistics
-  float cmax = -INFINITY;
+// Writes the warp's 32 x 32 fp32 chunk (row `lane` = this thread's values,
+// times alpha) to its staging buffer in the 128-byte-swizzled layout of the
+// output tensor map, then one lane issues the TMA store (or reduce-add). The
+// buffer is reused only after the previous store has read it.
+__device__ __forceinline__ void stage_and_store(uint8_t* buf, int lane, const uint32_t (&r)[32], float alpha,
+                                                const CUtensorMap* map, int x, int y, bool reduce) {
+  if (lane == 0) bulk_wait_read_all();
+  __syncwarp();
 #pragma unroll
-  for (int j = 0; j < 32; ++j)
-    if (j < nvalid) cmax = fmaxf(cmax, v[j]);
-  if (cmax > os.m) {
-    if (os.m != -INFINITY) {
-      const float dm = os.m - cmax;
-      os.d1 *= exp2f(dm * LOG2E);
-      os.dT *= exp2f(dm * lt);
-    }
-    os.m = cmax;
+  for (int c = 0; c < 8; ++c) {
+    const float4 q = make_float4(alpha * __uint_as_float(r[4 * c]), alpha * __uint_as_float(r[4 * c + 1]),
+                                 alpha * __uint_as_float(r[4 * c + 2]), alpha * __uint_as_float(r[4 * c + 3]));
+    *reinterpret_cast<float4*>(buf + lane * 128 + ((c ^ (lane & 7)) << 4)) = q;
   }
-  {
-    float a1 = 0.f, aT = 0.f, ax = 0.f;
-    const float m = os.m;
-#pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      if (j < nvalid) {
-        const float dx = v[j] - m;
-        if (e.own_d1) a1 += exp2f(dx * LOG2E);
-        if (e.own_dT) aT += exp2f(dx * lt);
-        ax += v[j];
-      }
-    }
-    os.d1 += a1;
-    os.dT += aT;
-    os.sx += ax;
-  }
-
-  if (!e.pair) return;
-  // paired teacher values for the same (row, columns)
-  float t[32];
-  if (row_ok) {
-    if (e.pair_is_bf16) {
-      const uint16_t* src = static_cast<const uint16_t*>(e.pair_src) + grow * e.ld_pair + col0;
-      if (nvalid == 32 && ((reinterpret_cast<uintptr_t>(src) & 15) == 0)) {
-#pragma unroll
-        for (int j = 0; j < 32; j += 8) {
-          uint4 q = *reinterpret_cast<const uint4*>(src + j);
-          t[j + 0] = __uint_as_float(q.x << 16);
-          t[j + 1] = __uint_as_float(q.x & 0xFFFF0000u);
-          t[j + 2] = __uint_as_float(q.y << 16);
-          t[j + 3] = __uint_as_float(q.y & 0xFFFF0000u);
-          t[j + 4] = __uint_as_float(q.z << 16);
-          t[j + 5] = __uint_as_float(q.z & 0xFFFF0000u);
-          t[j + 6] = __uint_as_float(q.w << 16);
-          t[j + 7] = __uint_as_float(q.w & 0xFFFF0000u);
-        }
-      } else {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) t[j] = j < nvalid ? bf16_bits_to_f32(src[j]) : 0.f;
-      }
-    } else {
-      const float* src = static_cast<const float*>(e.pair_src) + grow * e.ld_pair + col0;
-      if (nvalid == 32 && ((reinterpret_cast<uintptr_t>(src) & 15) == 0)) {
-#pragma unroll
-        for (int j = 0; j < 32; j += 4) {
-          float4 q = *reinterpret_cast<const float4*>(src + j);
-          t[j] = q.x;
-          t[j + 1] = q.y;
-          t[j + 2] = q.z;
-          t[j + 3] = q.w;
-        }
-      } else {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) t[j] = j < nvalid ? src[j] : 0.f;
-      }
-    }
-  } else {
-#pragma unroll
-    for (int j = 0; j < 32; ++j) t[j] = 0.f;
-  }
-  float tmax = -INFINITY;
-#pragma unroll
-  for (int j = 0; j < 32; ++j)
-    if (j < nvalid) tmax = fmaxf(tmax, t[j]);
-  if (tmax > ps.m) {
-    if (ps.m != -INFINITY) {
-      const float dm = ps.m - tmax;
-      const float fT = exp2f(dm * lt);
-      ps.dT *= fT;
-      ps.s *= fT;
-      ps.d1 *= exp2f(dm * LOG2E);
-    }
-    ps.m = tmax;
-  }
-  {
-    float a1 = 0.f, aT = 0.f, as = 0.f, ax = 0.f;
-    const float m = ps.m;
-#pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      if (j < nvalid) {
-        const float dx = t[j] - m;
-        const float eT = exp2f(dx * lt);
-        aT += eT;
-        as += eT * ((t[j] - v[j]) * inv_t);
-        if (e.pair_d1) a1 += exp2f(dx * LOG2E);
-        ax += t[j];
-      }
-    }
-    ps.dT += aT;
-    ps.s += as;
-    ps.d1 += a1;
-    ps.sx += ax;
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    if (reduce) tma_reduce_add_2d(map, buf, x, y);
+    else tma_store_2d(map, buf, x, y);
+    bulk_commit();
   }
 }
 
@@ -257,12 +209,13 @@ template <bool A_MN, bool B_MN, int EPI>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap mapA0, const __grid_constant__ CUtensorMap mapA1,
                 const __grid_constant__ CUtensorMap mapB0, const __grid_constant__ CUtensorMap mapB1,
-                const __grid_constant__ KParams p) {
+                const __grid_constant__ CUtensorMap mapC, const __grid_constant__ KParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_STAGE_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint8_t* sOut = smem + STAGES * STAGE_BYTES;  // 1024-byte aligned
+  uint64_t* full = reinterpret_cast<uint64_t*>(sOut + OUT_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
@@ -330,6 +283,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             }
             if (!B_MN) {
               tma_load_2d(b_dst, mbm, &full[stage], kb * BK, nb * BN);
+              if (p.prefetch_b > 0 && kb + p.prefetch_b < p.seg_kblocks[seg])
+                tma_prefetch_l2_2d(mbm, (kb + p.prefetch_b) * BK, nb * BN);
             } else {
 #pragma unroll
               for (int i = 0; i < BN / 64; ++i)
@@ -418,52 +373,86 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const bool row_ok = grow < p.M;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
                              static_cast<uint32_t>(acc * BN + half * 128);
+      const int colh = nb * BN + half * 128;
+      const int row0 = mb * BM + quad * 32;
+      uint8_t* buf = sOut + ew * OUT_STAGE_BYTES;
+      // Releases the accumulator to the MMA warp as soon as its last TMEM
+      // load has completed (the remaining work uses registers only).
+      auto release_tmem = [&]() {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[acc]);
+      };
       if constexpr (EPI == static_cast<int>(Epi::Store)) {
         const float alpha = p.e.alpha_ptr ? *p.e.alpha_ptr : p.e.alpha;
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          const int col0 = nb * BN + half * 128 + c * 32;
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(t_row + c * 32, r);
-          tmem_ld_wait();
-          if (col0 < p.N && row_ok) {
-            const int nvalid = min(32, p.N - col0);
-            epi_store_chunk(p, grow, col0, nvalid, r, alpha);
+        auto store = [&](int c, const uint32_t(&r)[32]) {
+          const int col0 = colh + c * 32;
+          if (col0 >= p.N) return;
+          if (p.tma_store) {
+            if (row0 < p.M) stage_and_store(buf, lane, r, alpha, &mapC, col0, row0, p.tma_reduce != 0);
           }
-        }
+          else if (row_ok) epi_store_chunk(p, grow, col0, min(32, p.N - col0), r, alpha);
+        };
+        // the TMEM load of chunk c+1 is in flight while chunk c is stored
+        uint32_t ra[32], rb[32];
+        tmem_ld_32x32b_x32(t_row, ra);
+        tmem_ld_wait();
+        tmem_ld_32x32b_x32(t_row + 32, rb);
+        store(0, ra);
+        tmem_ld_wait();
+        tmem_ld_32x32b_x32(t_row + 64, ra);
+        store(1, rb);
+        tmem_ld_wait();
+        tmem_ld_32x32b_x32(t_row + 96, rb);
+        store(2, ra);
+        tmem_ld_wait();
+        release_tmem();
+        store(3, rb);
       } else {
+        constexpr bool OWN_DT = (EPI & 1) != 0;
         OwnStats os{-INFINITY, 0.f, 0.f, 0.f};
-        PairStats ps{-INFINITY, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          const int col0 = nb * BN + half * 128 + c * 32;
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(t_row + c * 32, r);
-          tmem_ld_wait();
-          if (col0 < p.N) {
-            const int nvalid = min(32, p.N - col0);
-            epi_logits_chunk(p, grow, row_ok, col0, nvalid, r, os, ps);
+        const EpiArgs& e = p.e;
+        auto chunk = [&](int c, const uint32_t(&r)[32]) {
+          const int col0 = colh + c * 32;
+          if (col0 >= p.N) return;
+          logits_chunk_any<OWN_DT>(e, grow, row_ok, col0, p.N, r, os);
+          if (p.tma_store) {
+            if (row0 < p.M) stage_and_store(buf, lane, r, 1.0f, &mapC, col0, row0, false);
+          } else if (row_ok) {
+            float* dst = e.logits + grow * e.ldl + col0;
+            const int nv = min(32, p.N - col0);
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (j < nv) dst[j] = __uint_as_float(r[j]);
           }
-        }
-        const int part = nb * 2 + half;
-        if (row_ok && nb * BN + half * 128 < p.N) {
-          const long long ri = grow * p.e.n_parts + part;
-          reinterpret_cast<float4*>(p.e.rec_own)[ri] = make_float4(os.m, os.d1, os.dT, os.sx);
-          if (p.e.pair) {
-            float4* pr = reinterpret_cast<float4*>(p.e.rec_pair) + ri * 2;
-            pr[0] = make_float4(ps.m, ps.d1, ps.dT, ps.s);
-            pr[1] = make_float4(ps.sx, 0.f, 0.f, 0.f);
-          }
+        };
+        // the TMEM load of chunk c+1 is in flight while chunk c is processed
+        uint32_t ra[32], rb[32];
+        tmem_ld_32x32b_x32(t_row, ra);
+        tmem_ld_wait();
+        tmem_ld_32x32b_x32(t_row + 32, rb);
+        chunk(0, ra);
+        tmem_ld_wait();
+        tmem_ld_32x32b_x32(t_row + 64, ra);
+        chunk(1, rb);
+        tmem_ld_wait();
+        tmem_ld_32x32b_x32(t_row + 96, rb);
+        chunk(2, ra);
+        tmem_ld_wait();
+        release_tmem();
+        chunk(3, rb);
+        if (row_ok && colh < p.N) {
+          const long long ri = grow * e.n_parts + nb * 2 + half;
+          reinterpret_cast<float4*>(e.rec_own)[ri] = make_float4(os.m, os.d1, os.dT, os.sx);
         }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[acc]);
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1;
       }
     }
+    if (p.tma_store && lane == 0) bulk_wait_all();
+    __syncwarp();
   }
 
   tc_fence_before();
@@ -503,13 +492,38 @@ bool encode_map(CUtensorMap* map, const MatRef& m, int box_inner, int box_outer)
   return r == CUDA_SUCCESS;
 }
 
+// fp32 output map: rows x cols with leading dimension ld (elements), 32 x 32
+// box, 128-byte swizzle (the staging layout of the epilogue).
+bool encode_out_map(CUtensorMap* map, float* ptr, long long rows, long long cols, long long ld) {
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 4};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, ptr, dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+bool out_map_ok(const float* ptr, long long ld) {
+  return ptr && (reinterpret_cast<uintptr_t>(ptr) & 15) == 0 && (ld * 4) % 16 == 0;
+}
+
 template <bool A_MN, bool B_MN, int EPI>
 cudaError_t launch_t(const CUtensorMap* maps, const KParams& kp, int grid, cudaStream_t stream) {
   auto kern = gemm_kernel<A_MN, B_MN, EPI>;
-  // Per device and cheap; set on every launch so any device/thread works.
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-  if (e != cudaSuccess) return e;
-  kern<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(maps[0], maps[1], maps[2], maps[3], kp);
+  // The shared-memory opt-in is a per-device function attribute: set it once
+  // per device for this instantiation.
+  static std::atomic<uint64_t> attr_done{0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const uint64_t bit = 1ull << (dev & 63);
+  if (!(attr_done.load(std::memory_order_acquire) & bit)) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    attr_done.fetch_or(bit, std::memory_order_acq_rel);
+  }
+  kern<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(maps[0], maps[1], maps[2], maps[3], maps[4], kp);
   return cudaGetLastError();
 }
 
@@ -531,7 +545,7 @@ cudaError_t gemm_launch(const GemmDesc& d, int num_sms, cudaStream_t stream, con
   kp.nseg = d.nseg;
   kp.status = d.status;
   kp.e = d.args;
-  CUtensorMap maps[4];
+  CUtensorMap maps[5];
   for (int s = 0; s < 2; ++s) {
     const int src = s < d.nseg ? s : 0;
     kp.seg_kblocks[s] = s < d.nseg ? static_cast<int>((d.k_seg[s] + BK - 1) / BK) : 0;
@@ -550,6 +564,21 @@ cudaError_t gemm_launch(const GemmDesc& d, int num_sms, cudaStream_t stream, con
       return cudaErrorInvalidValue;
     }
   }
+  // L2 prefetch of B ahead of the ring: measured no gain for the logits GEMM
+  // (its B tiles are shared by the chunk's M tiles through L2 already).
+  kp.prefetch_b = 0;
+  // output through shared-memory staging + TMA when the output allows it
+  std::memset(&maps[4], 0, sizeof(CUtensorMap));
+  kp.tma_store = 0;
+  kp.tma_reduce = 0;
+  if (d.epi == Epi::Logits) {
+    if (out_map_ok(d.args.logits, d.args.ldl) && encode_out_map(&maps[4], d.args.logits, d.M, d.N, d.args.ldl))
+      kp.tma_store = 1;
+  } else if (d.args.split_row >= d.M && (d.args.beta == 0.0f || d.args.beta == 1.0f) &&
+             out_map_ok(d.args.out0, d.args.ld0) && encode_out_map(&maps[4], d.args.out0, d.M, d.N, d.args.ld0)) {
+    kp.tma_store = 1;
+    kp.tma_reduce = d.args.beta == 1.0f ? 1 : 0;
+  }
   if (kp.num_tiles == 0) return cudaSuccess;
   const int grid = kp.num_tiles < num_sms ? kp.num_tiles : num_sms;
   const int epi = static_cast<int>(d.epi);
@@ -558,7 +587,9 @@ cudaError_t gemm_launch(const GemmDesc& d, int num_sms, cudaStream_t stream, con
       if (why) *why = "logits epilogue requires K-major operands";
       return cudaErrorInvalidValue;
     }
-    return launch_t<false, false, 1>(maps, kp, grid, stream);
+    // EPI code: 16 | own dT
+    if (d.args.own_dT) return launch_t<false, false, 17>(maps, kp, grid, stream);
+    return launch_t<false, false, 16>(maps, kp, grid, stream);
   }
   if (!d.a_mn_major && !d.b_mn_major) return launch_t<false, false, 0>(maps, kp, grid, stream);
   if (!d.a_mn_major && d.b_mn_major) return launch_t<false, true, 0>(maps, kp, grid, stream);

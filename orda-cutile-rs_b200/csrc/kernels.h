@@ -37,14 +37,9 @@ struct EpiArgs {
   float* logits = nullptr;
   long long ldl = 0;
   float* rec_own = nullptr;   // float4 per (row, part)
-  float* rec_pair = nullptr;  // 8 floats per (row, part)
   int n_parts = 0;
-  const void* pair_src = nullptr;  // teacher logits paired with this tile (same row/col)
-  long long ld_pair = 0;
-  int pair_is_bf16 = 0;
   float inv_t = 1.0f;
-  int own_d1 = 0, own_dT = 0, own_sx = 0;
-  int pair = 0, pair_d1 = 0, pair_sx = 0;
+  int own_dT = 0;
 };
 
 struct GemmDesc {
@@ -69,35 +64,43 @@ cudaError_t gemm_launch(const GemmDesc& d, int num_sms, cudaStream_t stream, con
 struct RowArgs {
   int n;                  // rows in this chunk
   int v;                  // vocabulary
-  int n_parts;            // record parts per row
+  int n_parts;            // student record parts per row
+  int n_parts_t;          // teacher record parts per row (1 after the teacher pre-pass)
   const float* logits_s;  // [n, ldl] fp32 student logits
   const void* teacher;    // teacher logits rows for this chunk (fp32 or bf16)
   long long ld_teacher;
   int teacher_is_bf16;
   long long ldl;
-  const float* rec_own;   // [n] student own records
-  const float* rec_own_t; // [n] teacher own records (Tied/Separate teacher CE stats)
-  const float* rec_pair;  // [n] pair records (teacher KL stats, S)
+  const float* rec_own;   // [n] student records
+  const float* rec_own_t; // [n] teacher records (from the teacher GEMM or the pre-pass)
   const int64_t* labels;  // chunk labels
   int64_t ignore_index;
   float w_s, w_t, kd, temperature, inv_t, alpha;
   int need_kl;            // kd > 0
   int teacher_ce;         // w_t > 0 (teacher CE reported)
-  int teacher_ce_from_own;  // Tied/Separate: teacher CE stats from rec_own rows n..2n
   int teacher_grad;       // write teacher dlogits rows
   uint16_t* dlog_s;       // bf16 [n, ldd]
   uint16_t* dlog_t;       // bf16 [n, ldd] (teacher_grad)
   long long ldd;
   float* nll_s_rows;      // [n]
   float* nll_t_rows;      // [n]
-  double* kl_rows;        // [n] (KL * T^2, ignored -> 0)
+  double* kl_base_rows;   // [n] lse_s^T - lse_t^T (0 for ignored rows)
+  float* s_part;          // [n, nseg] KL cross-term partials sum_j p_t^T (t - x) / T
+  int nseg;               // column segments of the gradient pass
   void* row_const;        // [n] x 32 B scratch: per-row constants (stats -> gradient kernel)
+  int num_sms;
 };
-// Two launches: the per-row statistics kernel and the elementwise gradient
-// kernel.
+// Two launches: the per-row statistics kernel and the gradient kernel.
 constexpr int kRowLaunches = 2;
 constexpr size_t kRowConstBytes = 32;
+// Columns per CTA of the gradient pass (256 threads x 8 columns x 4 steps).
+constexpr int kGradSegCols = 8192;
 void launch_rows(const RowArgs& a, cudaStream_t stream);
+
+// Teacher statistics pre-pass over given teacher logits (Precomputed mode):
+// one (max, sum e^(t-m), sum e^((t-m)/T), sum t) record per row.
+void launch_teacher_stats(const void* teacher, long long ld, int is_bf16, int n, int v, float inv_t, float* rec,
+                          cudaStream_t stream);
 
 // Label pass: counts non-ignored labels, checks the range [0, v), marks
 // target rows (for the quantiser) and writes the mean scale.
@@ -105,9 +108,11 @@ void launch_label_prep(const int64_t* labels, long long bt, long long v, int64_t
                        long long denom_override, int* n_non_ignore, float* mean_scale, uint8_t* target_flags,
                        int* status, cudaStream_t stream);
 
-// Final deterministic reduction of per-row losses into the four scalars.
-void launch_finalize(const float* nll_s, const float* nll_t, const double* kl_rows, long long bt,
-                     const float* mean_scale, float w_s, float w_t, float kd, float* scalars, cudaStream_t stream);
+// Final deterministic reduction of per-row losses into the four scalars:
+// KL_row = (kl_base + sum over segments of s_part) * T^2.
+void launch_finalize(const float* nll_s, const float* nll_t, const double* kl_base, const float* s_part, int nseg,
+                     double t_sq, long long bt, const float* mean_scale, float w_s, float w_t, float kd,
+                     float* scalars, cudaStream_t stream);
 
 // f32 -> bf16 (round to nearest even) into a padded row-major buffer.
 void launch_f32_to_bf16(const float* src, long long rows, long long cols, uint16_t* dst, long long ld,

@@ -1,19 +1,25 @@
 // rows.cu -- bandwidth-bound row kernels of the distillation loss.
 //
-// Record layout written by the logits GEMM epilogue (gemm_sm100.cu), one
-// record per (row, 128-column part):
-//   own  (float4): m = max x, d1 = sum exp(x - m), dT = sum exp((x - m)/T),
-//                  sx = sum x
-//   pair (2 x float4, teacher values of the same row/columns):
-//                  m_t, d1_t, dT_t, S = sum exp((t - m_t)/T) * (t - x)/T | sx_t
-// The row kernel merges the records in double precision, evaluates the
-// per-row NLL and KL exactly as the reference defines them
-// (src/reference/cross_entropy.rs:20-74, src/reference/kl.rs:66-127), and
-// streams the row once to write the merged logit gradient
-//   dlogit_s = w_s*((p - a/V) - [j==y](1-a)) + kd*T*(p_s^T - p_t^T)
-//   dlogit_t = w_t*((p_t - a/V) - [j==y](1-a))
-// in bf16 (the operand type of the backward GEMMs), as src/api.rs:301-344
-// does on the CPU.
+// Record layout (float4 per record): m = max x, d1 = sum e^(x-m),
+// dT = sum e^((x-m)/T), sx = sum x. The logits GEMM epilogue writes one
+// record per (row, 128-column part) of the student (and of the teacher for
+// Tied/Separate); teacher_stats_kernel writes one record per row for given
+// (Precomputed) teacher logits.
+//
+// Per chunk:
+//   row_stats_kernel  merges a row's records (f64), evaluates the row's NLLs
+//                     (src/reference/cross_entropy.rs:32-57, label smoothing
+//                     included) and the lse terms of the KL, writes the row's
+//                     constants;
+//   row_grad_kernel   one pass over the row writing the bf16 logit gradients
+//                       dlogit_s = w_s((p - a/V) - [j==y](1-a)) + kd T (p_s^T - p_t^T)
+//                       dlogit_t = w_t((p_t - a/V) - [j==y](1-a))
+//                     (the merged CE + KL gradient of src/api.rs:303-344) and,
+//                     from the p_t^T it already evaluates, the KL cross term
+//                     sum_j p_t^T (t - x)/T per 8192-column segment, so that
+//                     KL = cross + lse_s^T - lse_t^T (src/reference/kl.rs:66-127)
+//                     without another pass; finalize adds the segments in a
+//                     fixed order (deterministic).
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -29,56 +35,24 @@ namespace {
 
 constexpr float LOG2E_F = 1.4426950408889634f;
 constexpr int ROW_THREADS = 256;
+constexpr int GRAD_THREADS = 256;
+constexpr int GRAD_STEPS = kGradSegCols / (GRAD_THREADS * 8);  // 4
+
+// e^x as 2^(x * log2 e) with the PTX ex2.approx.ftz.f32 instruction; its
+// ~2^-22 relative error is far below the bf16 rounding of the gradient.
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
 struct Acc {
-  double m, d1, dT, s, sx;
+  double m, d1, dT, sx;
 };
 
-__device__ __forceinline__ Acc acc_empty() { return Acc{-INFINITY, 0.0, 0.0, 0.0, 0.0}; }
-
-// Merge of two online-softmax partial states (d1 scales with exp(dm), dT and
-// S with exp(dm / T), sx adds).
-__device__ __forceinline__ Acc acc_merge(const Acc& a, const Acc& b, double inv_t) {
-  if (a.m == -INFINITY) return Acc{b.m, b.d1, b.dT, b.s, a.sx + b.sx};
-  if (b.m == -INFINITY) return Acc{a.m, a.d1, a.dT, a.s, a.sx + b.sx};
-  const double m = a.m > b.m ? a.m : b.m;
-  const double fa1 = exp(a.m - m), fb1 = exp(b.m - m);
-  const double faT = exp((a.m - m) * inv_t), fbT = exp((b.m - m) * inv_t);
-  return Acc{m, a.d1 * fa1 + b.d1 * fb1, a.dT * faT + b.dT * fbT, a.s * faT + b.s * fbT, a.sx + b.sx};
-}
-
-__device__ __forceinline__ Acc acc_shfl_down(const Acc& a, int off) {
-  Acc r;
-  r.m = __shfl_down_sync(0xffffffffu, a.m, off);
-  r.d1 = __shfl_down_sync(0xffffffffu, a.d1, off);
-  r.dT = __shfl_down_sync(0xffffffffu, a.dT, off);
-  r.s = __shfl_down_sync(0xffffffffu, a.s, off);
-  r.sx = __shfl_down_sync(0xffffffffu, a.sx, off);
-  return r;
-}
-
-// Block-wide merge; result valid in thread 0.
-__device__ Acc block_merge(Acc a, double inv_t, Acc* sh) {
-  for (int off = 16; off > 0; off >>= 1) a = acc_merge(a, acc_shfl_down(a, off), inv_t);
-  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
-  if (l == 0) sh[w] = a;
-  __syncthreads();
-  if (w == 0) {
-    a = l < (blockDim.x >> 5) ? sh[l] : acc_empty();
-    for (int off = 16; off > 0; off >>= 1) a = acc_merge(a, acc_shfl_down(a, off), inv_t);
-  }
-  __syncthreads();
-  return a;
-}
-
-__device__ __forceinline__ Acc load_own(const float* rec, long long idx) {
+__device__ __forceinline__ Acc load_rec(const float* rec, long long idx) {
   const float4 r = reinterpret_cast<const float4*>(rec)[idx];
-  return Acc{r.x, r.y, r.z, 0.0, r.w};
-}
-__device__ __forceinline__ Acc load_pair(const float* rec, long long idx) {
-  const float4 r0 = reinterpret_cast<const float4*>(rec)[idx * 2];
-  const float4 r1 = reinterpret_cast<const float4*>(rec)[idx * 2 + 1];
-  return Acc{r0.x, r0.y, r0.z, r0.w, r1.x};
+  return Acc{r.x, r.y, r.z, r.w};
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
@@ -86,8 +60,79 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
   return static_cast<uint32_t>(__bfloat16_as_ushort(ha)) | (static_cast<uint32_t>(__bfloat16_as_ushort(hb)) << 16);
 }
 
-// Per-row constants handed from the statistics kernel to the gradient
-// kernel (lse terms pre-multiplied by log2(e) for exp2).
+__device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+
+// ------------------------------------------------------ block reductions
+// Results are returned to every thread; the order of additions is fixed, so
+// the sums are deterministic.
+__device__ __forceinline__ double block_max(double v, double* sh) {
+  for (int off = 16; off > 0; off >>= 1) v = fmax(v, __shfl_xor_sync(0xffffffffu, v, off));
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) sh[w] = v;
+  __syncthreads();
+  v = sh[0];
+  for (int k = 1; k < static_cast<int>(blockDim.x >> 5); ++k) v = fmax(v, sh[k]);
+  return v;
+}
+
+template <int N>
+__device__ __forceinline__ void block_sum(double (&v)[N], double* sh) {
+#pragma unroll
+  for (int q = 0; q < N; ++q)
+    for (int off = 16; off > 0; off >>= 1) v[q] += __shfl_xor_sync(0xffffffffu, v[q], off);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = blockDim.x >> 5;
+  __syncthreads();
+  if (l == 0)
+#pragma unroll
+    for (int q = 0; q < N; ++q) sh[q * 32 + w] = v[q];
+  __syncthreads();
+#pragma unroll
+  for (int q = 0; q < N; ++q) {
+    double t = 0.0;
+    for (int k = 0; k < nw; ++k) t += sh[q * 32 + k];
+    v[q] = t;
+  }
+}
+
+constexpr int kMaxPartsPerThread = 4;
+
+// Merges the records of one row in two passes (block max, then one rescale
+// per record and plain sums) in double precision.
+__device__ Acc merge_row(const float* rec, long long row, int P, double inv_t, double* sh) {
+  Acc loc[kMaxPartsPerThread];
+  double mx = -INFINITY;
+#pragma unroll
+  for (int k = 0; k < kMaxPartsPerThread; ++k) {
+    const int p = threadIdx.x + k * blockDim.x;
+    loc[k] = p < P ? load_rec(rec, row * P + p) : Acc{-INFINITY, 0.0, 0.0, 0.0};
+    mx = fmax(mx, loc[k].m);
+  }
+  for (int p = threadIdx.x + kMaxPartsPerThread * blockDim.x; p < P; p += blockDim.x)
+    mx = fmax(mx, static_cast<double>(rec[(row * P + p) * 4]));
+  const double M = block_max(mx, sh);
+  double sums[3] = {0.0, 0.0, 0.0};  // d1, dT, sx
+#pragma unroll
+  for (int k = 0; k < kMaxPartsPerThread; ++k) {
+    if (loc[k].m != -INFINITY) {
+      sums[0] += loc[k].d1 * exp(loc[k].m - M);
+      sums[1] += loc[k].dT * exp((loc[k].m - M) * inv_t);
+    }
+    sums[2] += loc[k].sx;
+  }
+  for (int p = threadIdx.x + kMaxPartsPerThread * blockDim.x; p < P; p += blockDim.x) {
+    const Acc r = load_rec(rec, row * P + p);
+    sums[0] += r.d1 * exp(r.m - M);
+    sums[1] += r.dT * exp((r.m - M) * inv_t);
+    sums[2] += r.sx;
+  }
+  block_sum(sums, sh);
+  return Acc{M, sums[0], sums[1], sums[2]};
+}
+
+// Per-row constants handed from the statistics kernel to the gradient kernel
+// (lse terms pre-multiplied by log2(e) for exp2).
 struct RowConst {
   float c_s1, c_sT, c_tT, c_t1;
   int y;
@@ -95,25 +140,15 @@ struct RowConst {
   int pad0, pad1;
 };
 
-// ---- kernel 1: merge the records of one row, evaluate its losses, write
-// its constants. One CTA per row.
+// ---- one CTA per row: merge records, per-row losses, constants.
 __global__ void __launch_bounds__(ROW_THREADS) row_stats_kernel(const RowArgs a) {
-  __shared__ Acc sh[ROW_THREADS / 32];
+  __shared__ double sh[3 * 32];
   const int i = blockIdx.x;
-  const int P = a.n_parts;
   const double inv_t = static_cast<double>(a.inv_t);
-  const bool want_pair = a.need_kl || (a.teacher_ce && !a.teacher_ce_from_own);
-  const bool want_tow = a.teacher_ce && a.teacher_ce_from_own;
+  const bool want_t = a.need_kl || a.teacher_ce;
 
-  Acc own = acc_empty(), pr = acc_empty(), tow = acc_empty();
-  for (int p = threadIdx.x; p < P; p += blockDim.x) {
-    own = acc_merge(own, load_own(a.rec_own, static_cast<long long>(i) * P + p), inv_t);
-    if (want_pair) pr = acc_merge(pr, load_pair(a.rec_pair, static_cast<long long>(i) * P + p), inv_t);
-    if (want_tow) tow = acc_merge(tow, load_own(a.rec_own_t, static_cast<long long>(i) * P + p), inv_t);
-  }
-  own = block_merge(own, inv_t, sh);
-  if (want_pair) pr = block_merge(pr, inv_t, sh);
-  if (want_tow) tow = block_merge(tow, inv_t, sh);
+  const Acc own = merge_row(a.rec_own, i, a.n_parts, inv_t, sh);
+  const Acc ts = want_t ? merge_row(a.rec_own_t, i, a.n_parts_t, inv_t, sh) : Acc{0.0, 1.0, 1.0, 0.0};
   if (threadIdx.x != 0) return;
 
   const int64_t y64 = a.labels[i];
@@ -135,18 +170,12 @@ __global__ void __launch_bounds__(ROW_THREADS) row_stats_kernel(const RowArgs a)
   double lse_sT = 0.0, lse_tT = 0.0;
   if (a.need_kl) {
     lse_sT = own.m * inv_t + log(own.dT);
-    lse_tT = pr.m * inv_t + log(pr.dT);
-    // KL = sum p_t (log p_t - log p_s) = S / d_t + lse_s^T - lse_t^T
-    const double kl = pr.s / pr.dT + lse_sT - lse_tT;
-    const double t_sq = static_cast<double>(a.temperature * a.temperature);
-    a.kl_rows[i] = ignored ? 0.0 : kl * t_sq;
-  } else {
-    a.kl_rows[i] = 0.0;
+    lse_tT = ts.m * inv_t + log(ts.dT);
   }
+  a.kl_base_rows[i] = (a.need_kl && !ignored) ? lse_sT - lse_tT : 0.0;
 
   double lse_t1 = 0.0;
   if (a.teacher_ce) {
-    const Acc& ts = a.teacher_ce_from_own ? tow : pr;
     lse_t1 = ts.m + log(ts.d1);
     double nll_t = 0.0;
     if (!ignored) {
@@ -177,41 +206,43 @@ __global__ void __launch_bounds__(ROW_THREADS) row_stats_kernel(const RowArgs a)
 
 // Scalars shared by every element of the gradient pass.
 struct GradScalars {
-  float ws, wt, kdT, eps, ws_tgt, wt_tgt, l1, lT;
+  float ws, wt, kdT, eps, ws_tgt, wt_tgt, l1, lT, inv_t;
 };
 
-__device__ __forceinline__ void grad_elem(const GradScalars& g, const RowConst& c, bool want_kl, bool want_t,
-                                          int j, float x, float t, float& gs, float& gt) {
-  float s = g.ws * (exp2f(fmaf(x, g.l1, -c.c_s1)) - g.eps);
-  if (want_kl) s += g.kdT * (exp2f(fmaf(x, g.lT, -c.c_sT)) - exp2f(fmaf(t, g.lT, -c.c_tT)));
+// One element: the student (and teacher) logit gradient and the KL cross
+// term p_t^T (t - x) / T.
+template <bool KL, bool TGRAD>
+__device__ __forceinline__ void grad_elem(const GradScalars& g, const RowConst& c, int j, float x, float t, float& gs,
+                                          float& gt, float& cross) {
+  float s = g.ws * (fast_exp2(fmaf(x, g.l1, -c.c_s1)) - g.eps);
+  if (KL) {
+    const float pt = fast_exp2(fmaf(t, g.lT, -c.c_tT));
+    s += g.kdT * (fast_exp2(fmaf(x, g.lT, -c.c_sT)) - pt);
+    cross = fmaf(pt, (t - x) * g.inv_t, cross);
+  }
   if (j == c.y) s -= g.ws_tgt;
   float u = 0.0f;
-  if (want_t) {
-    u = g.wt * (exp2f(fmaf(t, g.l1, -c.c_t1)) - g.eps);
+  if (TGRAD) {
+    u = g.wt * (fast_exp2(fmaf(t, g.l1, -c.c_t1)) - g.eps);
     if (j == c.y) u -= g.wt_tgt;
-  }
-  if (c.ignored) {
-    s = 0.0f;
-    u = 0.0f;
   }
   gs = s;
   gt = u;
 }
 
-__device__ __forceinline__ void load_teacher8(const RowArgs& a, long long row, int j0, float (&t)[8]) {
-  if (a.teacher_is_bf16) {
-    const uint4 q = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.teacher) +
-                                                         row * a.ld_teacher + j0));
-    t[0] = __uint_as_float(q.x << 16);
-    t[1] = __uint_as_float(q.x & 0xFFFF0000u);
-    t[2] = __uint_as_float(q.y << 16);
-    t[3] = __uint_as_float(q.y & 0xFFFF0000u);
-    t[4] = __uint_as_float(q.z << 16);
-    t[5] = __uint_as_float(q.z & 0xFFFF0000u);
-    t[6] = __uint_as_float(q.w << 16);
-    t[7] = __uint_as_float(q.w & 0xFFFF0000u);
+__device__ __forceinline__ void load_teacher8(const void* teacher, bool is_bf16, long long off, float (&t)[8]) {
+  if (is_bf16) {
+    const uint4 q = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(teacher) + off));
+    t[0] = bf16_lo(q.x);
+    t[1] = bf16_hi(q.x);
+    t[2] = bf16_lo(q.y);
+    t[3] = bf16_hi(q.y);
+    t[4] = bf16_lo(q.z);
+    t[5] = bf16_hi(q.z);
+    t[6] = bf16_lo(q.w);
+    t[7] = bf16_hi(q.w);
   } else {
-    const float* tp = static_cast<const float*>(a.teacher) + row * a.ld_teacher + j0;
+    const float* tp = static_cast<const float*>(teacher) + off;
     const float4 t0 = __ldg(reinterpret_cast<const float4*>(tp));
     const float4 t1 = __ldg(reinterpret_cast<const float4*>(tp + 4));
     t[0] = t0.x; t[1] = t0.y; t[2] = t0.z; t[3] = t0.w;
@@ -219,74 +250,160 @@ __device__ __forceinline__ void load_teacher8(const RowArgs& a, long long row, i
   }
 }
 
-// ---- kernel 2: flat elementwise pass over the chunk's [n, V] logits,
-// 8 columns per thread per step (32 B fp32 student, 16/32 B teacher in;
-// 16 B bf16 gradient out per row kind), grid-stride so every SM stays busy.
-// Requires V % 8 == 0 and 16-byte aligned rows (checked by the launcher).
-__global__ void __launch_bounds__(256) row_grad_kernel_vec(const RowArgs a, const GradScalars g) {
-  const long long vecs_per_row = a.v / 8;
-  const long long total = static_cast<long long>(a.n) * vecs_per_row;
-  const bool want_kl = a.need_kl != 0;
-  const bool want_t = a.teacher_grad != 0;
-  const bool need_teacher = want_kl || want_t;
-  const RowConst* rcs = reinterpret_cast<const RowConst*>(a.row_const);
-  for (long long idx = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; idx < total;
-       idx += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const long long row = idx / vecs_per_row;
-    const int j0 = static_cast<int>(idx - row * vecs_per_row) * 8;
-    const RowConst c = rcs[row];
-    const float* xs = a.logits_s + row * a.ldl + j0;
-    const float4 x0 = __ldg(reinterpret_cast<const float4*>(xs));
-    const float4 x1 = __ldg(reinterpret_cast<const float4*>(xs + 4));
-    const float x[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-    float t[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    if (need_teacher) load_teacher8(a, row, j0, t);
-    float gs[8], gt[8];
-#pragma unroll
-    for (int k = 0; k < 8; ++k) grad_elem(g, c, want_kl, want_t, j0 + k, x[k], t[k], gs[k], gt[k]);
-    uint4 o;
-    o.x = pack_bf16x2(gs[0], gs[1]);
-    o.y = pack_bf16x2(gs[2], gs[3]);
-    o.z = pack_bf16x2(gs[4], gs[5]);
-    o.w = pack_bf16x2(gs[6], gs[7]);
-    *reinterpret_cast<uint4*>(a.dlog_s + row * a.ldd + j0) = o;
-    if (want_t) {
-      o.x = pack_bf16x2(gt[0], gt[1]);
-      o.y = pack_bf16x2(gt[2], gt[3]);
-      o.z = pack_bf16x2(gt[4], gt[5]);
-      o.w = pack_bf16x2(gt[6], gt[7]);
-      *reinterpret_cast<uint4*>(a.dlog_t + row * a.ldd + j0) = o;
+// Block sum of one float, deterministic; result valid in thread 0.
+__device__ __forceinline__ float block_sum_f(float v, float* sh) {
+  for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  if (l == 0) sh[w] = v;
+  __syncthreads();
+  float t = 0.0f;
+  if (threadIdx.x == 0)
+    for (int k = 0; k < static_cast<int>(blockDim.x >> 5); ++k) t += sh[k];
+  return t;
+}
+
+// ---- grid (segment, row): gradients of one 8192-column segment of one row.
+// VEC: V % 8 == 0 and 16-byte aligned rows (8 columns per thread step).
+template <bool VEC, bool KL, bool TGRAD>
+__global__ void __launch_bounds__(GRAD_THREADS) row_grad_kernel(const RowArgs a, const GradScalars g) {
+  __shared__ float sh[GRAD_THREADS / 32];
+  const int seg = blockIdx.x;
+  const long long row = blockIdx.y;
+  const RowConst c = reinterpret_cast<const RowConst*>(a.row_const)[row];
+  const float* xs = a.logits_s + row * a.ldl;
+  uint16_t* gs_row = a.dlog_s + row * a.ldd;
+  uint16_t* gt_row = TGRAD ? a.dlog_t + row * a.ldd : nullptr;
+  const bool need_t = KL || TGRAD;
+  const int V = a.v;
+  const int c0 = seg * kGradSegCols;
+  const int c1 = min(V, c0 + kGradSegCols);
+  float cross = 0.0f;
+  if (c.ignored) {
+    // ignored row: zero gradients, no KL contribution
+    if (VEC) {
+      for (int j0 = c0 + threadIdx.x * 8; j0 < c1; j0 += GRAD_THREADS * 8) {
+        *reinterpret_cast<uint4*>(gs_row + j0) = make_uint4(0, 0, 0, 0);
+        if (TGRAD) *reinterpret_cast<uint4*>(gt_row + j0) = make_uint4(0, 0, 0, 0);
+      }
+    } else {
+      for (int j = c0 + threadIdx.x; j < c1; j += GRAD_THREADS) {
+        gs_row[j] = 0;
+        if (TGRAD) gt_row[j] = 0;
+      }
     }
+  } else if (VEC) {
+#pragma unroll
+    for (int step = 0; step < GRAD_STEPS; ++step) {
+      const int j0 = c0 + (step * GRAD_THREADS + threadIdx.x) * 8;
+      if (j0 < c1) {
+        const float4 x0 = __ldg(reinterpret_cast<const float4*>(xs + j0));
+        const float4 x1 = __ldg(reinterpret_cast<const float4*>(xs + j0 + 4));
+        const float x[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+        float t[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        if (need_t) load_teacher8(a.teacher, a.teacher_is_bf16, row * a.ld_teacher + j0, t);
+        float gsv[8], gtv[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) grad_elem<KL, TGRAD>(g, c, j0 + k, x[k], t[k], gsv[k], gtv[k], cross);
+        *reinterpret_cast<uint4*>(gs_row + j0) = make_uint4(pack_bf16x2(gsv[0], gsv[1]), pack_bf16x2(gsv[2], gsv[3]),
+                                                            pack_bf16x2(gsv[4], gsv[5]), pack_bf16x2(gsv[6], gsv[7]));
+        if (TGRAD)
+          *reinterpret_cast<uint4*>(gt_row + j0) =
+              make_uint4(pack_bf16x2(gtv[0], gtv[1]), pack_bf16x2(gtv[2], gtv[3]), pack_bf16x2(gtv[4], gtv[5]),
+                         pack_bf16x2(gtv[6], gtv[7]));
+      }
+    }
+  } else {
+    for (int j = c0 + threadIdx.x; j < c1; j += GRAD_THREADS) {
+      float t = 0.0f;
+      if (need_t) {
+        if (a.teacher_is_bf16) {
+          const uint16_t b = static_cast<const uint16_t*>(a.teacher)[row * a.ld_teacher + j];
+          t = __uint_as_float(static_cast<uint32_t>(b) << 16);
+        } else {
+          t = static_cast<const float*>(a.teacher)[row * a.ld_teacher + j];
+        }
+      }
+      float gs, gt;
+      grad_elem<KL, TGRAD>(g, c, j, xs[j], t, gs, gt, cross);
+      gs_row[j] = __bfloat16_as_ushort(__float2bfloat16_rn(gs));
+      if (TGRAD) gt_row[j] = __bfloat16_as_ushort(__float2bfloat16_rn(gt));
+    }
+  }
+  if (KL) {
+    const float tot = block_sum_f(cross, sh);
+    if (threadIdx.x == 0) a.s_part[row * a.nseg + seg] = tot;
   }
 }
 
-// Scalar fallback for vocabularies that are not a multiple of 8.
-__global__ void __launch_bounds__(256) row_grad_kernel_scalar(const RowArgs a, const GradScalars g) {
-  const long long total = static_cast<long long>(a.n) * a.v;
-  const bool want_kl = a.need_kl != 0;
-  const bool want_t = a.teacher_grad != 0;
-  const bool need_teacher = want_kl || want_t;
-  const RowConst* rcs = reinterpret_cast<const RowConst*>(a.row_const);
-  for (long long idx = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; idx < total;
-       idx += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const long long row = idx / a.v;
-    const int j = static_cast<int>(idx - row * a.v);
-    const RowConst c = rcs[row];
-    const float x = a.logits_s[row * a.ldl + j];
-    float t = 0.0f;
-    if (need_teacher) {
-      if (a.teacher_is_bf16) {
-        const uint16_t b = static_cast<const uint16_t*>(a.teacher)[row * a.ld_teacher + j];
-        t = __uint_as_float(static_cast<uint32_t>(b) << 16);
-      } else {
-        t = static_cast<const float*>(a.teacher)[row * a.ld_teacher + j];
+__device__ __forceinline__ float teacher_at(const void* teacher, int is_bf16, long long idx) {
+  return is_bf16 ? __uint_as_float(static_cast<uint32_t>(static_cast<const uint16_t*>(teacher)[idx]) << 16)
+                 : static_cast<const float*>(teacher)[idx];
+}
+
+// ---- teacher statistics pre-pass over given teacher logits: one CTA per
+// row; every thread keeps four independent 16-byte loads in flight.
+__global__ void __launch_bounds__(ROW_THREADS) teacher_stats_kernel(const void* teacher, long long ld, int is_bf16,
+                                                                    int v, float inv_t, float* rec) {
+  __shared__ double sh[3 * 32];
+  const long long row = blockIdx.x;
+  const bool vec = (v % 8 == 0) && ((ld * (is_bf16 ? 2 : 4)) % 16 == 0) &&
+                   ((reinterpret_cast<uintptr_t>(teacher) & 15) == 0);
+  const float lt = LOG2E_F * inv_t;
+  float m = -INFINITY, d1 = 0.f, dT = 0.f, sx = 0.f;
+  if (vec) {
+    constexpr int U = 4;  // vectors of 8 per thread per iteration
+    for (int base = threadIdx.x * 8; base < v; base += ROW_THREADS * 8 * U) {
+      float t[U][8];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int j0 = base + u * ROW_THREADS * 8;
+        if (j0 < v) {
+          load_teacher8(teacher, is_bf16, row * ld + j0, t[u]);
+        } else {
+#pragma unroll
+          for (int k = 0; k < 8; ++k) t[u][k] = -INFINITY;
+        }
       }
+      float vm = -INFINITY;
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+#pragma unroll
+        for (int k = 0; k < 8; ++k) vm = fmaxf(vm, t[u][k]);
+      if (vm > m) {
+        const float dm = m - vm;  // -inf on the first block: factors 0
+        d1 *= fast_exp2(dm * LOG2E_F);
+        dT *= fast_exp2(dm * lt);
+        m = vm;
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          if (t[u][k] != -INFINITY) {
+            const float x = t[u][k] - m;
+            d1 += fast_exp2(x * LOG2E_F);
+            dT += fast_exp2(x * lt);
+            sx += t[u][k];
+          }
+        }
     }
-    float gs, gt;
-    grad_elem(g, c, want_kl, want_t, j, x, t, gs, gt);
-    a.dlog_s[row * a.ldd + j] = __bfloat16_as_ushort(__float2bfloat16_rn(gs));
-    if (want_t) a.dlog_t[row * a.ldd + j] = __bfloat16_as_ushort(__float2bfloat16_rn(gt));
+  } else {
+    for (int j = threadIdx.x; j < v; j += ROW_THREADS) m = fmaxf(m, teacher_at(teacher, is_bf16, row * ld + j));
+    for (int j = threadIdx.x; j < v; j += ROW_THREADS) {
+      const float t = teacher_at(teacher, is_bf16, row * ld + j);
+      d1 += fast_exp2((t - m) * LOG2E_F);
+      dT += fast_exp2((t - m) * lt);
+      sx += t;
+    }
   }
+  const double M = block_max(static_cast<double>(m), sh);
+  const double f1 = m == -INFINITY ? 0.0 : exp(static_cast<double>(m) - M);
+  const double fT = m == -INFINITY ? 0.0 : exp((static_cast<double>(m) - M) * static_cast<double>(inv_t));
+  double sums[3] = {static_cast<double>(d1) * f1, static_cast<double>(dT) * fT, static_cast<double>(sx)};
+  block_sum(sums, sh);
+  if (threadIdx.x == 0)
+    reinterpret_cast<float4*>(rec)[row] = make_float4(static_cast<float>(M), static_cast<float>(sums[0]),
+                                                      static_cast<float>(sums[1]), static_cast<float>(sums[2]));
 }
 
 // ------------------------------------------------------------ label pass
@@ -333,15 +450,20 @@ __global__ void target_flags_kernel(const int64_t* labels, long long bt, long lo
 
 // ------------------------------------------------------------- finalize
 __global__ void __launch_bounds__(1024) finalize_kernel(const float* nll_s, const float* nll_t,
-                                                        const double* kl_rows, long long bt,
-                                                        const float* mean_scale, float w_s, float w_t, float kd,
-                                                        float* scalars) {
+                                                        const double* kl_base, const float* s_part, int nseg,
+                                                        double t_sq, long long bt, const float* mean_scale,
+                                                        float w_s, float w_t, float kd, float* scalars) {
   __shared__ double sh[3][32];
   double s0 = 0.0, s1 = 0.0, s2 = 0.0;
   for (long long r = threadIdx.x; r < bt; r += blockDim.x) {
     s0 += static_cast<double>(nll_s[r]);
     s1 += static_cast<double>(nll_t[r]);
-    s2 += kl_rows[r];
+    if (nseg > 0) {
+      // ignored rows have kl_base 0 and no cross-term segments
+      double cross = 0.0;
+      for (int k = 0; k < nseg; ++k) cross += static_cast<double>(s_part[r * nseg + k]);
+      s2 += (kl_base[r] + cross) * t_sq;
+    }
   }
   for (int off = 16; off > 0; off >>= 1) {
     s0 += __shfl_down_sync(0xffffffffu, s0, off);
@@ -387,6 +509,16 @@ __global__ void f32_to_bf16_kernel(const float* src, long long rows, long long c
   }
 }
 
+template <bool VEC>
+void launch_grad(const RowArgs& a, const GradScalars& g, cudaStream_t stream) {
+  const dim3 grid(static_cast<unsigned>((a.v + kGradSegCols - 1) / kGradSegCols), static_cast<unsigned>(a.n));
+  const bool kl = a.need_kl != 0, tg = a.teacher_grad != 0;
+  if (kl && tg) row_grad_kernel<VEC, true, true><<<grid, GRAD_THREADS, 0, stream>>>(a, g);
+  else if (kl) row_grad_kernel<VEC, true, false><<<grid, GRAD_THREADS, 0, stream>>>(a, g);
+  else if (tg) row_grad_kernel<VEC, false, true><<<grid, GRAD_THREADS, 0, stream>>>(a, g);
+  else row_grad_kernel<VEC, false, false><<<grid, GRAD_THREADS, 0, stream>>>(a, g);
+}
+
 }  // namespace
 
 void launch_rows(const RowArgs& a, cudaStream_t stream) {
@@ -403,19 +535,20 @@ void launch_rows(const RowArgs& a, cudaStream_t stream) {
   g.wt_tgt = a.w_t * one_minus_a;
   g.l1 = LOG2E_F;
   g.lT = LOG2E_F * a.inv_t;
-  int dev = 0, sms = 148;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  g.inv_t = a.inv_t;
   const long long tsz = a.teacher_is_bf16 ? 2 : 4;
-  const bool vec = (a.v % 8 == 0) && (a.ldl % 4 == 0) && (a.ldd % 8 == 0) &&
-                   ((a.ld_teacher * tsz) % 16 == 0) && ((reinterpret_cast<uintptr_t>(a.teacher) & 15) == 0) &&
+  const bool teacher_ok = !(a.need_kl || a.teacher_grad) ||
+                          (((a.ld_teacher * tsz) % 16 == 0) && ((reinterpret_cast<uintptr_t>(a.teacher) & 15) == 0));
+  const bool vec = (a.v % 8 == 0) && (a.ldl % 4 == 0) && (a.ldd % 8 == 0) && teacher_ok &&
                    ((reinterpret_cast<uintptr_t>(a.logits_s) & 15) == 0);
-  const long long work = vec ? static_cast<long long>(a.n) * (a.v / 8) : static_cast<long long>(a.n) * a.v;
-  long long blocks = (work + 255) / 256;
-  const long long cap = static_cast<long long>(sms) * 8;
-  if (blocks > cap) blocks = cap;
-  if (vec) row_grad_kernel_vec<<<static_cast<int>(blocks), 256, 0, stream>>>(a, g);
-  else row_grad_kernel_scalar<<<static_cast<int>(blocks), 256, 0, stream>>>(a, g);
+  if (vec) launch_grad<true>(a, g, stream);
+  else launch_grad<false>(a, g, stream);
+}
+
+void launch_teacher_stats(const void* teacher, long long ld, int is_bf16, int n, int v, float inv_t, float* rec,
+                          cudaStream_t stream) {
+  if (n <= 0) return;
+  teacher_stats_kernel<<<n, ROW_THREADS, 0, stream>>>(teacher, ld, is_bf16, v, inv_t, rec);
 }
 
 void launch_label_prep(const int64_t* labels, long long bt, long long v, int64_t ignore_index, int reduction_sum,
@@ -432,9 +565,11 @@ void launch_target_flags(const int64_t* labels, long long bt, long long v, int64
   target_flags_kernel<<<blocks, 256, 0, stream>>>(labels, bt, v, ignore_index, target_flags);
 }
 
-void launch_finalize(const float* nll_s, const float* nll_t, const double* kl_rows, long long bt,
-                     const float* mean_scale, float w_s, float w_t, float kd, float* scalars, cudaStream_t stream) {
-  finalize_kernel<<<1, 1024, 0, stream>>>(nll_s, nll_t, kl_rows, bt, mean_scale, w_s, w_t, kd, scalars);
+void launch_finalize(const float* nll_s, const float* nll_t, const double* kl_base, const float* s_part, int nseg,
+                     double t_sq, long long bt, const float* mean_scale, float w_s, float w_t, float kd,
+                     float* scalars, cudaStream_t stream) {
+  finalize_kernel<<<1, 1024, 0, stream>>>(nll_s, nll_t, kl_base, s_part, nseg, t_sq, bt, mean_scale, w_s, w_t, kd,
+                                          scalars);
 }
 
 void launch_f32_to_bf16(const float* src, long long rows, long long cols, uint16_t* dst, long long ld,
