@@ -231,6 +231,13 @@ ORDA_API int orda_context_phase_times(OrdaContext* ctx, double* ms_out, uint64_t
 ORDA_API void orda_context_reset_timing(OrdaContext* ctx);
 /* Total kernels this context has launched (all calls, timing on or off). */
 ORDA_API uint64_t orda_context_launch_count(const OrdaContext* ctx);
+/* Failure-detection self-test: launches a one-warp kernel whose bounded
+ * device wait (the same mechanism every kernel uses) on a barrier that nothing
+ * completes gives up after limit_us microseconds (at most 1 s) and records a
+ * timeout; orda_context_check then returns ORDA_ERR_TIMEOUT and the context
+ * stays usable for further calls. */
+ORDA_API int orda_context_selftest_bounded_wait(OrdaContext* ctx, uint32_t limit_us, void* stream, char* err,
+                                                size_t err_len);
 /* Test hook for the OOM ladder: the next `count` workspace allocations fail
  * as if cudaMalloc had returned cudaErrorMemoryAllocation. */
 ORDA_API void orda_context_inject_alloc_failures(OrdaContext* ctx, int count);

@@ -89,12 +89,18 @@ struct Flags {
 struct WsLayout {
   size_t logits = 0, rec_own = 0, rec_own_t = 0, dlog_s = 0, dlog_t = 0, nll_s = 0, nll_t = 0, kl_base = 0,
          s_part = 0, flags = 0, row_const = 0, total = 0;
-  size_t ldv = 0, ldd = 0, parts = 0, parts_t = 0, nseg = 0, cs = 0, group_rows = 0;
+  size_t ldv = 0, ldd = 0, parts = 0, parts_t = 0, nseg = 0, cs = 0, fwd_rows = 0, group_rows = 0;
 };
 
-WsLayout make_layout(const DevInputs& in, const Flags& f, size_t cs, size_t group_rows) {
+// Workspace for one rung of the OOM ladder. `fwd_rows` rows (a whole number
+// of the plan's chunks, fwd_rows <= group_rows) go through each launch of the
+// forward-side kernels (logits GEMMs, statistics, gradient pass);
+// `group_rows` rows of bf16 logit gradients are kept for each backward GEMM
+// launch. Both are chunk-invariant groupings of the resolver's plan.
+WsLayout make_layout(const DevInputs& in, const Flags& f, size_t cs, size_t fwd_rows, size_t group_rows) {
   WsLayout L;
   L.cs = cs;
+  L.fwd_rows = fwd_rows;
   L.group_rows = group_rows;
   L.ldv = round_up(in.v, 8);
   L.ldd = round_up(in.v, 8);
@@ -107,9 +113,9 @@ WsLayout make_layout(const DevInputs& in, const Flags& f, size_t cs, size_t grou
     off = round_up(off + bytes, 256);
     return o;
   };
-  L.logits = take((f.teacher_rows ? 2 : 1) * cs * L.ldv * sizeof(float));
-  L.rec_own = take(cs * L.parts * 16);
-  L.rec_own_t = take(f.need_teacher ? cs * L.parts_t * 16 : 0);
+  L.logits = take((f.teacher_rows ? 2 : 1) * fwd_rows * L.ldv * sizeof(float));
+  L.rec_own = take(fwd_rows * L.parts * 16);
+  L.rec_own_t = take(f.need_teacher ? fwd_rows * L.parts_t * 16 : 0);
   L.dlog_s = take(group_rows * L.ldd * 2);
   L.dlog_t = take(f.teacher_grad ? group_rows * L.ldd * 2 : 0);
   L.nll_s = take(in.bt * sizeof(float));
@@ -117,7 +123,7 @@ WsLayout make_layout(const DevInputs& in, const Flags& f, size_t cs, size_t grou
   L.kl_base = take(in.bt * sizeof(double));
   L.s_part = take(in.bt * L.nseg * sizeof(float));
   L.flags = take(f.quant ? in.v : 0);
-  L.row_const = take(cs * kRowConstBytes);
+  L.row_const = take(fwd_rows * kRowConstBytes);
   L.total = off;
   return L;
 }
@@ -151,15 +157,18 @@ struct AllocTry {
   WsLayout layout;
 };
 
-// Workspace for a rung of the OOM ladder: the chunk buffers plus the dlogits
-// group buffer, whose depth (chunks per backward-GEMM group) is the largest
-// that keeps the group within 60% of the memory this call may use.
+// Allocation for a rung of the OOM ladder: the largest forward and backward
+// groups (in whole chunks) whose workspace stays within 60% of the memory
+// this call may use; every chunk in one group when that fits, which holds
+// for all BASELINE configurations on a 180 GB B200.
 int try_alloc_cb(size_t num_chunks, size_t chunk_size, void* user) {
   AllocTry* t = static_cast<AllocTry*>(user);
-  // Fast path (no device query): the held workspace already fits a group of
-  // every chunk.
+  const size_t bt = t->in->bt;
+  const size_t all_rows = std::min(num_chunks * chunk_size, bt);
+  // Fast path (no device query): the held workspace already fits one group
+  // of every chunk.
   {
-    const WsLayout full = make_layout(*t->in, *t->f, chunk_size, std::min(num_chunks * chunk_size, t->in->bt));
+    const WsLayout full = make_layout(*t->in, *t->f, chunk_size, all_rows, all_rows);
     if (t->ctx->inject_fail <= 0 && t->ctx->ws_bytes >= full.total) {
       t->layout = full;
       return 0;
@@ -167,14 +176,22 @@ int try_alloc_cb(size_t num_chunks, size_t chunk_size, void* user) {
   }
   size_t free_b = 0, total_b = 0;
   cudaMemGetInfo(&free_b, &total_b);
-  const size_t avail = free_b + t->ctx->ws_bytes;
-  const WsLayout base = make_layout(*t->in, *t->f, chunk_size, 0);
-  const size_t per_chunk = chunk_size * base.ldd * 2 * (t->f->teacher_grad ? 2 : 1);
-  size_t g = num_chunks;
-  const size_t budget = avail > base.total ? static_cast<size_t>((avail - base.total) * 0.6) : 0;
-  if (per_chunk > 0) g = std::min(num_chunks, std::max<size_t>(1, budget / per_chunk));
-  const size_t group_rows = std::min(g * chunk_size, t->in->bt);
-  WsLayout L = make_layout(*t->in, *t->f, chunk_size, group_rows);
+  const size_t budget = static_cast<size_t>((free_b + t->ctx->ws_bytes) * 0.6);
+  WsLayout L = make_layout(*t->in, *t->f, chunk_size, chunk_size, chunk_size);
+  for (size_t g = num_chunks; g >= 1; g = g / 2) {
+    bool found = false;
+    for (size_t fw = g; fw >= 1; fw = fw / 2) {
+      const WsLayout c = make_layout(*t->in, *t->f, chunk_size, std::min(fw * chunk_size, bt),
+                                     std::min(g * chunk_size, bt));
+      if (c.total <= budget) {
+        L = c;
+        found = true;
+        break;
+      }
+      if (fw == 1) break;
+    }
+    if (found || g == 1) break;
+  }
   if (ensure_ws(t->ctx, L.total) != cudaSuccess) return 1;
   t->layout = L;
   return 0;
@@ -284,7 +301,7 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
 
   uint8_t* ws = static_cast<uint8_t*>(ctx->ws);
   float* logits = reinterpret_cast<float*>(ws + L.logits);
-  float* logits_t = logits + L.cs * L.ldv;
+  float* logits_t = logits + L.fwd_rows * L.ldv;
   float* rec_own = reinterpret_cast<float*>(ws + L.rec_own);
   float* rec_own_t = reinterpret_cast<float*>(ws + L.rec_own_t);
   uint16_t* dlog_s = reinterpret_cast<uint16_t*>(ws + L.dlog_s);
@@ -311,13 +328,13 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
 
   const float inv_t = 1.0f / f.temperature;
   const char* why = nullptr;
-  const size_t cs = used.chunk_size;
+  const size_t fwd_rows = L.fwd_rows;
   const size_t group_rows = L.group_rows;
   const size_t t_esz = in.t_logits_bf16 ? 2 : 4;
   for (size_t g0 = 0; g0 < bt; g0 += group_rows) {
     const size_t g1 = std::min(g0 + group_rows, bt);
-    for (size_t s = g0; s < g1; s += cs) {
-      const size_t n = std::min(cs, g1 - s);
+    for (size_t s = g0; s < g1; s += fwd_rows) {
+      const size_t n = std::min(fwd_rows, g1 - s);
       const void* t_rows = live_teacher ? static_cast<const void*>(logits_t)
                                         : static_cast<const void*>(static_cast<const uint8_t*>(in.t_logits) +
                                                                    s * in.ld_t_logits * t_esz);
@@ -834,6 +851,23 @@ void orda_context_reset_timing(OrdaContext* ctx) {
 }
 
 uint64_t orda_context_launch_count(const OrdaContext* ctx) { return ctx ? ctx->launches : 0; }
+
+int orda_context_selftest_bounded_wait(OrdaContext* ctx, uint32_t limit_us, void* stream, char* err,
+                                       size_t err_len) {
+  if (!ctx || limit_us == 0 || limit_us > 1000000) {
+    set_error(err, err_len, "invalid argument (limit_us must be in (0, 1e6])");
+    return ORDA_ERR_INVALID;
+  }
+  std::lock_guard<std::mutex> lock(ctx->mu);
+  cudaSetDevice(ctx->device);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemsetAsync(ctx->d_words, 0, sizeof(int), st);
+  if (e == cudaSuccess) e = launch_bounded_wait_selftest(ctx->d_words, static_cast<uint64_t>(limit_us) * 1000, st);
+  if (e != cudaSuccess) return cuda_fail(e, "bounded-wait self-test", err, err_len);
+  ctx->launches += 1;
+  ctx->last_stream = st;
+  return ORDA_OK;
+}
 
 // ------------------------------------------------------------ host-Mat entry
 

@@ -126,4 +126,8 @@ void launch_quant(float* grad_w, long long v, long long h, long long ld, const u
 void launch_target_flags(const int64_t* labels, long long bt, long long v, int64_t ignore_index,
                          uint8_t* target_flags, cudaStream_t stream);
 
+// One-warp kernel whose bounded wait on a never-completed mbarrier expires
+// after limit_ns and records DEV_TIMEOUT_SELFTEST in *status.
+cudaError_t launch_bounded_wait_selftest(int* status, uint64_t limit_ns, cudaStream_t stream);
+
 }  // namespace orda

@@ -24,6 +24,7 @@ enum DeviceStatus : int {
   DEV_TIMEOUT_EPILOGUE = 0x103,
   DEV_TIMEOUT_DRAIN = 0x104,
   DEV_LABEL_RANGE = 0x201,
+  DEV_TIMEOUT_SELFTEST = 0x301,
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -69,7 +70,8 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity
 // Bounded wait for the phase with the given parity to complete. Returns false
 // (and records `code` in *status) when the time limit expires or when another
 // role of the kernel has already recorded a failure.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code,
+                                          uint64_t limit_ns = ORDA_WAIT_LIMIT_NS) {
   const uint32_t addr = smem_u32(bar);
   if (mbar_try_wait(addr, parity)) return true;
   const uint64_t t0 = global_timer_ns();
@@ -78,7 +80,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
     for (int i = 0; i < 32; ++i)
       if (mbar_try_wait(addr, parity)) return true;
     if (*(volatile int*)status != DEV_OK) return false;
-    if (global_timer_ns() - t0 > ORDA_WAIT_LIMIT_NS) {
+    if (global_timer_ns() - t0 > limit_ns) {
       atomicCAS(status, DEV_OK, code);
       return false;
     }

@@ -193,6 +193,7 @@ SIGNATURES = {
     "orda_context_phase_times": (C.c_int, [C.c_void_p, C.POINTER(C.c_double), C.POINTER(C.c_uint64)]),
     "orda_context_reset_timing": (None, [C.c_void_p]),
     "orda_context_launch_count": (C.c_uint64, [C.c_void_p]),
+    "orda_context_selftest_bounded_wait": (C.c_int, [C.c_void_p, C.c_uint32, C.c_void_p, C.c_char_p, C.c_size_t]),
     "orda_distillation_loss_device": (
         C.c_int,
         [

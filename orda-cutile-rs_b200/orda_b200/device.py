@@ -59,6 +59,11 @@ class DeviceContext:
     def launch_count(self) -> int:
         return int(_lib().orda_context_launch_count(self.handle))
 
+    def selftest_bounded_wait(self, limit_us: int = 50000, stream=None) -> None:
+        """Runs the bounded-wait self-test kernel (a wait that expires)."""
+        buf = _abi.err_buf()
+        _check(_lib().orda_context_selftest_bounded_wait(self.handle, limit_us, _stream(stream), buf, len(buf)), buf)
+
     def __enter__(self):
         return self
 

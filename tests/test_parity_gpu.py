@@ -243,6 +243,34 @@ def test_device_label_range_error(ob):
             ctx.check()
 
 
+def test_bounded_wait_expiry_is_reported_and_context_survives(ob, c1):
+    """A device wait that nothing completes gives up after its limit (50 ms
+    here), the context reports a timeout, and the same context then computes
+    a correct loss: failure detection without a GPU fault."""
+    import time
+
+    from orda_b200.device import DeviceContext, distillation_loss_device
+
+    s, w, labs, t = c1
+    opts = ob.LossOptions(kd_weight=0.4, temperature=1.5)
+    host = ob.distillation_loss(s, w, labs, t, opts)
+    with DeviceContext(0) as ctx:
+        t0 = time.perf_counter()
+        ctx.selftest_bounded_wait(50000)
+        with pytest.raises(ob.OrdaError, match="bounded device wait expired"):
+            ctx.check()
+        waited = time.perf_counter() - t0
+        d = distillation_loss_device(
+            ctx, torch.from_numpy(s.a).cuda().bfloat16(), torch.from_numpy(w.a).cuda().bfloat16(),
+            torch.tensor(labs, dtype=torch.int64, device="cuda"), ob.TeacherMode.Tied,
+            teacher_hidden=torch.from_numpy(t.hidden.a).cuda().bfloat16(), opts=opts)
+        torch.cuda.synchronize()
+        ctx.check()
+        sc = d.scalars.cpu().numpy()
+    assert 0.04 <= waited < 5.0
+    assert np.allclose(sc, [host.loss, host.student_ce, host.teacher_ce, host.kl], rtol=1e-6, atol=0)
+
+
 # ------------------------------------------------------- BASELINE subsets
 
 def _subset_case(ob, cfg, rows, gen):
