@@ -1,25 +1,37 @@
 // gemm_sm100.cu -- persistent bf16 tensor-core GEMM for sm_100a.
 //
 // C[M,N] = op(A) @ op(B)^T with fp32 accumulation in TMEM.
-//   * TMA (cp.async.bulk.tensor, 128-byte swizzle) stages 128x64 A tiles and
-//     256x64 B tiles through a 4-deep shared-memory ring (48 KB per stage);
-//   * one thread issues tcgen05.mma (M=128, N=256, K=16) into one of two
-//     128x256 fp32 TMEM accumulators (all 512 TMEM columns), so the epilogue
-//     of tile i overlaps the main loop of tile i+1;
+//   * TMA (cp.async.bulk.tensor, 128-byte swizzle) stages 64-deep K slices of
+//     A and B through a shared-memory ring;
+//   * one thread issues tcgen05.mma (K=16 per instruction) into one of two
+//     fp32 TMEM accumulators of 128 lanes x 256 columns (all 512 TMEM
+//     columns), so the epilogue of tile i overlaps the main loop of tile i+1;
 //   * eight epilogue warps read the accumulator with tcgen05.ld (each warp
 //     owns one 32-lane TMEM quadrant and one 128-column half);
-//   * one CTA per SM walks the tile list (persistent scheduling).
+//   * persistent scheduling: each CTA (or CTA pair) walks the tile list.
+// Two tile shapes share one kernel body:
+//   CG = 1: one CTA computes a 128 x 256 tile (A 16 KB + B 32 KB per stage,
+//           4 stages);
+//   CG = 2: a CTA pair (cluster of 2, tcgen05 cta_group::2) computes a
+//           256 x 256 tile: each CTA stages its 128 rows of A and half of the
+//           256 rows of B (16 KB + 16 KB per stage, 6 stages), the leader
+//           issues M=256 MMAs that read both CTAs' shared memory, and each
+//           CTA's TMEM receives its 128 rows. Per CTA this halves the B
+//           traffic into shared memory for the same math.
 // Operands may be K-major ([rows, K] row-major) or MN-major ([K, rows]),
 // which covers the three GEMMs of the distillation loss without transposes:
 //   logits = h @ W^T      (A K-major, B K-major)
 //   grad_h = dlogits @ W  (A K-major, B MN-major)
 //   grad_W = dlogits^T @ h (A MN-major, B MN-major)
-// Epilogues: plain scaled store, or the logits epilogue that writes fp32
-// logits and per-(row, 128-column part) online-softmax statistics (max,
-// sum exp(x-m), sum exp((x-m)/T), sum x) from the fp32 accumulators, so the
-// loss needs no separate reduction pass over the logits.
+// Epilogues: plain scaled store (or TMA reduce-add), or the logits epilogue
+// that writes fp32 logits and per-(row, 128-column part) online-softmax
+// statistics (max, sum exp(x-m), sum exp((x-m)/T), sum x) from the fp32
+// accumulators, so the loss needs no separate reduction pass over the logits.
+// L2 policies: the operand that is small and reused by every tile is loaded
+// evict-last, large streamed outputs are stored evict-first.
 //
-// No TMA multicast is used anywhere (the same kernels serve multi-GPU runs).
+// No TMA load uses cluster multicast (the same kernels serve multi-GPU runs);
+// the CTA pair's loads each land in their own CTA.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cudaTypedefs.h>
@@ -27,6 +39,7 @@
 
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <atomic>
 #include <mutex>
@@ -38,13 +51,8 @@ namespace orda {
 
 namespace {
 
-constexpr int BM = 128;
-constexpr int BN = 256;
-constexpr int BK = 64;
-constexpr int STAGES = 4;
-constexpr int A_STAGE_BYTES = BM * BK * 2;  // 16 KB
-constexpr int B_STAGE_BYTES = BN * BK * 2;  // 32 KB
-constexpr int STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
+constexpr int BN = 256;  // tile columns (N)
+constexpr int BK = 64;   // K slice per stage (128 bytes of bf16)
 constexpr int NUM_THREADS = 384;  // warp 0 TMA, 1 MMA, 2 TMEM, 3 idle, 4..11 epilogue
 constexpr int EPI_WARP0 = 4;
 constexpr int NUM_EPI_WARPS = 8;
@@ -52,30 +60,50 @@ constexpr int TMEM_COLS = 512;
 // Per epilogue warp: one 32 x 32 fp32 output chunk staged for a TMA store.
 constexpr int OUT_STAGE_BYTES = 32 * 32 * 4;
 constexpr int OUT_BYTES = NUM_EPI_WARPS * OUT_STAGE_BYTES;  // 32 KB
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + OUT_BYTES + 1024 /*align*/ + 256 /*barriers*/;
-static_assert(SMEM_BYTES <= 232448, "shared memory over the sm_100 opt-in limit");
 constexpr float LOG2E = 1.4426950408889634f;
+
+template <int CG>
+struct TileCfg {
+  static constexpr int TILE_M = 128 * CG;     // rows of C per tile
+  static constexpr int B_ROWS = BN / CG;      // B rows staged by one CTA
+  static constexpr int A_STAGE = 128 * BK * 2;
+  static constexpr int B_STAGE = B_ROWS * BK * 2;
+  static constexpr int STAGE = A_STAGE + B_STAGE;
+  static constexpr int STAGES = CG == 2 ? 6 : 4;
+  static constexpr int SMEM = STAGES * STAGE + OUT_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  static_assert(SMEM <= 232448, "shared memory over the sm_100 opt-in limit");
+  static_assert((2 * STAGES + 5) * 8 + 4 <= 256, "barrier area");
+};
 
 struct KParams {
   int M, N;
-  int m_blocks, n_blocks, num_tiles;
+  int m_blocks, n_blocks, num_tiles;  // m_blocks in units of TILE_M
   int raster_n_fastest;
+  int group_m;     // M-fastest raster: tiles walk groups of group_m M blocks
   int nseg;
   int seg_kblocks[2];
   int* status;
-  int prefetch_b;  // L2 prefetch distance (k-blocks) for a K-major B operand; 0 = off
   int tma_store;   // output written through the staging buffers + TMA
   int tma_reduce;  // TMA reduce-add into the output (beta == 1)
+  int pol_a, pol_b, pol_c;  // L2 policy kinds (0 normal, 1 evict-first, 2 evict-last)
   EpiArgs e;
 };
 
+// Tile index -> (M block, N block). N-fastest: the N blocks of one M block
+// are consecutive. Otherwise M-fastest inside groups of group_m M blocks, so
+// a wave of tiles shares a few B tiles and a bounded slab of A.
 __device__ __forceinline__ void tile_coords(const KParams& p, int tile, int& mb, int& nb) {
   if (p.raster_n_fastest) {
     nb = tile % p.n_blocks;
     mb = tile / p.n_blocks;
   } else {
-    mb = tile % p.m_blocks;
-    nb = tile / p.m_blocks;
+    const int per_group = p.group_m * p.n_blocks;
+    const int g = tile / per_group;
+    const int first_m = g * p.group_m;
+    const int gm = min(p.group_m, p.m_blocks - first_m);
+    const int r = tile - g * per_group;
+    mb = first_m + r % gm;
+    nb = r / gm;
   }
 }
 
@@ -185,7 +213,8 @@ __device__ __forceinline__ void logits_chunk_any(const EpiArgs& e, long long gro
 // output tensor map, then one lane issues the TMA store (or reduce-add). The
 // buffer is reused only after the previous store has read it.
 __device__ __forceinline__ void stage_and_store(uint8_t* buf, int lane, const uint32_t (&r)[32], float alpha,
-                                                const CUtensorMap* map, int x, int y, bool reduce) {
+                                                const CUtensorMap* map, int x, int y, bool reduce,
+                                                uint64_t policy) {
   if (lane == 0) bulk_wait_read_all();
   __syncwarp();
 #pragma unroll
@@ -197,42 +226,49 @@ __device__ __forceinline__ void stage_and_store(uint8_t* buf, int lane, const ui
   fence_proxy_async_smem();
   __syncwarp();
   if (lane == 0) {
-    if (reduce) tma_reduce_add_2d(map, buf, x, y);
-    else tma_store_2d(map, buf, x, y);
+    if (reduce) tma_reduce_add_2d_hint(map, buf, x, y, policy);
+    else tma_store_2d_hint(map, buf, x, y, policy);
     bulk_commit();
   }
 }
 
 // ------------------------------------------------------------------ kernel
 
-template <bool A_MN, bool B_MN, int EPI>
+template <int CG, bool A_MN, bool B_MN, int EPI>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap mapA0, const __grid_constant__ CUtensorMap mapA1,
                 const __grid_constant__ CUtensorMap mapB0, const __grid_constant__ CUtensorMap mapB1,
                 const __grid_constant__ CUtensorMap mapC, const __grid_constant__ KParams p) {
+  using T = TileCfg<CG>;
+  constexpr bool PAIR = CG == 2;
   extern __shared__ uint8_t smem_raw[];
+  // Same static layout in both CTAs of a pair: the MMA reads the peer's
+  // operands at the leader's offsets.
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
-  uint8_t* sB = smem + STAGES * A_STAGE_BYTES;
-  uint8_t* sOut = smem + STAGES * STAGE_BYTES;  // 1024-byte aligned
+  uint8_t* sB = smem + T::STAGES * T::A_STAGE;
+  uint8_t* sOut = smem + T::STAGES * T::STAGE;  // 1024-byte aligned
   uint64_t* full = reinterpret_cast<uint64_t*>(sOut + OUT_BYTES);
-  uint64_t* empty = full + STAGES;
-  uint64_t* tfull = empty + STAGES;
+  uint64_t* empty = full + T::STAGES;
+  uint64_t* tfull = empty + T::STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+  const int unit = PAIR ? static_cast<int>(cluster_id_x()) : static_cast<int>(blockIdx.x);
+  const int nunits = PAIR ? static_cast<int>(num_clusters_x()) : static_cast<int>(gridDim.x);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
+    for (int s = 0; s < T::STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull[i], 1);
-      mbar_init(&tempty[i], NUM_EPI_WARPS);
+      mbar_init(&tempty[i], NUM_EPI_WARPS * CG);  // both CTAs' epilogues release the leader's MMA
     }
     mbar_init(drain, 1);
     fence_mbarrier_init();
@@ -246,69 +282,75 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
   }
   if (warp == 2) {
-    tmem_alloc(tmem_slot, TMEM_COLS);
-    tmem_relinquish();
+    tmem_alloc_cg<CG>(tmem_slot, TMEM_COLS);
+    tmem_relinquish_cg<CG>();
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) cluster_sync();  // peer barriers initialised before any remote arrival
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
   if (warp == 0) {
     // ---------------------------------------------------------- producer
+    // Both CTAs of a pair load their own A rows and B half; the bytes of both
+    // complete on the leader's full barrier, which the leader arms.
+    const uint64_t pol_a = l2_policy(p.pol_a);
+    const uint64_t pol_b = l2_policy(p.pol_b);
     int stage = 0;
     uint32_t phase = 0;
     bool ok = true;
-    for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+    for (int tile = unit; tile < p.num_tiles && ok; tile += nunits) {
       int mb, nb;
       tile_coords(p, tile, mb, nb);
+      const int a_row = mb * T::TILE_M + static_cast<int>(rank) * 128;
+      const int b_row = nb * BN + static_cast<int>(rank) * T::B_ROWS;
       for (int seg = 0; seg < p.nseg && ok; ++seg) {
         const CUtensorMap* ma = seg == 0 ? &mapA0 : &mapA1;
         const CUtensorMap* mbm = seg == 0 ? &mapB0 : &mapB1;
         for (int kb = 0; kb < p.seg_kblocks[seg]; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1, p.status, DEV_TIMEOUT_PRODUCER)) {
+          if (!mbar_wait<PAIR>(&empty[stage], phase ^ 1, p.status, DEV_TIMEOUT_PRODUCER)) {
             ok = false;
             break;
           }
           if (lane == 0) {
-            mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
-            uint8_t* a_dst = sA + stage * A_STAGE_BYTES;
-            uint8_t* b_dst = sB + stage * B_STAGE_BYTES;
+            if (rank == 0) mbar_arrive_expect_tx(&full[stage], T::STAGE * CG);
+            const uint32_t bar = PAIR ? mapa_shared(smem_u32(&full[stage]), 0) : smem_u32(&full[stage]);
+            uint8_t* a_dst = sA + stage * T::A_STAGE;
+            uint8_t* b_dst = sB + stage * T::B_STAGE;
             if (!A_MN) {
-              tma_load_2d(a_dst, ma, &full[stage], kb * BK, mb * BM);
+              tma_load_2d_hint<CG>(a_dst, ma, bar, kb * BK, a_row, pol_a);
             } else {
 #pragma unroll
-              for (int i = 0; i < BM / 64; ++i)
-                tma_load_2d(a_dst + i * (BK * 128), ma, &full[stage], mb * BM + i * 64, kb * BK);
+              for (int i = 0; i < 128 / 64; ++i)
+                tma_load_2d_hint<CG>(a_dst + i * (BK * 128), ma, bar, a_row + i * 64, kb * BK, pol_a);
             }
             if (!B_MN) {
-              tma_load_2d(b_dst, mbm, &full[stage], kb * BK, nb * BN);
-              if (p.prefetch_b > 0 && kb + p.prefetch_b < p.seg_kblocks[seg])
-                tma_prefetch_l2_2d(mbm, (kb + p.prefetch_b) * BK, nb * BN);
+              tma_load_2d_hint<CG>(b_dst, mbm, bar, kb * BK, b_row, pol_b);
             } else {
 #pragma unroll
-              for (int i = 0; i < BN / 64; ++i)
-                tma_load_2d(b_dst + i * (BK * 128), mbm, &full[stage], nb * BN + i * 64, kb * BK);
+              for (int i = 0; i < T::B_ROWS / 64; ++i)
+                tma_load_2d_hint<CG>(b_dst + i * (BK * 128), mbm, bar, b_row + i * 64, kb * BK, pol_b);
             }
           }
           __syncwarp();
-          if (++stage == STAGES) {
+          if (++stage == T::STAGES) {
             stage = 0;
             phase ^= 1;
           }
         }
       }
     }
-  } else if (warp == 1) {
+  } else if (warp == 1 && rank == 0) {
     // --------------------------------------------------------------- MMA
-    constexpr uint32_t idesc = make_idesc_bf16_f32(BM, BN, A_MN, B_MN);
+    constexpr uint32_t idesc = make_idesc_bf16_f32(T::TILE_M, BN, A_MN, B_MN);
     int stage = 0;
     uint32_t phase = 0;
     int acc = 0;
     uint32_t acc_phase = 0;
     bool ok = true;
-    for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
-      if (!mbar_wait(&tempty[acc], acc_phase ^ 1, p.status, DEV_TIMEOUT_MMA)) {
+    for (int tile = unit; tile < p.num_tiles && ok; tile += nunits) {
+      if (!mbar_wait<PAIR>(&tempty[acc], acc_phase ^ 1, p.status, DEV_TIMEOUT_MMA)) {
         ok = false;
         break;
       }
@@ -317,14 +359,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       bool first = true;
       for (int seg = 0; seg < p.nseg && ok; ++seg) {
         for (int kb = 0; kb < p.seg_kblocks[seg]; ++kb) {
-          if (!mbar_wait(&full[stage], phase, p.status, DEV_TIMEOUT_MMA)) {
+          if (!mbar_wait<PAIR>(&full[stage], phase, p.status, DEV_TIMEOUT_MMA)) {
             ok = false;
             break;
           }
           tc_fence_after();
           if (lane == 0) {
-            const uint32_t a_base = smem_u32(sA + stage * A_STAGE_BYTES);
-            const uint32_t b_base = smem_u32(sB + stage * B_STAGE_BYTES);
+            const uint32_t a_base = smem_u32(sA + stage * T::A_STAGE);
+            const uint32_t b_base = smem_u32(sB + stage * T::B_STAGE);
 #pragma unroll
             for (int k = 0; k < BK / 16; ++k) {
               uint64_t ad, bd;
@@ -332,20 +374,25 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
               else ad = make_smem_desc_sw128(a_base + k * 2048, BK * 128, 1024);
               if (!B_MN) bd = make_smem_desc_sw128(b_base + k * 32, 16, 1024);
               else bd = make_smem_desc_sw128(b_base + k * 2048, BK * 128, 1024);
-              umma_bf16(d_tmem, ad, bd, idesc, (first && k == 0) ? 0u : 1u);
+              umma_bf16_cg<CG>(d_tmem, ad, bd, idesc, (first && k == 0) ? 0u : 1u);
             }
-            umma_commit(&empty[stage]);
+            // frees this stage in both CTAs once the MMAs have read it
+            if constexpr (PAIR) umma_commit_pair(&empty[stage], 0x3);
+            else umma_commit(&empty[stage]);
           }
           __syncwarp();
           first = false;
-          if (++stage == STAGES) {
+          if (++stage == T::STAGES) {
             stage = 0;
             phase ^= 1;
           }
         }
       }
       if (!ok) break;
-      if (lane == 0) umma_commit(&tfull[acc]);
+      if (lane == 0) {
+        if constexpr (PAIR) umma_commit_pair(&tfull[acc], 0x3);
+        else umma_commit(&tfull[acc]);
+      }
       __syncwarp();
       if (++acc == 2) {
         acc = 0;
@@ -353,35 +400,40 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
     }
     // Drain: every MMA this thread issued has completed before teardown.
-    if (lane == 0) umma_commit(drain);
+    if (lane == 0) umma_commit_cg<CG>(drain);
     __syncwarp();
-    mbar_wait(drain, 0, p.status, DEV_TIMEOUT_DRAIN);
+    mbar_wait<PAIR>(drain, 0, p.status, DEV_TIMEOUT_DRAIN);
   } else if (warp >= EPI_WARP0) {
     // ---------------------------------------------------------- epilogue
     const int ew = warp - EPI_WARP0;
     const int quad = warp & 3;  // TMEM lane quadrant this warp may access
     const int half = ew >> 2;   // which 128-column half of the tile
-    const int row_in_tile = quad * 32 + lane;
+    const int row_in_tile = static_cast<int>(rank) * 128 + quad * 32 + lane;
+    const uint64_t pol_c = l2_policy(p.pol_c);
+    const uint32_t tempty_leader0 = PAIR ? mapa_shared(smem_u32(&tempty[0]), 0) : 0u;
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
+    for (int tile = unit; tile < p.num_tiles; tile += nunits) {
       int mb, nb;
       tile_coords(p, tile, mb, nb);
-      if (!mbar_wait(&tfull[acc], acc_phase, p.status, DEV_TIMEOUT_EPILOGUE)) break;
+      if (!mbar_wait<PAIR>(&tfull[acc], acc_phase, p.status, DEV_TIMEOUT_EPILOGUE)) break;
       tc_fence_after();
-      const long long grow = static_cast<long long>(mb) * BM + row_in_tile;
+      const long long grow = static_cast<long long>(mb) * T::TILE_M + row_in_tile;
       const bool row_ok = grow < p.M;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
                              static_cast<uint32_t>(acc * BN + half * 128);
       const int colh = nb * BN + half * 128;
-      const int row0 = mb * BM + quad * 32;
+      const int row0 = mb * T::TILE_M + static_cast<int>(rank) * 128 + quad * 32;
       uint8_t* buf = sOut + ew * OUT_STAGE_BYTES;
-      // Releases the accumulator to the MMA warp as soon as its last TMEM
-      // load has completed (the remaining work uses registers only).
+      // Releases the accumulator to the (leader's) MMA warp as soon as its
+      // last TMEM load has completed (the remaining work uses registers only).
       auto release_tmem = [&]() {
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&tempty[acc]);
+        if (lane == 0) {
+          if constexpr (PAIR) mbar_arrive_cluster(tempty_leader0 + static_cast<uint32_t>(acc * 8));
+          else mbar_arrive(&tempty[acc]);
+        }
       };
       if constexpr (EPI == static_cast<int>(Epi::Store)) {
         const float alpha = p.e.alpha_ptr ? *p.e.alpha_ptr : p.e.alpha;
@@ -389,7 +441,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const int col0 = colh + c * 32;
           if (col0 >= p.N) return;
           if (p.tma_store) {
-            if (row0 < p.M) stage_and_store(buf, lane, r, alpha, &mapC, col0, row0, p.tma_reduce != 0);
+            if (row0 < p.M) stage_and_store(buf, lane, r, alpha, &mapC, col0, row0, p.tma_reduce != 0, pol_c);
           }
           else if (row_ok) epi_store_chunk(p, grow, col0, min(32, p.N - col0), r, alpha);
         };
@@ -417,7 +469,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           if (col0 >= p.N) return;
           logits_chunk_any<OWN_DT>(e, grow, row_ok, col0, p.N, r, os);
           if (p.tma_store) {
-            if (row0 < p.M) stage_and_store(buf, lane, r, 1.0f, &mapC, col0, row0, false);
+            if (row0 < p.M) stage_and_store(buf, lane, r, 1.0f, &mapC, col0, row0, false, pol_c);
           } else if (row_ok) {
             float* dst = e.logits + grow * e.ldl + col0;
             const int nv = min(32, p.N - col0);
@@ -457,9 +509,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
   tc_fence_before();
   __syncthreads();
+  // A pair stays resident until the leader's MMAs (which read the peer's
+  // shared memory and write its TMEM) have drained.
+  if constexpr (PAIR) cluster_sync();
   if (warp == 2) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, TMEM_COLS);
+    tmem_dealloc_cg<CG>(tmem_base, TMEM_COLS);
   }
 }
 
@@ -509,22 +564,95 @@ bool out_map_ok(const float* ptr, long long ld) {
   return ptr && (reinterpret_cast<uintptr_t>(ptr) & 15) == 0 && (ld * 4) % 16 == 0;
 }
 
-template <bool A_MN, bool B_MN, int EPI>
-cudaError_t launch_t(const CUtensorMap* maps, const KParams& kp, int grid, cudaStream_t stream) {
-  auto kern = gemm_kernel<A_MN, B_MN, EPI>;
-  // The shared-memory opt-in is a per-device function attribute: set it once
-  // per device for this instantiation.
-  static std::atomic<uint64_t> attr_done{0};
+// Per-device, per-instantiation launch state: the shared-memory opt-in
+// (a function attribute that must be set once per device) and, for CTA
+// pairs, how many 2-CTA clusters can be resident at once.
+struct LaunchCache {
+  std::mutex mu;
+  uint64_t attr_done = 0;
+  int max_clusters[64] = {0};
+};
+
+template <int CG, bool A_MN, bool B_MN, int EPI>
+cudaError_t launch_t(const CUtensorMap* maps, const KParams& kp, int num_sms, cudaStream_t stream) {
+  using T = TileCfg<CG>;
+  auto kern = gemm_kernel<CG, A_MN, B_MN, EPI>;
+  static LaunchCache cache;
   int dev = 0;
   cudaGetDevice(&dev);
-  const uint64_t bit = 1ull << (dev & 63);
-  if (!(attr_done.load(std::memory_order_acquire) & bit)) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-    if (e != cudaSuccess) return e;
-    attr_done.fetch_or(bit, std::memory_order_acq_rel);
+  dev &= 63;
+  int units = num_sms / CG;
+  {
+    std::lock_guard<std::mutex> lock(cache.mu);
+    if (!(cache.attr_done & (1ull << dev))) {
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, T::SMEM);
+      if (e != cudaSuccess) return e;
+      if (CG > 1) {
+        cudaLaunchConfig_t q = {};
+        q.gridDim = dim3(static_cast<unsigned>(units * CG), 1, 1);
+        q.blockDim = dim3(NUM_THREADS, 1, 1);
+        q.dynamicSmemBytes = T::SMEM;
+        cudaLaunchAttribute qa[1];
+        qa[0].id = cudaLaunchAttributeClusterDimension;
+        qa[0].val.clusterDim.x = CG;
+        qa[0].val.clusterDim.y = 1;
+        qa[0].val.clusterDim.z = 1;
+        q.attrs = qa;
+        q.numAttrs = 1;
+        int n = 0;
+        e = cudaOccupancyMaxActiveClusters(&n, kern, &q);
+        if (e != cudaSuccess) return e;
+        if (n <= 0) return cudaErrorInvalidConfiguration;
+        cache.max_clusters[dev] = n;
+      }
+      cache.attr_done |= 1ull << dev;
+    }
+    if (CG > 1) units = cache.max_clusters[dev];
   }
-  kern<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(maps[0], maps[1], maps[2], maps[3], maps[4], kp);
-  return cudaGetLastError();
+  if (kp.num_tiles < units) units = kp.num_tiles;
+  if (CG == 1) {
+    kern<<<units, NUM_THREADS, T::SMEM, stream>>>(maps[0], maps[1], maps[2], maps[3], maps[4], kp);
+    return cudaGetLastError();
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(units * CG), 1, 1);
+  cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+  cfg.dynamicSmemBytes = T::SMEM;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = CG;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, maps[0], maps[1], maps[2], maps[3], maps[4], kp);
+}
+
+template <int CG>
+cudaError_t dispatch(const GemmDesc& d, const CUtensorMap* maps, const KParams& kp, int num_sms,
+                     cudaStream_t stream, const char** why) {
+  if (d.epi == Epi::Logits) {
+    if (d.a_mn_major || d.b_mn_major) {
+      if (why) *why = "logits epilogue requires K-major operands";
+      return cudaErrorInvalidValue;
+    }
+    // EPI code: 16 | own dT
+    if (d.args.own_dT) return launch_t<CG, false, false, 17>(maps, kp, num_sms, stream);
+    return launch_t<CG, false, false, 16>(maps, kp, num_sms, stream);
+  }
+  if (!d.a_mn_major && !d.b_mn_major) return launch_t<CG, false, false, 0>(maps, kp, num_sms, stream);
+  if (!d.a_mn_major && d.b_mn_major) return launch_t<CG, false, true, 0>(maps, kp, num_sms, stream);
+  if (d.a_mn_major && !d.b_mn_major) return launch_t<CG, true, false, 0>(maps, kp, num_sms, stream);
+  return launch_t<CG, true, true, 0>(maps, kp, num_sms, stream);
+}
+
+// CTA pairs by default; ORDA_GEMM_CTA_PAIR=0 selects single-CTA tiles (a
+// diagnostic switch for comparing the two tile shapes; both compute the same
+// result).
+bool use_cta_pair() {
+  const char* v = std::getenv("ORDA_GEMM_CTA_PAIR");
+  return !(v && v[0] == '0');
 }
 
 }  // namespace
@@ -535,20 +663,25 @@ cudaError_t gemm_launch(const GemmDesc& d, int num_sms, cudaStream_t stream, con
     if (why) *why = "cuTensorMapEncodeTiled entry point unavailable";
     return cudaErrorNotSupported;
   }
+  const int cg = use_cta_pair() ? 2 : 1;
+  const int tile_m = 128 * cg;
+  const int b_rows = BN / cg;
   KParams kp{};
   kp.M = static_cast<int>(d.M);
   kp.N = static_cast<int>(d.N);
-  kp.m_blocks = static_cast<int>((d.M + BM - 1) / BM);
+  kp.m_blocks = static_cast<int>((d.M + tile_m - 1) / tile_m);
   kp.n_blocks = static_cast<int>((d.N + BN - 1) / BN);
   kp.num_tiles = kp.m_blocks * kp.n_blocks;
   kp.raster_n_fastest = d.raster_n_fastest ? 1 : 0;
   kp.nseg = d.nseg;
   kp.status = d.status;
   kp.e = d.args;
+  long long k_total = 0;
   CUtensorMap maps[5];
   for (int s = 0; s < 2; ++s) {
     const int src = s < d.nseg ? s : 0;
     kp.seg_kblocks[s] = s < d.nseg ? static_cast<int>((d.k_seg[s] + BK - 1) / BK) : 0;
+    if (s < d.nseg) k_total += d.k_seg[s];
     const MatRef& a = d.a[src];
     const MatRef& b = d.b[src];
     for (const MatRef* m : {&a, &b}) {
@@ -557,16 +690,31 @@ cudaError_t gemm_launch(const GemmDesc& d, int num_sms, cudaStream_t stream, con
         return cudaErrorInvalidValue;
       }
     }
-    bool ok = d.a_mn_major ? encode_map(&maps[s], a, 64, BK) : encode_map(&maps[s], a, BK, BM);
-    ok = ok && (d.b_mn_major ? encode_map(&maps[2 + s], b, 64, BK) : encode_map(&maps[2 + s], b, BK, BN));
+    // boxes: K-major 64 (K) x rows-per-CTA; MN-major 64 (MN) x 64 (K)
+    bool ok = d.a_mn_major ? encode_map(&maps[s], a, 64, BK) : encode_map(&maps[s], a, BK, 128);
+    ok = ok && (d.b_mn_major ? encode_map(&maps[2 + s], b, 64, BK) : encode_map(&maps[2 + s], b, BK, b_rows));
     if (!ok) {
       if (why) *why = "cuTensorMapEncodeTiled failed";
       return cudaErrorInvalidValue;
     }
   }
-  // L2 prefetch of B ahead of the ring: measured no gain for the logits GEMM
-  // (its B tiles are shared by the chunk's M tiles through L2 already).
-  kp.prefetch_b = 0;
+  // L2 policies: an operand of at most 64 MB that is no larger than the
+  // other one is re-read by every tile of its rows/columns: keep it
+  // (evict-last). Outputs larger than 32 MB are written once: evict-first.
+  constexpr long long kKeepBytes = 64ll << 20;
+  const long long a_bytes = d.M * k_total * 2, b_bytes = d.N * k_total * 2, c_bytes = d.M * d.N * 4;
+  kp.pol_a = (a_bytes <= kKeepBytes && a_bytes <= b_bytes) ? 2 : 0;
+  kp.pol_b = (b_bytes <= kKeepBytes && b_bytes < a_bytes) ? 2 : 0;
+  kp.pol_c = c_bytes > (32ll << 20) ? 1 : 0;
+  // M-fastest raster in groups whose A slab is at most 32 MB: a wave of
+  // tiles shares its B tiles, and B is re-read once per group.
+  {
+    const long long slab = static_cast<long long>(tile_m) * k_total * 2;
+    long long g = slab > 0 ? (32ll << 20) / slab : kp.m_blocks;
+    if (g < 1) g = 1;
+    if (g > kp.m_blocks) g = kp.m_blocks;
+    kp.group_m = static_cast<int>(g > 0 ? g : 1);
+  }
   // output through shared-memory staging + TMA when the output allows it
   std::memset(&maps[4], 0, sizeof(CUtensorMap));
   kp.tma_store = 0;
@@ -580,21 +728,8 @@ cudaError_t gemm_launch(const GemmDesc& d, int num_sms, cudaStream_t stream, con
     kp.tma_reduce = d.args.beta == 1.0f ? 1 : 0;
   }
   if (kp.num_tiles == 0) return cudaSuccess;
-  const int grid = kp.num_tiles < num_sms ? kp.num_tiles : num_sms;
-  const int epi = static_cast<int>(d.epi);
-  if (epi == static_cast<int>(Epi::Logits)) {
-    if (d.a_mn_major || d.b_mn_major) {
-      if (why) *why = "logits epilogue requires K-major operands";
-      return cudaErrorInvalidValue;
-    }
-    // EPI code: 16 | own dT
-    if (d.args.own_dT) return launch_t<false, false, 17>(maps, kp, grid, stream);
-    return launch_t<false, false, 16>(maps, kp, grid, stream);
-  }
-  if (!d.a_mn_major && !d.b_mn_major) return launch_t<false, false, 0>(maps, kp, grid, stream);
-  if (!d.a_mn_major && d.b_mn_major) return launch_t<false, true, 0>(maps, kp, grid, stream);
-  if (d.a_mn_major && !d.b_mn_major) return launch_t<true, false, 0>(maps, kp, grid, stream);
-  return launch_t<true, true, 0>(maps, kp, grid, stream);
+  if (cg == 2) return dispatch<2>(d, maps, kp, num_sms, stream, why);
+  return dispatch<1>(d, maps, kp, num_sms, stream, why);
 }
 
 }  // namespace orda

@@ -5,7 +5,9 @@ of the same bf16 operands, for every operand layout the loss uses:
   kind (1,1)  C = A^T @ B   wgrad    (A [K,M], B [K,N])
   kind (1,0)  C = A^T @ B^T          (A [K,M], B [N,K])
 Shapes cover single tiles, K/M/N tails that rely on TMA zero fill, and a
-multi-wave persistent schedule. Tolerance: fp32 accumulation of exact bf16
+multi-wave persistent schedule; each runs with the CTA-pair tiles (256 x 256,
+tcgen05 cta_group::2, the default) and with single-CTA tiles (128 x 256,
+ORDA_GEMM_CTA_PAIR=0). Tolerance: fp32 accumulation of exact bf16
 products, so the relative L2 error to the float64 product is <= 1e-5 for
 K <= 4096 and <= 1e-4 for the long-K (32000) case.
 """
@@ -40,12 +42,20 @@ SHAPES = [
     (1, 8, 8),
     (513, 1000, 1000),
     (64, 4096, 512),
+    (1000, 2304, 136),
+    (2048, 8192, 256),
 ]
+
+
+@pytest.fixture(params=["pair", "single"])
+def tiles(request, monkeypatch):
+    monkeypatch.setenv("ORDA_GEMM_CTA_PAIR", "1" if request.param == "pair" else "0")
+    return request.param
 
 
 @pytest.mark.parametrize("a_kind,b_kind", [(0, 0), (0, 1), (1, 1), (1, 0)])
 @pytest.mark.parametrize("m,n,k", SHAPES)
-def test_gemm_layouts(ctx, a_kind, b_kind, m, n, k):
+def test_gemm_layouts(ctx, tiles, a_kind, b_kind, m, n, k):
     from orda_b200.device import gemm_bf16
 
     gen = torch.Generator(device="cuda").manual_seed(m * 7 + n * 13 + k)
@@ -63,7 +73,7 @@ def test_gemm_layouts(ctx, a_kind, b_kind, m, n, k):
     assert err < 1e-5, f"rel L2 {err:.3e}"
 
 
-def test_gemm_alpha_beta_accumulate(ctx):
+def test_gemm_alpha_beta_accumulate(ctx, tiles):
     from orda_b200.device import gemm_bf16
 
     gen = torch.Generator(device="cuda").manual_seed(5)
@@ -78,7 +88,7 @@ def test_gemm_alpha_beta_accumulate(ctx):
     assert ((c.double() - ref).norm() / ref.norm()) < 1e-5
 
 
-def test_gemm_long_k(ctx):
+def test_gemm_long_k(ctx, tiles):
     """Long-K shape of the dgrad GEMM (K = vocabulary)."""
     from orda_b200.device import gemm_bf16
 
