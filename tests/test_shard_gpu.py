@@ -1,0 +1,158 @@
+"""Row-sharded distillation on two GPUs with NCCL (orda_b200/shard.py driving
+the device entry), against the same problem computed on one GPU.
+
+Each rank runs its block of rows through orda_distillation_loss_device with
+the global mean denominator and without the INT8 step, the shard module
+reduce-scatters grad_W over NCCL and quantises each rank's vocabulary slice.
+The combined scalars, grad_hidden rows and grad_W slices must match the
+single-GPU call on the whole batch: scalars within 1e-5 relative (the row
+sums are added in another order), gradients within rel-L2 1e-5 (fp32 sums of
+the same bf16 products in another order), and the INT8 codes of the slice
+within one code of the single-GPU ones (a scale computed from a grad_W row
+that differs in the last bits can move a value across a rounding boundary).
+
+Skipped unless two GPUs are visible. Ranks run as spawned processes with a
+short process-group timeout; NVLS is off so no rank binds multicast memory.
+"""
+from __future__ import annotations
+
+import os
+import socket
+import sys
+from pathlib import Path
+
+import pytest
+import torch
+
+REPO = Path(__file__).resolve().parent.parent
+pytestmark = pytest.mark.gpu
+
+BT, H, V = 512, 512, 8192
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _inputs(dev):
+    g = torch.Generator(device=dev).manual_seed(21)
+    hs = torch.randn(BT, H, generator=g, device=dev).bfloat16()
+    w = (0.02 * torch.randn(V, H, generator=g, device=dev)).bfloat16()
+    tl = (2.0 ** 0.5 * torch.randn(BT, V, generator=g, device=dev)).bfloat16()
+    labels = torch.randint(0, V, (BT,), generator=g, device=dev)
+    labels[::17] = -100
+    return hs, w, tl, labels
+
+
+def _opts(ob):
+    return ob.LossOptions(kd_weight=0.4, temperature=1.5, config=ob.KernelConfig(quantize_grad_weight=True))
+
+
+def _worker(rank, world, port, outdir):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    import datetime
+
+    import torch.distributed as dist
+
+    sys.path.insert(0, str(REPO / "orda-cutile-rs_b200"))
+    import orda_b200 as ob
+    from orda_b200 import shard
+    from orda_b200.device import DeviceContext, distillation_loss_device, quantize_grad_w
+
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        hs, w, tl, labels = _inputs(dev)
+        r0, r1 = shard.shard_rows(BT, world, rank)
+        lab = labels[r0:r1].contiguous()
+        n_global = shard.global_non_ignore(lab, -100)
+        ctx = DeviceContext(rank)
+        nsl = V // world
+        q = torch.empty(nsl, H, device=dev, dtype=torch.int8)
+        qs = torch.empty(nsl, device=dev)
+
+        def compute(n):
+            r = distillation_loss_device(ctx, hs[r0:r1].contiguous(), w, lab, ob.TeacherMode.Precomputed,
+                                         teacher_logits=tl[r0:r1].contiguous(), opts=_opts(ob),
+                                         global_non_ignore=n, skip_quantize=True)
+            return r.scalars, r.grad_student_hidden, r.grad_weight
+
+        raw = {}
+
+        def quant(sl, shifted):
+            raw["gw"] = sl.clone()  # the reduced slice before the in-place INT8 round trip
+            quantize_grad_w(ctx, sl, shifted, -100, False, 0, q, qs)
+
+        res = shard.row_sharded_step(compute, lab, -100, n_global, quantize=quant)
+        torch.cuda.synchronize()
+        ctx.check()
+        torch.save({"scalars": res.scalars.cpu(), "gsh": res.grad_student_hidden.cpu(), "gw": raw["gw"].cpu(),
+                    "gw_dq": res.grad_weight_slice.cpu(), "q": q.cpu(), "qs": qs.cpu(), "rows": (r0, r1),
+                    "vocab": res.vocab_range}, os.path.join(outdir, f"rank{rank}.pt"))
+        ctx.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_row_sharded_two_gpus_match_single_gpu(ob, tmp_path):
+    import torch.multiprocessing as mp
+
+    from conftest import rel_l2
+    from orda_b200.device import DeviceContext, distillation_loss_device
+
+    world = 2
+    ctxm = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctxm.Process(target=_worker, args=(r, world, port, str(tmp_path))) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    codes = [p.exitcode for p in procs]
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    assert codes == [0, 0], f"rank exit codes {codes}"
+
+    dev = torch.device("cuda", 0)
+    hs, w, tl, labels = _inputs(dev)
+    with DeviceContext(0) as ctx:
+        ref = distillation_loss_device(ctx, hs, w, labels, ob.TeacherMode.Precomputed, teacher_logits=tl,
+                                       opts=_opts(ob), skip_quantize=True)
+        torch.cuda.synchronize()
+        ctx.check()
+    sc_ref = ref.scalars.cpu()
+    gsh_ref = ref.grad_student_hidden.cpu()
+    gw_ref = ref.grad_weight.cpu()
+    parts = [torch.load(tmp_path / f"rank{r}.pt") for r in range(world)]
+    for p in parts:
+        assert torch.allclose(p["scalars"], sc_ref, rtol=1e-5, atol=1e-7), (p["scalars"], sc_ref)
+        r0, r1 = p["rows"]
+        assert rel_l2(p["gsh"].numpy(), gsh_ref[r0:r1].numpy()) < 1e-5
+        v0, v1 = p["vocab"]
+        assert rel_l2(p["gw"].numpy(), gw_ref[v0:v1].numpy()) < 1e-5
+        # INT8 slice: quantise the single-GPU slice the same way and compare codes
+        from orda_b200.device import quantize_grad_w
+
+        with DeviceContext(0) as ctx:
+            sl = gw_ref[v0:v1].clone().to(dev)
+            lab = labels.clone()
+            shifted = torch.where(lab == -100, torch.full_like(lab, -1), lab - v0)
+            q = torch.empty(v1 - v0, H, device=dev, dtype=torch.int8)
+            qs = torch.empty(v1 - v0, device=dev)
+            quantize_grad_w(ctx, sl, shifted, -100, False, 0, q, qs)
+            torch.cuda.synchronize()
+        dq = (p["q"].int() - q.cpu().int()).abs()
+        assert int(dq.max()) <= 1
+        assert torch.allclose(p["qs"], qs.cpu(), rtol=1e-5, atol=0)
+        # the dequantised slices then agree to within those code differences
+        assert rel_l2(p["gw_dq"].numpy(), sl.cpu().numpy()) < 1e-3
