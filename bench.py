@@ -23,6 +23,7 @@ import argparse
 import ctypes as C
 import json
 import os
+import re
 import statistics
 import subprocess
 import sys
@@ -307,12 +308,16 @@ def run_ours(args):
     gemm_launches = sum(phases[p][1] for p in ("logits_gemm", "dgrad_gemm", "wgrad_gemm")) / args.steps
     flops = algorithmic_flops(bt, h, v)
     achieved = flops / (gemm_ms / 1e3) / 1e12
+    # DRAM bytes of the step's GEMM launches from the committed ncu launch list
+    # of this workload (dram__bytes_read.sum + dram__bytes_write.sum)
     traffic = None
-    tfile = REPO / "profiles" / "gemm_traffic.json"
-    if tfile.exists():
-        traffic = json.loads(tfile.read_text()).get("bytes_per_step")
+    tfile = REPO / "profiles" / "launch_list_c4_bench.md"
+    if tfile.exists() and bt == CFG["bt"]:
+        m = re.search(r"traffic_bytes_per_step_gemm = (\d+)", tfile.read_text())
+        traffic = int(m.group(1)) if m else None
     roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-                "traffic": traffic, "kernel": "gemm_kernel (tcgen05, 3 layouts)",
+                "traffic": traffic, "traffic_scope": "DRAM bytes of the step's 3 GEMM launches (ncu launch list, "
+                "profiles/launch_list_c4_bench.md)", "kernel": "gemm_kernel (tcgen05 cta_group::2, 3 layouts)",
                 "launches_per_step": gemm_launches, "gemm_ms_per_step": gemm_ms,
                 "peak_kind": f"{peak_kind} burst bf16 (MEASURED_PEAKS.json bf16_tflops)",
                 "frac_of_sustained": achieved / peak_sus if peak_sus else None}
