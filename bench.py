@@ -243,22 +243,46 @@ def run_ours(args):
     ctx = DeviceContext(local)
     n_global = bt * world if world == 1 else shard.global_non_ignore(labels, -100)
 
+    # N > 1: the grad_W reduce-scatter is fused into the wgrad GEMM (peer
+    # stores into the owners' slot buffers) unless --reduce nccl
+    fused = shard.SlotReduceScatter(ctx, v, h) if world > 1 and args.reduce == "fused" else None
+    gw_slice = torch.empty(v // world, h, device=dev) if fused else None
+    if fused:
+        del out["grad_weight"]  # the local full grad_W is never materialised
+    marks = []  # (after compute, end of step) events of the timed steps
+
     def step():
         if world == 1:
             out["grad_weight_q"], out["grad_weight_scale"] = q, qs
             return distillation_loss_device(ctx, hs, w, labels, ob.TeacherMode.Precomputed, teacher_logits=tl,
                                             opts=opts, out=out, want_int8=True, stream=stream)
+        ev = [torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)]
 
-        def compute(n):
-            r = distillation_loss_device(ctx, hs, w, labels, ob.TeacherMode.Precomputed, teacher_logits=tl,
-                                         opts=opts, out=out, global_non_ignore=n, skip_quantize=True,
-                                         stream=stream)
-            return r.scalars, r.grad_student_hidden, r.grad_weight
+        if fused:
+            def compute_scatter(n):
+                r = distillation_loss_device(ctx, hs, w, labels, ob.TeacherMode.Precomputed, teacher_logits=tl,
+                                             opts=opts, out=out, global_non_ignore=n, scatter_grad_weight=True,
+                                             stream=stream)
+                ev[0].record(stream)
+                return r.scalars, r.grad_student_hidden
 
-        def quant(sl, shifted):
-            quantize_grad_w(ctx, sl, shifted, -100, False, 0, q, qs, stream=stream)
+            res = fused.step(compute_scatter, labels, -100, n_global, gw_slice, quantize=True, q=q, scale=qs,
+                             stream=stream)
+        else:
+            def compute(n):
+                r = distillation_loss_device(ctx, hs, w, labels, ob.TeacherMode.Precomputed, teacher_logits=tl,
+                                             opts=opts, out=out, global_non_ignore=n, skip_quantize=True,
+                                             stream=stream)
+                ev[0].record(stream)
+                return r.scalars, r.grad_student_hidden, r.grad_weight
 
-        return shard.row_sharded_step(compute, labels, -100, n_global, quantize=quant)
+            def quant(sl, shifted):
+                quantize_grad_w(ctx, sl, shifted, -100, False, 0, q, qs, stream=stream)
+
+            res = shard.row_sharded_step(compute, labels, -100, n_global, quantize=quant)
+        ev[1].record(stream)
+        marks.append(ev)
+        return res
 
     for _ in range(args.warmup):
         step()
@@ -279,6 +303,7 @@ def run_ours(args):
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
+    marks.clear()
     ev0.record(stream)
     h0 = time.perf_counter()
     for _ in range(args.steps):
@@ -289,6 +314,9 @@ def run_ours(args):
     if world > 1:
         dist.barrier()
     ms_total = ev0.elapsed_time(ev1)
+    # N > 1: time from the end of the device entry to the end of the step
+    # (scalar all-reduce, grad_W reduction and the slice's INT8 round trip)
+    collective_ms = statistics.mean(a.elapsed_time(b) for a, b in marks) if marks else None
     phases = ctx.phase_times()
     ctx.enable_timing(False)
     launches = ctx.launch_count() - launches0
@@ -329,11 +357,13 @@ def run_ours(args):
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": WORKLOAD if bt == CFG["bt"] else f"{WORKLOAD} [profiling size: {bt} rows]",
                    "global_batch": tokens, "seq_len": None, "rows_per_gpu": bt,
-                   "parallelism": "rows sharded, grad_W reduce-scatter" if world > 1 else "single GPU",
+                   "parallelism": (f"rows sharded, grad_W reduce-scatter "
+                                   f"({'fused into the wgrad GEMM' if args.reduce == 'fused' else 'NCCL'})"
+                                   if world > 1 else "single GPU"),
                    "l2": "inputs larger than L2 (W 1 GiB, teacher logits 2 GiB per GPU); no flush"},
         "step_tflops_per_gpu": step_tflops, "step_frac_of_peak": step_tflops / peak,
         "phases_ms_per_step": {k: v_[0] / args.steps for k, v_ in phases.items()},
-        "host_enqueue_ms_per_step": host_ms,
+        "host_enqueue_ms_per_step": host_ms, "collective_ms_per_step": collective_ms,
         "roofline": roofline, "gpu_launches": int(launches), "clocks": clocks,
     }
 
@@ -424,6 +454,8 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-clocks", action="store_true")
+    ap.add_argument("--reduce", choices=["fused", "nccl"], default="fused",
+                    help="N > 1: grad_W reduce-scatter fused into the wgrad GEMM, or an NCCL reduce-scatter")
     args = ap.parse_args()
     if args.warmup < 3:
         print("note: at least 3 warm-up steps are required for a valid number; using 3", file=sys.stderr)

@@ -279,6 +279,11 @@ typedef struct OrdaDeviceOutputs {
 typedef struct OrdaShardOptions {
   int64_t global_non_ignore; /* > 0: use this token count as the mean denominator */
   int32_t skip_quantize;     /* 1: leave grad_W un-quantized (quantize after the reduction) */
+  int32_t scatter_grad_weight; /* 1: the wgrad GEMM writes this rank's grad_W partial straight into the
+                                  owning ranks' slot buffers (orda_context_slots_*), overlapping the
+                                  reduce-scatter with the GEMM; out->grad_weight is not written and may
+                                  be NULL; implies skip_quantize. Finish with orda_reduce_slots_device
+                                  after a cross-rank barrier. */
 } OrdaShardOptions;
 
 /* The timed path. Enqueues everything on `stream` (a cudaStream_t; NULL =
@@ -289,6 +294,37 @@ ORDA_API int orda_distillation_loss_device(OrdaContext* ctx, const OrdaDeviceMat
                                   const OrdaDeviceTeacher* teacher, const OrdaLossOptions* opts,
                                   const OrdaDeviceOutputs* out, const OrdaShardOptions* shard,
                                   void* stream, OrdaChunkPlan* plan_out, char* err, size_t err_len);
+
+/* Fused grad_W reduce-scatter for row-sharded runs on the GPUs of one node
+ * (up to 8 ranks, one process per GPU). There is no counterpart in the
+ * reference, which runs on one device; for data-parallel callers that
+ * split the rows across GPUs it replaces a separate NCCL reduce-scatter of
+ * the fp32 grad_W.
+ *   1. orda_context_slots_create: rank `rank` of `world` allocates its slot
+ *      buffer, fp32 [world][slice_rows][h] (slice_rows = V / world), and gets
+ *      its CUDA IPC handle;
+ *   2. the caller all-gathers the handles; orda_context_slots_attach maps the
+ *      other ranks' buffers (handles indexed by rank);
+ *   3. orda_distillation_loss_device with shard->scatter_grad_weight = 1: the
+ *      wgrad GEMM stores each rank's partial of grad_W rows [o*slice,
+ *      (o+1)*slice) into rank o's buffer, partial index = this rank;
+ *   4. after a barrier across the ranks (e.g. an NCCL all-reduce of one value
+ *      on the same stream), orda_reduce_slots_device sums the `world` partials
+ *      of this rank's rows in rank order into grad_w_slice [slice_rows, h] and,
+ *      if quantize, applies the INT8 round trip of orda_quantize_grad_w_device
+ *      with the labels of all ranks (target rows are labels in this rank's
+ *      row range; stochastic draws are indexed by the global row).
+ * The buffers are released by orda_context_destroy or the next create. */
+typedef struct OrdaIpcHandle {
+  char bytes[64];
+} OrdaIpcHandle;
+ORDA_API int orda_context_slots_create(OrdaContext* ctx, int world, int rank, size_t slice_rows, size_t h,
+                                       OrdaIpcHandle* handle_out, char* err, size_t err_len);
+ORDA_API int orda_context_slots_attach(OrdaContext* ctx, const OrdaIpcHandle* handles, char* err, size_t err_len);
+ORDA_API int orda_reduce_slots_device(OrdaContext* ctx, float* grad_w_slice, size_t ld, const int64_t* labels,
+                                      size_t n_labels, int64_t ignore_index, int quantize, int stochastic,
+                                      uint64_t seed, int8_t* q, float* scale, void* stream, char* err,
+                                      size_t err_len);
 
 /* INT8 row-wise grad_W quantisation on the device: `quantize_grad_w` +
  * `dequantize_grad_w(.., 1.0)` (src/quant.rs:157-202). grad_w [V,H] fp32 is

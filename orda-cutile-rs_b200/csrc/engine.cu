@@ -64,6 +64,16 @@ struct OrdaContext {
   double phase_ms[ORDA_NUM_PHASES] = {};
   uint64_t phase_launches[ORDA_NUM_PHASES] = {};
   uint64_t launches = 0;
+  // Slot buffers of the fused grad_W reduce-scatter (orda_context_slots_*):
+  // this rank owns grad_W rows [rank*slice, (rank+1)*slice) and receives
+  // every rank's partial of them, fp32 [world][slice][h].
+  float* slots = nullptr;
+  int slot_world = 0;
+  int slot_rank = -1;
+  long long slot_slice = 0;
+  long long slot_h = 0;
+  float* slot_peer[orda::kMaxSlotRanks] = {};  // rank -> its slot buffer (IPC mapping for other ranks)
+  bool slots_attached = false;
 };
 
 namespace orda {
@@ -255,11 +265,24 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
   f.teacher_rows = f.need_teacher && live_teacher;
   f.teacher_grad = f.w_t > 0.0f && live_teacher;
   f.teacher_ce = f.w_t > 0.0f;
-  f.quant = o.config.quantize_grad_weight != 0 && !(shard && shard->skip_quantize);
+  const bool scatter = shard && shard->scatter_grad_weight;
+  f.quant = o.config.quantize_grad_weight != 0 && !(shard && shard->skip_quantize) && !scatter;
 
-  if (!out.grad_student_hidden || !out.grad_weight || !out.scalars) {
+  if (!out.grad_student_hidden || (!out.grad_weight && !scatter) || !out.scalars) {
     set_error(err, len, "grad_student_hidden, grad_weight and scalars outputs are required");
     return ORDA_ERR_INVALID;
+  }
+  if (scatter) {
+    if (!ctx->slots_attached) {
+      set_error(err, len, "scatter_grad_weight needs slot buffers (orda_context_slots_create / _attach)");
+      return ORDA_ERR_INVALID;
+    }
+    if (static_cast<long long>(in.v) != ctx->slot_slice * ctx->slot_world ||
+        static_cast<long long>(in.h) != ctx->slot_h) {
+      set_error(err, len, "slot buffers were made for V=%lld, H=%lld; this call has V=%zu, H=%zu",
+                ctx->slot_slice * ctx->slot_world, ctx->slot_h, in.v, in.h);
+      return ORDA_ERR_INVALID;
+    }
   }
   if (f.teacher_grad && !out.grad_teacher_hidden) {
     set_error(err, len, "grad_teacher_hidden output is required (teacher CE weight > 0 with a live teacher)");
@@ -481,8 +504,18 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
       gd.N = static_cast<long long>(h);
       gd.raster_n_fastest = true;
       gd.status = status;
-      gd.args.out0 = out.grad_weight;
-      gd.args.ld0 = static_cast<long long>(out.ld_grad_weight);
+      if (scatter) {
+        // each owner's rows go straight to its slot buffer: the reduce-scatter
+        // transfer overlaps this GEMM
+        gd.args.scatter = 1;
+        gd.args.slot_rank = ctx->slot_rank;
+        gd.args.slot_slice = ctx->slot_slice;
+        gd.args.slot_ld = ctx->slot_h;
+        for (int r = 0; r < kMaxSlotRanks; ++r) gd.args.slot[r] = ctx->slot_peer[r];
+      } else {
+        gd.args.out0 = out.grad_weight;
+        gd.args.ld0 = static_cast<long long>(out.ld_grad_weight);
+      }
       gd.args.alpha_ptr = ctx->d_mean_scale;
       gd.args.beta = g0 > 0 ? 1.0f : 0.0f;
       if ((e = gemm_launch(gd, ctx->num_sms, st, &why)) != cudaSuccess)
@@ -645,10 +678,125 @@ int orda_context_create(int device, OrdaContext** out, char* err, size_t err_len
   return ORDA_OK;
 }
 
+static void release_slots(OrdaContext* ctx) {
+  for (int r = 0; r < orda::kMaxSlotRanks; ++r) {
+    if (ctx->slot_peer[r] && r != ctx->slot_rank) cudaIpcCloseMemHandle(ctx->slot_peer[r]);
+    ctx->slot_peer[r] = nullptr;
+  }
+  if (ctx->slots) cudaFree(ctx->slots);
+  ctx->slots = nullptr;
+  ctx->slot_world = 0;
+  ctx->slot_rank = -1;
+  ctx->slot_slice = 0;
+  ctx->slot_h = 0;
+  ctx->slots_attached = false;
+}
+
+int orda_context_slots_create(OrdaContext* ctx, int world, int rank, size_t slice_rows, size_t h,
+                              OrdaIpcHandle* handle_out, char* err, size_t err_len) {
+  if (!ctx || !handle_out || world < 1 || world > orda::kMaxSlotRanks || rank < 0 || rank >= world ||
+      slice_rows == 0 || h == 0) {
+    set_error(err, err_len, "invalid argument (world in [1, %d], rank in [0, world), slice_rows and h > 0)",
+              orda::kMaxSlotRanks);
+    return ORDA_ERR_INVALID;
+  }
+  std::lock_guard<std::mutex> lock(ctx->mu);
+  cudaSetDevice(ctx->device);
+  cudaDeviceSynchronize();
+  release_slots(ctx);
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, static_cast<size_t>(world) * slice_rows * h * sizeof(float));
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    set_error(err, err_len, "slot buffer allocation failed (%zu bytes)",
+              static_cast<size_t>(world) * slice_rows * h * sizeof(float));
+    return ORDA_ERR_OOM;
+  }
+  cudaIpcMemHandle_t hd;
+  if ((e = cudaIpcGetMemHandle(&hd, p)) != cudaSuccess) {
+    cudaFree(p);
+    return cuda_fail(e, "cudaIpcGetMemHandle", err, err_len);
+  }
+  static_assert(sizeof(hd) <= sizeof(handle_out->bytes), "IPC handle size");
+  std::memset(handle_out->bytes, 0, sizeof(handle_out->bytes));
+  std::memcpy(handle_out->bytes, &hd, sizeof(hd));
+  ctx->slots = static_cast<float*>(p);
+  ctx->slot_world = world;
+  ctx->slot_rank = rank;
+  ctx->slot_slice = static_cast<long long>(slice_rows);
+  ctx->slot_h = static_cast<long long>(h);
+  return ORDA_OK;
+}
+
+int orda_context_slots_attach(OrdaContext* ctx, const OrdaIpcHandle* handles, char* err, size_t err_len) {
+  if (!ctx || !handles || !ctx->slots) {
+    set_error(err, err_len, "invalid argument (create the slot buffer first)");
+    return ORDA_ERR_INVALID;
+  }
+  std::lock_guard<std::mutex> lock(ctx->mu);
+  cudaSetDevice(ctx->device);
+  for (int r = 0; r < ctx->slot_world; ++r) {
+    if (r == ctx->slot_rank) {
+      ctx->slot_peer[r] = ctx->slots;
+      continue;
+    }
+    cudaIpcMemHandle_t hd;
+    std::memcpy(&hd, handles[r].bytes, sizeof(hd));
+    void* p = nullptr;
+    cudaError_t e = cudaIpcOpenMemHandle(&p, hd, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      for (int k = 0; k < r; ++k)
+        if (k != ctx->slot_rank && ctx->slot_peer[k]) {
+          cudaIpcCloseMemHandle(ctx->slot_peer[k]);
+          ctx->slot_peer[k] = nullptr;
+        }
+      return cuda_fail(e, "cudaIpcOpenMemHandle (peer slot buffer)", err, err_len);
+    }
+    ctx->slot_peer[r] = static_cast<float*>(p);
+  }
+  ctx->slots_attached = true;
+  return ORDA_OK;
+}
+
+int orda_reduce_slots_device(OrdaContext* ctx, float* grad_w_slice, size_t ld, const int64_t* labels, size_t n_labels,
+                             int64_t ignore_index, int quantize, int stochastic, uint64_t seed, int8_t* q, float* scale,
+                             void* stream, char* err, size_t err_len) {
+  if (!ctx || !grad_w_slice || (n_labels > 0 && !labels) || !ctx->slots ||
+      ld < static_cast<size_t>(ctx->slot_h)) {
+    set_error(err, err_len, "invalid argument (slot buffer, output slice and its ld >= H)");
+    return ORDA_ERR_INVALID;
+  }
+  std::lock_guard<std::mutex> lock(ctx->mu);
+  cudaSetDevice(ctx->device);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const long long slice = ctx->slot_slice, h = ctx->slot_h;
+  orda::launch_slot_reduce(ctx->slots, ctx->slot_world, slice, h, grad_w_slice, static_cast<long long>(ld), st);
+  ctx->launches += 1;
+  if (quantize) {
+    if (ensure_ws(ctx, round_up(static_cast<size_t>(slice), 256)) != cudaSuccess) {
+      set_error(err, err_len, "device workspace allocation failed");
+      return ORDA_ERR_OOM;
+    }
+    uint8_t* flags = static_cast<uint8_t*>(ctx->ws);
+    cudaError_t e = cudaMemsetAsync(flags, 0, static_cast<size_t>(slice), st);
+    if (e != cudaSuccess) return cuda_fail(e, "memset", err, err_len);
+    const long long row0 = static_cast<long long>(ctx->slot_rank) * slice;
+    orda::launch_target_flags(labels, static_cast<long long>(n_labels), slice, ignore_index, flags, st, row0);
+    orda::launch_quant(grad_w_slice, slice, h, static_cast<long long>(ld), flags, stochastic, seed, q, scale, st, row0);
+    ctx->launches += 2;
+  }
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "slot reduction", err, err_len);
+  ctx->last_stream = st;
+  return ORDA_OK;
+}
+
 void orda_context_destroy(OrdaContext* ctx) {
   if (!ctx) return;
   cudaSetDevice(ctx->device);
   cudaDeviceSynchronize();
+  release_slots(ctx);
   cudaFree(ctx->ws);
   cudaFree(ctx->stage);
   cudaFree(ctx->d_words);

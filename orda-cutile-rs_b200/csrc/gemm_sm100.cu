@@ -232,6 +232,48 @@ __device__ __forceinline__ void stage_and_store(uint8_t* buf, int lane, const ui
   }
 }
 
+// Row-sharded grad_W: the warp's 32 x 32 chunk (times alpha) goes to the
+// ranks that own its rows. The chunk is staged in shared memory in the same
+// swizzled layout as for a TMA store and read back so that each warp store
+// instruction writes four full 128-byte row segments; the destination is
+// this rank's partial slot in the owner's buffer (plain stores, over NVLink
+// for other ranks). beta == 1 accumulates into the slot (backward groups).
+// Requires N and the slot leading dimension to be multiples of 4.
+__device__ __forceinline__ void stage_and_scatter(uint8_t* buf, int lane, const uint32_t (&r)[32], float alpha,
+                                                  const KParams& p, int col0, int row0) {
+  const EpiArgs& e = p.e;
+  __syncwarp();  // every lane has finished reading the previous chunk
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    const float4 q = make_float4(alpha * __uint_as_float(r[4 * c]), alpha * __uint_as_float(r[4 * c + 1]),
+                                 alpha * __uint_as_float(r[4 * c + 2]), alpha * __uint_as_float(r[4 * c + 3]));
+    *reinterpret_cast<float4*>(buf + lane * 128 + ((c ^ (lane & 7)) << 4)) = q;
+  }
+  __syncwarp();
+  const int sub = lane >> 3;  // row within a group of four
+  const int c = lane & 7;     // 16-byte column piece
+  const int col = col0 + c * 4;
+#pragma unroll
+  for (int it = 0; it < 8; ++it) {
+    const int rr = it * 4 + sub;
+    const long long g = static_cast<long long>(row0) + rr;
+    if (g < p.M && col < p.N) {
+      float4 v = *reinterpret_cast<const float4*>(buf + rr * 128 + ((c ^ (rr & 7)) << 4));
+      const long long o = g / e.slot_slice;
+      float* dst = e.slot[o] + (static_cast<long long>(e.slot_rank) * e.slot_slice + (g - o * e.slot_slice)) * e.slot_ld +
+                   col;
+      if (e.beta != 0.0f) {
+        const float4 old = *reinterpret_cast<const float4*>(dst);
+        v.x += e.beta * old.x;
+        v.y += e.beta * old.y;
+        v.z += e.beta * old.z;
+        v.w += e.beta * old.w;
+      }
+      *reinterpret_cast<float4*>(dst) = v;
+    }
+  }
+}
+
 // ------------------------------------------------------------------ kernel
 
 template <int CG, bool A_MN, bool B_MN, int EPI>
@@ -442,8 +484,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           if (col0 >= p.N) return;
           if (p.tma_store) {
             if (row0 < p.M) stage_and_store(buf, lane, r, alpha, &mapC, col0, row0, p.tma_reduce != 0, pol_c);
+          } else if (p.e.scatter) {
+            if (row0 < p.M) stage_and_scatter(buf, lane, r, alpha, p, col0, row0);
+          } else if (row_ok) {
+            epi_store_chunk(p, grow, col0, min(32, p.N - col0), r, alpha);
           }
-          else if (row_ok) epi_store_chunk(p, grow, col0, min(32, p.N - col0), r, alpha);
         };
         // the TMEM load of chunk c+1 is in flight while chunk c is stored
         uint32_t ra[32], rb[32];
@@ -504,6 +549,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
     }
     if (p.tma_store && lane == 0) bulk_wait_all();
+    // scattered stores reach the other ranks' memory before the kernel ends
+    if (p.e.scatter) __threadfence_system();
     __syncwarp();
   }
 
@@ -719,7 +766,13 @@ cudaError_t gemm_launch(const GemmDesc& d, int num_sms, cudaStream_t stream, con
   std::memset(&maps[4], 0, sizeof(CUtensorMap));
   kp.tma_store = 0;
   kp.tma_reduce = 0;
-  if (d.epi == Epi::Logits) {
+  if (d.args.scatter) {
+    if (d.epi != Epi::Store || d.N % 4 != 0 || d.args.slot_ld % 4 != 0 || d.args.slot_slice <= 0 ||
+        (d.M + d.args.slot_slice - 1) / d.args.slot_slice > kMaxSlotRanks) {
+      if (why) *why = "scattered grad_W store needs a plain store, N and the slot ld multiples of 4, <= 8 owners";
+      return cudaErrorInvalidValue;
+    }
+  } else if (d.epi == Epi::Logits) {
     if (out_map_ok(d.args.logits, d.args.ldl) && encode_out_map(&maps[4], d.args.logits, d.M, d.N, d.args.ldl))
       kp.tma_store = 1;
   } else if (d.args.split_row >= d.M && (d.args.beta == 0.0f || d.args.beta == 1.0f) &&

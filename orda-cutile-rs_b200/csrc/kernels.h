@@ -23,6 +23,8 @@ enum class Epi : int { Store = 0, Logits = 1 };
 // split_row go to out0, the rest to out1 (row - split_row).
 // Logits: fp32 logits written to `logits` (ldl) plus per-(row, 128-column
 // part) online-softmax records (see rows.cu for the record layout).
+constexpr int kMaxSlotRanks = 8;  // ranks of one node that a scattered grad_W store can address
+
 struct EpiArgs {
   // Store
   float* out0 = nullptr;
@@ -40,6 +42,15 @@ struct EpiArgs {
   int n_parts = 0;
   float inv_t = 1.0f;
   int own_dT = 0;
+  // Store, scattered to the owners of grad_W rows (row-sharded runs): global
+  // row g belongs to rank o = g / slot_slice and lands in rank o's slot
+  // buffer, at partial slot_rank, row g - o * slot_slice (fp32, ld slot_ld).
+  // slot[o] is rank o's buffer (a peer mapping for o != slot_rank).
+  int scatter = 0;
+  int slot_rank = 0;
+  long long slot_slice = 0;
+  long long slot_ld = 0;
+  float* slot[kMaxSlotRanks] = {};
 };
 
 struct GemmDesc {
@@ -118,13 +129,22 @@ void launch_finalize(const float* nll_s, const float* nll_t, const double* kl_ba
 void launch_f32_to_bf16(const float* src, long long rows, long long cols, uint16_t* dst, long long ld,
                         cudaStream_t stream);
 
-// INT8 row-wise quantisation of grad_W (in place dequantised result).
+// INT8 row-wise quantisation of grad_W (in place dequantised result). Row r
+// of grad_w is row r + row_offset of the full matrix (the stochastic draw
+// index is (r + row_offset) * h + c).
 void launch_quant(float* grad_w, long long v, long long h, long long ld, const uint8_t* target_flags,
-                  int stochastic, uint64_t seed, int8_t* q, float* scale, cudaStream_t stream);
+                  int stochastic, uint64_t seed, int8_t* q, float* scale, cudaStream_t stream,
+                  long long row_offset = 0);
 
-// Marks target rows only (used by the stand-alone quantiser entry).
+// Marks target rows only (used by the stand-alone quantiser entry): label t
+// flags row t - row0 when that lies in [0, v).
 void launch_target_flags(const int64_t* labels, long long bt, long long v, int64_t ignore_index,
-                         uint8_t* target_flags, cudaStream_t stream);
+                         uint8_t* target_flags, cudaStream_t stream, long long row0 = 0);
+
+// out[r, :] = sum over k = 0..world-1 (in that order) of
+// slots[(k * slice + r) * h + :], for r < slice (fp32).
+void launch_slot_reduce(const float* slots, int world, long long slice, long long h, float* out, long long ld,
+                        cudaStream_t stream);
 
 // One-warp kernel whose bounded wait on a never-completed mbarrier expires
 // after limit_ns and records DEV_TIMEOUT_SELFTEST in *status.

@@ -41,7 +41,7 @@ __device__ __forceinline__ float splitmix_uniform(uint64_t seed, uint64_t k) {
 
 __global__ void __launch_bounds__(QT) quant_kernel(float* grad_w, long long h, long long ld,
                                                    const uint8_t* target_flags, int stochastic, uint64_t seed,
-                                                   int8_t* q, float* scale) {
+                                                   int8_t* q, float* scale, long long row_offset) {
   __shared__ float sh[QT / 32];
   const long long r = blockIdx.x;
   float* row = grad_w + r * ld;
@@ -80,7 +80,7 @@ __global__ void __launch_bounds__(QT) quant_kernel(float* grad_w, long long h, l
     } else {
       const float fl = floorf(scaled);
       const float frac = scaled - fl;
-      const float u = splitmix_uniform(seed, static_cast<uint64_t>(r) * static_cast<uint64_t>(h) +
+      const float u = splitmix_uniform(seed, static_cast<uint64_t>(r + row_offset) * static_cast<uint64_t>(h) +
                                                  static_cast<uint64_t>(c));
       qi = to_i8(fl + (frac > u ? 1.0f : 0.0f));
     }
@@ -89,12 +89,50 @@ __global__ void __launch_bounds__(QT) quant_kernel(float* grad_w, long long h, l
   }
 }
 
+// Sum of the world partial slices of a slot buffer, in rank order (the
+// fixed order makes the reduced grad_W independent of arrival order).
+// One CTA per row, 128-bit accesses when the row allows them.
+__global__ void __launch_bounds__(QT) slot_reduce_kernel(const float* __restrict__ slots, int world,
+                                                         long long slice, long long h, float* out, long long ld) {
+  const long long r = blockIdx.x;
+  const long long part = slice * h;
+  float* orow = out + r * ld;
+  const float* srow = slots + r * h;
+  if (h % 4 == 0 && ld % 4 == 0) {
+    for (long long c = threadIdx.x * 4; c < h; c += QT * 4) {
+      float4 acc = *reinterpret_cast<const float4*>(srow + c);
+      for (int k = 1; k < world; ++k) {
+        const float4 x = *reinterpret_cast<const float4*>(srow + k * part + c);
+        acc.x += x.x;
+        acc.y += x.y;
+        acc.z += x.z;
+        acc.w += x.w;
+      }
+      *reinterpret_cast<float4*>(orow + c) = acc;
+    }
+  } else {
+    for (long long c = threadIdx.x; c < h; c += QT) {
+      float acc = srow[c];
+      for (int k = 1; k < world; ++k) acc += srow[k * part + c];
+      orow[c] = acc;
+    }
+  }
+}
+
 }  // namespace
 
 void launch_quant(float* grad_w, long long v, long long h, long long ld, const uint8_t* target_flags,
-                  int stochastic, uint64_t seed, int8_t* q, float* scale, cudaStream_t stream) {
+                  int stochastic, uint64_t seed, int8_t* q, float* scale, cudaStream_t stream,
+                  long long row_offset) {
   if (v <= 0 || h <= 0) return;
-  quant_kernel<<<static_cast<unsigned>(v), QT, 0, stream>>>(grad_w, h, ld, target_flags, stochastic, seed, q, scale);
+  quant_kernel<<<static_cast<unsigned>(v), QT, 0, stream>>>(grad_w, h, ld, target_flags, stochastic, seed, q, scale,
+                                                            row_offset);
+}
+
+void launch_slot_reduce(const float* slots, int world, long long slice, long long h, float* out, long long ld,
+                        cudaStream_t stream) {
+  if (slice <= 0 || h <= 0) return;
+  slot_reduce_kernel<<<static_cast<unsigned>(slice), QT, 0, stream>>>(slots, world, slice, h, out, ld);
 }
 
 }  // namespace orda

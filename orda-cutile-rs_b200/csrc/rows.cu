@@ -440,11 +440,13 @@ __global__ void __launch_bounds__(1024) label_prep_kernel(const int64_t* labels,
 }
 
 __global__ void target_flags_kernel(const int64_t* labels, long long bt, long long v, int64_t ignore_index,
-                                    uint8_t* flags) {
+                                    uint8_t* flags, long long row0) {
   for (long long r = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; r < bt;
        r += static_cast<long long>(gridDim.x) * blockDim.x) {
     const int64_t t = labels[r];
-    if (t != ignore_index && t >= 0 && t < v) flags[t] = 1;
+    if (t == ignore_index) continue;
+    const long long u = static_cast<long long>(t) - row0;
+    if (u >= 0 && u < v) flags[u] = 1;
   }
 }
 
@@ -559,10 +561,10 @@ void launch_label_prep(const int64_t* labels, long long bt, long long v, int64_t
 }
 
 void launch_target_flags(const int64_t* labels, long long bt, long long v, int64_t ignore_index,
-                         uint8_t* target_flags, cudaStream_t stream) {
+                         uint8_t* target_flags, cudaStream_t stream, long long row0) {
   if (bt <= 0) return;
   const int blocks = static_cast<int>((bt + 255) / 256 < 1024 ? (bt + 255) / 256 : 1024);
-  target_flags_kernel<<<blocks, 256, 0, stream>>>(labels, bt, v, ignore_index, target_flags);
+  target_flags_kernel<<<blocks, 256, 0, stream>>>(labels, bt, v, ignore_index, target_flags, row0);
 }
 
 void launch_finalize(const float* nll_s, const float* nll_t, const double* kl_base, const float* s_part, int nseg,

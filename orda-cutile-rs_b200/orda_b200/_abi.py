@@ -126,7 +126,12 @@ class OrdaDeviceOutputs(C.Structure):
 
 
 class OrdaShardOptions(C.Structure):
-    _fields_ = [("global_non_ignore", C.c_int64), ("skip_quantize", C.c_int32)]
+    _fields_ = [("global_non_ignore", C.c_int64), ("skip_quantize", C.c_int32),
+                ("scatter_grad_weight", C.c_int32)]
+
+
+class OrdaIpcHandle(C.Structure):
+    _fields_ = [("bytes", C.c_ubyte * 64)]  # opaque; c_ubyte so no NUL truncation
 
 
 TRY_ALLOC_FN = C.CFUNCTYPE(C.c_int, C.c_size_t, C.c_size_t, C.c_void_p)
@@ -193,6 +198,13 @@ SIGNATURES = {
     "orda_context_phase_times": (C.c_int, [C.c_void_p, C.POINTER(C.c_double), C.POINTER(C.c_uint64)]),
     "orda_context_reset_timing": (None, [C.c_void_p]),
     "orda_context_launch_count": (C.c_uint64, [C.c_void_p]),
+    "orda_context_slots_create": (
+        C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_size_t, C.c_size_t, C.POINTER(OrdaIpcHandle), C.c_char_p,
+                  C.c_size_t]),
+    "orda_context_slots_attach": (C.c_int, [C.c_void_p, C.POINTER(OrdaIpcHandle), C.c_char_p, C.c_size_t]),
+    "orda_reduce_slots_device": (
+        C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p, C.c_size_t, C.c_int64, C.c_int, C.c_int,
+                  C.c_uint64, C.c_void_p, C.c_void_p, C.c_void_p, C.c_char_p, C.c_size_t]),
     "orda_context_selftest_bounded_wait": (C.c_int, [C.c_void_p, C.c_uint32, C.c_void_p, C.c_char_p, C.c_size_t]),
     "orda_distillation_loss_device": (
         C.c_int,

@@ -59,6 +59,37 @@ class DeviceContext:
     def launch_count(self) -> int:
         return int(_lib().orda_context_launch_count(self.handle))
 
+    def slots_create(self, world: int, rank: int, slice_rows: int, h: int) -> bytes:
+        """`orda_context_slots_create`: allocates this rank's slot buffer for
+        the fused grad_W reduce-scatter; returns its 64-byte IPC handle."""
+        hd = _abi.OrdaIpcHandle()
+        buf = _abi.err_buf()
+        _check(_lib().orda_context_slots_create(self.handle, world, rank, slice_rows, h, C.byref(hd), buf, len(buf)),
+               buf)
+        return C.string_at(C.addressof(hd), C.sizeof(hd))
+
+    def slots_attach(self, handles: list) -> None:
+        """`orda_context_slots_attach` with every rank's handle, by rank."""
+        arr = (_abi.OrdaIpcHandle * len(handles))()
+        for i, b in enumerate(handles):
+            b = bytes(b)
+            if len(b) != C.sizeof(_abi.OrdaIpcHandle):
+                raise ValueError(f"IPC handle {i} has {len(b)} bytes")
+            C.memmove(C.addressof(arr[i]), b, len(b))
+        buf = _abi.err_buf()
+        _check(_lib().orda_context_slots_attach(self.handle, arr, buf, len(buf)), buf)
+
+    def reduce_slots(self, grad_w_slice: torch.Tensor, labels: torch.Tensor, ignore_index: int = -100,
+                     quantize: bool = False, stochastic: bool = False, seed: int = 0,
+                     q: Optional[torch.Tensor] = None, scale: Optional[torch.Tensor] = None, stream=None) -> None:
+        """`orda_reduce_slots_device`: this rank's grad_W rows, summed over
+        the ranks' partials (and INT8 round trip when quantize)."""
+        buf = _abi.err_buf()
+        _check(_lib().orda_reduce_slots_device(
+            self.handle, grad_w_slice.data_ptr(), grad_w_slice.stride(0), labels.data_ptr(), labels.numel(),
+            ignore_index, int(quantize), int(stochastic), seed, _ptr(q), _ptr(scale), _stream(stream), buf,
+            len(buf)), buf)
+
     def selftest_bounded_wait(self, limit_us: int = 50000, stream=None) -> None:
         """Runs the bounded-wait self-test kernel (a wait that expires)."""
         buf = _abi.err_buf()
@@ -128,8 +159,11 @@ def distillation_loss_device(
     skip_quantize: bool = False,
     want_int8: bool = False,
     stream=None,
+    scatter_grad_weight: bool = False,
 ) -> DeviceLossResult:
-    """`orda_distillation_loss_device`: bf16 device inputs, fp32 device grads."""
+    """`orda_distillation_loss_device`: bf16 device inputs, fp32 device grads.
+    With scatter_grad_weight the grad_W partial goes to the slot buffers
+    (see DeviceContext.slots_create) and the returned grad_weight is None."""
     opts = opts or LossOptions()
     dev = student_hidden.device
     bt, h = student_hidden.shape
@@ -145,8 +179,10 @@ def distillation_loss_device(
     if gsh is None:
         gsh = torch.empty(bt, h, **f32)
     gw = out.get("grad_weight")
-    if gw is None:
+    if gw is None and not scatter_grad_weight:
         gw = torch.empty(v, h, **f32)
+    if scatter_grad_weight:
+        gw = None
     gth = out.get("grad_teacher_hidden")
     if gth is None and w_t > 0 and live:
         gth = torch.empty(bt, ht, **f32)
@@ -172,8 +208,9 @@ def distillation_loss_device(
     o = _abi.OrdaDeviceOutputs()
     o.grad_student_hidden = gsh.data_ptr()
     o.ld_grad_student_hidden = gsh.stride(0)
-    o.grad_weight = gw.data_ptr()
-    o.ld_grad_weight = gw.stride(0)
+    if gw is not None:
+        o.grad_weight = gw.data_ptr()
+        o.ld_grad_weight = gw.stride(0)
     if gth is not None:
         o.grad_teacher_hidden = gth.data_ptr()
         o.ld_grad_teacher_hidden = gth.stride(0)
@@ -183,7 +220,7 @@ def distillation_loss_device(
     o.grad_weight_q = _ptr(q)
     o.grad_weight_scale = _ptr(sc)
     o.scalars = scal.data_ptr()
-    shard = _abi.OrdaShardOptions(int(global_non_ignore), int(skip_quantize))
+    shard = _abi.OrdaShardOptions(int(global_non_ignore), int(skip_quantize), int(scatter_grad_weight))
     plan = _abi.OrdaChunkPlan()
     buf = _abi.err_buf()
     rc = _lib().orda_distillation_loss_device(

@@ -12,6 +12,9 @@ rows of its vocabulary slice. grad_hidden stays local.
 The collective flow is written against a `compute` callable so the same code
 drives the B200 path (NCCL, CUDA tensors) and the CPU tests (gloo, with the
 oracle as compute).
+
+SlotReduceScatter replaces the NCCL reduce-scatter of grad_W on one node:
+the wgrad GEMM writes each owner's rows into the owner's memory itself.
 """
 from __future__ import annotations
 
@@ -93,3 +96,62 @@ def row_sharded_step(
         shifted = torch.where(labels_all == ignore_index, torch.full_like(labels_all, -1), labels_all - v0)
         quantize(sl, shifted)
     return ShardResult(scalars=scalars, grad_student_hidden=gsh, grad_weight_slice=sl, vocab_range=(v0, v1))
+
+
+class SlotReduceScatter:
+    """The fused grad_W reduce-scatter over the GPUs of one node.
+
+    Every rank allocates a slot buffer fp32 [world][V/world][H] for the grad_W
+    rows it owns and maps the other ranks' buffers (CUDA IPC handles
+    exchanged with an all-gather). The device entry then runs with
+    scatter_grad_weight: its wgrad GEMM stores this rank's partial of every
+    owner's rows straight into that owner's buffer while the GEMM runs, so no
+    separate reduce-scatter pass over grad_W is left. After a barrier the
+    owner sums the partials in rank order (deterministic) and applies the
+    INT8 round trip in the same pass.
+    """
+
+    def __init__(self, ctx, v: int, h: int, group=None):
+        self.ctx = ctx
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.v0, self.v1 = vocab_slice(v, self.world, self.rank)
+        handle = ctx.slots_create(self.world, self.rank, self.v1 - self.v0, h)
+        handles = [None] * self.world
+        dist.all_gather_object(handles, handle, group=group)
+        ctx.slots_attach(handles)
+        dev = torch.device("cuda", torch.cuda.current_device())
+        self._token = torch.zeros(1, device=dev)
+        dist.barrier(group=group)
+
+    def step(
+        self,
+        compute: Callable[[int], tuple[torch.Tensor, torch.Tensor]],
+        labels_local: torch.Tensor,
+        ignore_index: int,
+        n_global: int,
+        grad_weight_slice: torch.Tensor,
+        quantize: bool = False,
+        stochastic: bool = False,
+        seed: int = 0,
+        q: Optional[torch.Tensor] = None,
+        scale: Optional[torch.Tensor] = None,
+        stream=None,
+    ) -> ShardResult:
+        """compute(n_global) -> (scalars[4], grad_student_hidden) runs the
+        local rows with scatter_grad_weight; grad_weight_slice [V/world, H]
+        receives this rank's reduced (and, with quantize, dequantised) rows."""
+        gathered = [torch.empty_like(labels_local) for _ in range(self.world)]
+        dist.all_gather(gathered, labels_local, group=self.group)
+        labels_all = torch.cat(gathered)
+        scalars, gsh = compute(n_global)
+        # the scalar all-reduce is also the barrier after which every rank's
+        # partials have landed in this rank's slot buffer
+        dist.all_reduce(scalars, group=self.group)
+        self.ctx.reduce_slots(grad_weight_slice, labels_all, ignore_index, quantize, stochastic, seed, q, scale,
+                              stream=stream)
+        # the slot buffers are read; the next step's GEMMs may write them
+        dist.all_reduce(self._token, group=self.group)
+        return ShardResult(scalars=scalars, grad_student_hidden=gsh, grad_weight_slice=grad_weight_slice,
+                           vocab_range=(self.v0, self.v1))

@@ -11,6 +11,11 @@ the same bf16 products in another order), and the INT8 codes of the slice
 within one code of the single-GPU ones (a scale computed from a grad_W row
 that differs in the last bits can move a value across a rounding boundary).
 
+Two variants: the NCCL reduce-scatter of the full local grad_W, and the fused
+path in which the wgrad GEMM writes each owner's rows straight into the
+owner's slot buffer (CUDA IPC peer stores) and the owner sums the partials
+and quantises them in one pass.
+
 Skipped unless two GPUs are visible. Ranks run as spawned processes with a
 short process-group timeout; NVLS is off so no rank binds multicast memory.
 """
@@ -52,7 +57,7 @@ def _opts(ob):
     return ob.LossOptions(kd_weight=0.4, temperature=1.5, config=ob.KernelConfig(quantize_grad_weight=True))
 
 
-def _worker(rank, world, port, outdir):
+def _worker(rank, world, port, outdir, mode="nccl"):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     os.environ["NCCL_NVLS_ENABLE"] = "0"
@@ -91,7 +96,24 @@ def _worker(rank, world, port, outdir):
             raw["gw"] = sl.clone()  # the reduced slice before the in-place INT8 round trip
             quantize_grad_w(ctx, sl, shifted, -100, False, 0, q, qs)
 
-        res = shard.row_sharded_step(compute, lab, -100, n_global, quantize=quant)
+        if mode == "nccl":
+            res = shard.row_sharded_step(compute, lab, -100, n_global, quantize=quant)
+        else:
+            # fused: the wgrad GEMM writes the owners' slot buffers; two steps in a
+            # row (the second reuses the buffers), first without the INT8 step to
+            # keep the raw reduced slice, then with it
+            fused = shard.SlotReduceScatter(ctx, V, H)
+
+            def compute_scatter(n):
+                r = distillation_loss_device(ctx, hs[r0:r1].contiguous(), w, lab, ob.TeacherMode.Precomputed,
+                                             teacher_logits=tl[r0:r1].contiguous(), opts=_opts(ob),
+                                             global_non_ignore=n, scatter_grad_weight=True)
+                return r.scalars, r.grad_student_hidden
+
+            sl = torch.full((nsl, H), float("nan"), device=hs.device)
+            fused.step(compute_scatter, lab, -100, n_global, sl)
+            raw["gw"] = sl.clone()
+            res = fused.step(compute_scatter, lab, -100, n_global, sl, quantize=True, q=q, scale=qs)
         torch.cuda.synchronize()
         ctx.check()
         torch.save({"scalars": res.scalars.cpu(), "gsh": res.grad_student_hidden.cpu(), "gw": raw["gw"].cpu(),
@@ -103,7 +125,8 @@ def _worker(rank, world, port, outdir):
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_row_sharded_two_gpus_match_single_gpu(ob, tmp_path):
+@pytest.mark.parametrize("mode", ["nccl", "fused"])
+def test_row_sharded_two_gpus_match_single_gpu(ob, tmp_path, mode):
     import torch.multiprocessing as mp
 
     from conftest import rel_l2
@@ -112,7 +135,7 @@ def test_row_sharded_two_gpus_match_single_gpu(ob, tmp_path):
     world = 2
     ctxm = mp.get_context("spawn")
     port = _free_port()
-    procs = [ctxm.Process(target=_worker, args=(r, world, port, str(tmp_path))) for r in range(world)]
+    procs = [ctxm.Process(target=_worker, args=(r, world, port, str(tmp_path), mode)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
