@@ -256,7 +256,10 @@ def run_ours(args):
             out["grad_weight_q"], out["grad_weight_scale"] = q, qs
             return distillation_loss_device(ctx, hs, w, labels, ob.TeacherMode.Precomputed, teacher_logits=tl,
                                             opts=opts, out=out, want_int8=True, stream=stream)
-        ev = [torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)]
+        # events: [0] device entry done, [1] step done, [2] barrier passed,
+        # [3] slot reduction done, [4] step start
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+        ev[4].record(stream)
 
         if fused:
             def compute_scatter(n):
@@ -267,7 +270,7 @@ def run_ours(args):
                 return r.scalars, r.grad_student_hidden
 
             res = fused.step(compute_scatter, labels, -100, n_global, gw_slice, quantize=True, q=q, scale=qs,
-                             stream=stream)
+                             stream=stream, marks=ev[2:4])
         else:
             def compute(n):
                 r = distillation_loss_device(ctx, hs, w, labels, ob.TeacherMode.Precomputed, teacher_logits=tl,
@@ -316,7 +319,19 @@ def run_ours(args):
     ms_total = ev0.elapsed_time(ev1)
     # N > 1: time from the end of the device entry to the end of the step
     # (scalar all-reduce, grad_W reduction and the slice's INT8 round trip)
-    collective_ms = statistics.mean(a.elapsed_time(b) for a, b in marks) if marks else None
+    collective_ms = statistics.mean(ev[0].elapsed_time(ev[1]) for ev in marks) if marks else None
+    rank_split = None
+    if world > 1:
+        # per rank: device-entry time, then (fused path) the wait at the
+        # barrier and the slot reduction, averaged over the timed steps
+        mine = [statistics.mean(ev[4].elapsed_time(ev[0]) for ev in marks)]
+        if fused:
+            mine += [statistics.mean(ev[0].elapsed_time(ev[2]) for ev in marks),
+                     statistics.mean(ev[2].elapsed_time(ev[3]) for ev in marks)]
+        t = torch.tensor(mine, device=dev, dtype=torch.float64)
+        allt = [torch.empty_like(t) for _ in range(world)]
+        dist.all_gather(allt, t)
+        rank_split = [[round(x, 3) for x in a.tolist()] for a in allt]
     phases = ctx.phase_times()
     ctx.enable_timing(False)
     launches = ctx.launch_count() - launches0
@@ -364,6 +379,8 @@ def run_ours(args):
         "step_tflops_per_gpu": step_tflops, "step_frac_of_peak": step_tflops / peak,
         "phases_ms_per_step": {k: v_[0] / args.steps for k, v_ in phases.items()},
         "host_enqueue_ms_per_step": host_ms, "collective_ms_per_step": collective_ms,
+        "per_rank_ms": ({"fields": ["device_entry", "barrier_wait", "slot_reduce_quant"] if fused
+                         else ["device_entry"], "ranks": rank_split} if rank_split else None),
         "roofline": roofline, "gpu_launches": int(launches), "clocks": clocks,
     }
 

@@ -138,10 +138,13 @@ class SlotReduceScatter:
         q: Optional[torch.Tensor] = None,
         scale: Optional[torch.Tensor] = None,
         stream=None,
+        marks: Optional[list] = None,
     ) -> ShardResult:
         """compute(n_global) -> (scalars[4], grad_student_hidden) runs the
         local rows with scatter_grad_weight; grad_weight_slice [V/world, H]
-        receives this rank's reduced (and, with quantize, dequantised) rows."""
+        receives this rank's reduced (and, with quantize, dequantised) rows.
+        marks (optional): two CUDA events, recorded after the barrier and
+        after the reduction, for timing."""
         gathered = [torch.empty_like(labels_local) for _ in range(self.world)]
         dist.all_gather(gathered, labels_local, group=self.group)
         labels_all = torch.cat(gathered)
@@ -149,8 +152,12 @@ class SlotReduceScatter:
         # the scalar all-reduce is also the barrier after which every rank's
         # partials have landed in this rank's slot buffer
         dist.all_reduce(scalars, group=self.group)
+        if marks is not None:
+            marks[0].record(stream)
         self.ctx.reduce_slots(grad_weight_slice, labels_all, ignore_index, quantize, stochastic, seed, q, scale,
                               stream=stream)
+        if marks is not None:
+            marks[1].record(stream)
         # the slot buffers are read; the next step's GEMMs may write them
         dist.all_reduce(self._token, group=self.group)
         return ShardResult(scalars=scalars, grad_student_hidden=gsh, grad_weight_slice=grad_weight_slice,
