@@ -295,6 +295,49 @@ ORDA_API int orda_distillation_loss_device(OrdaContext* ctx, const OrdaDeviceMat
                                   const OrdaDeviceOutputs* out, const OrdaShardOptions* shard,
                                   void* stream, OrdaChunkPlan* plan_out, char* err, size_t err_len);
 
+/* Vocabulary-sharded calls (tensor parallel over the output head) for the
+ * largest vocabularies: rank r of `world` holds W rows [v0, v0 + V_r) of the
+ * full v_total (and the same rows of a Separate teacher's W, or the same
+ * columns of Precomputed teacher logits) and every rank holds all BT rows of
+ * the hidden states and labels. No counterpart in the reference, which runs
+ * on one device; the loss and gradients are those of `distillation_loss`
+ * (src/api.rs:188-422) on the full vocabulary:
+ *   1. orda_vocab_forward_device: the slice's logits GEMMs; writes one tuple
+ *      of ORDA_VOCAB_TUPLE floats per row (the slice's max / sum-exp
+ *      statistics of student and teacher and the label's logits when the
+ *      slice holds the label column) to row_partials [bt][ORDA_VOCAB_TUPLE];
+ *   2. the caller all-gathers the tuples of every rank, by rank, into
+ *      [world][bt][ORDA_VOCAB_TUPLE] (e.g. an NCCL all-gather);
+ *   3. orda_vocab_backward_device on the same context and inputs: merges the
+ *      tuples (rank order, f64), the gradient pass over the slice and the
+ *      backward GEMMs. Outputs: grad_weight / grad_teacher_weight = this
+ *      slice's rows [V_r, H] (complete), grad_student_hidden /
+ *      grad_teacher_hidden = this rank's partial sums over its slice, and
+ *      scalars = this rank's partial scalars: sum both over the ranks (e.g.
+ *      an NCCL all-reduce). Exactly one rank sets include_rows = 1 (it adds
+ *      the per-row CE and KL terms to its scalars). The INT8 round trip, if
+ *      configured, runs on the slice (target rows = labels in the slice).
+ * The slice logits of the whole batch stay in the context's workspace
+ * between the two calls; nothing else may run on the context in between. */
+#define ORDA_VOCAB_TUPLE 12
+typedef struct OrdaVocabShard {
+  int64_t v_total;      /* full vocabulary */
+  int64_t v0;           /* first vocabulary row of this rank's slice */
+  int32_t world;        /* ranks whose tuples phase 2 merges */
+  int32_t include_rows; /* phase 2: 1 on exactly one rank */
+} OrdaVocabShard;
+ORDA_API int orda_vocab_forward_device(OrdaContext* ctx, const OrdaDeviceMat* student_hidden,
+                                       const OrdaDeviceMat* weight_slice, const int64_t* labels, size_t bt,
+                                       const OrdaDeviceTeacher* teacher, const OrdaLossOptions* opts,
+                                       const OrdaVocabShard* vs, float* row_partials, void* stream, char* err,
+                                       size_t err_len);
+ORDA_API int orda_vocab_backward_device(OrdaContext* ctx, const OrdaDeviceMat* student_hidden,
+                                        const OrdaDeviceMat* weight_slice, const int64_t* labels, size_t bt,
+                                        const OrdaDeviceTeacher* teacher, const OrdaLossOptions* opts,
+                                        const OrdaVocabShard* vs, const float* all_partials,
+                                        const OrdaDeviceOutputs* out, void* stream, OrdaChunkPlan* plan_out,
+                                        char* err, size_t err_len);
+
 /* Fused grad_W reduce-scatter for row-sharded runs on the GPUs of one node
  * (up to 8 ranks, one process per GPU). There is no counterpart in the
  * reference, which runs on one device; for data-parallel callers that

@@ -74,6 +74,12 @@ struct OrdaContext {
   long long slot_h = 0;
   float* slot_peer[orda::kMaxSlotRanks] = {};  // rank -> its slot buffer (IPC mapping for other ranks)
   bool slots_attached = false;
+  // Vocabulary-sharded calls: the workspace layout and shapes of the last
+  // orda_vocab_forward_device, whose slice logits the backward phase reuses.
+  bool vocab_ready = false;
+  size_t vocab_bt = 0, vocab_v = 0, vocab_h = 0;
+  OrdaChunkPlan vocab_plan{};
+  size_t vocab_layout[24] = {};
 };
 
 namespace orda {
@@ -248,8 +254,26 @@ int cuda_fail(cudaError_t e, const char* what, char* err, size_t len) {
   return ORDA_ERR_CUDA;
 }
 
+// A vocabulary-sharded call: this rank's W (and teacher) rows are
+// [v0, v0 + V) of v_total. Phase 1 runs the slice's logits GEMMs and writes
+// one partial statistics tuple per row; phase 2 (after the caller gathered
+// every rank's tuples) merges them and runs the gradient pass and the
+// backward GEMMs of the slice.
+static_assert(kVocabTuple == ORDA_VOCAB_TUPLE, "tuple size of the C ABI");
+
+struct VocabCall {
+  int phase = 0;
+  long long v_total = 0, v0 = 0;
+  float* partials_out = nullptr;
+  const float* partials_in = nullptr;
+  int world = 1;
+  int include_rows = 1;
+};
+
 int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, const OrdaDeviceOutputs& out,
-               const OrdaShardOptions* shard, cudaStream_t st, OrdaChunkPlan* plan_out, char* err, size_t len) {
+               const OrdaShardOptions* shard, cudaStream_t st, OrdaChunkPlan* plan_out, char* err, size_t len,
+               const VocabCall* vc = nullptr) {
+  const int vphase = vc ? vc->phase : 0;
   Flags f{};
   f.w_s = o.student_ce_weight;
   f.w_t = o.has_teacher_ce_weight ? o.teacher_ce_weight : orda_default_teacher_ce_weight(in.mode);
@@ -268,8 +292,19 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
   const bool scatter = shard && shard->scatter_grad_weight;
   f.quant = o.config.quantize_grad_weight != 0 && !(shard && shard->skip_quantize) && !scatter;
 
-  if (!out.grad_student_hidden || (!out.grad_weight && !scatter) || !out.scalars) {
+  if (vphase == 1) {
+    if (!vc->partials_out) {
+      set_error(err, len, "row_partials output is required");
+      return ORDA_ERR_INVALID;
+    }
+  } else if (!out.grad_student_hidden || (!out.grad_weight && !scatter) || !out.scalars) {
     set_error(err, len, "grad_student_hidden, grad_weight and scalars outputs are required");
+    return ORDA_ERR_INVALID;
+  }
+  if (vphase && (vc->v0 < 0 || vc->v0 + static_cast<long long>(in.v) > vc->v_total || vc->world < 1 ||
+                 (vphase == 2 && !vc->partials_in))) {
+    set_error(err, len, "vocabulary shard out of range (v0 = %lld, slice rows = %zu, v_total = %lld)", vc->v0, in.v,
+              vc->v_total);
     return ORDA_ERR_INVALID;
   }
   if (scatter) {
@@ -284,26 +319,54 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
       return ORDA_ERR_INVALID;
     }
   }
-  if (f.teacher_grad && !out.grad_teacher_hidden) {
+  if (vphase != 1 && f.teacher_grad && !out.grad_teacher_hidden) {
     set_error(err, len, "grad_teacher_hidden output is required (teacher CE weight > 0 with a live teacher)");
     return ORDA_ERR_INVALID;
   }
-  if (f.teacher_grad && in.mode == ORDA_TEACHER_SEPARATE && !out.grad_teacher_weight) {
+  if (vphase != 1 && f.teacher_grad && in.mode == ORDA_TEACHER_SEPARATE && !out.grad_teacher_weight) {
     set_error(err, len, "grad_teacher_weight output is required (Separate teacher with teacher CE weight > 0)");
     return ORDA_ERR_INVALID;
   }
 
   const size_t bt = in.bt, v = in.v, h = in.h, ht = in.ht_dim;
-  OrdaChunkPlan plan = resolve_chunk_size(bt, o.chunk_size, true, v, o.config.has_max_chunks != 0,
-                                          o.config.max_chunks);
+  // the plan of the full vocabulary (a vocabulary-sharded call reports the
+  // plan the single-device call would use)
+  OrdaChunkPlan plan = resolve_chunk_size(bt, o.chunk_size, true, vphase ? static_cast<size_t>(vc->v_total) : v,
+                                          o.config.has_max_chunks != 0, o.config.max_chunks);
   const size_t limit = o.config.has_max_chunks ? o.config.max_chunks : default_max_chunks_limit(bt);
   AllocTry at{ctx, &in, &f, {}};
   OrdaChunkPlan used{};
-  // Rung 0 is the resolver's plan itself (a Fixed chunk size keeps its row
-  // count); after an allocation failure the ladder doubles the chunk count
-  // along chunk_doubling_schedule, as the upstream dispatcher does.
-  bool have = try_alloc_cb(plan.num_chunks, plan.chunk_size, &at) == 0;
-  if (have) used = plan;
+  static_assert(sizeof(WsLayout) <= sizeof(ctx->vocab_layout), "saved layout");
+  bool have = false;
+  if (vphase == 2) {
+    // the forward phase's workspace, with its slice logits and statistics
+    if (!ctx->vocab_ready || ctx->vocab_bt != bt || ctx->vocab_v != v || ctx->vocab_h != h) {
+      set_error(err, len, "orda_vocab_backward_device must follow orda_vocab_forward_device on the same context "
+                          "with the same shapes");
+      return ORDA_ERR_INVALID;
+    }
+    std::memcpy(&at.layout, ctx->vocab_layout, sizeof(WsLayout));
+    used = ctx->vocab_plan;
+    have = true;
+  } else if (vphase == 1) {
+    // the slice logits of the whole batch stay in the workspace until the
+    // backward phase: one forward and one backward group
+    ctx->vocab_ready = false;
+    at.layout = make_layout(in, f, plan.chunk_size, bt, bt);
+    if (ensure_ws(ctx, at.layout.total) != cudaSuccess) {
+      set_error(err, len, "vocabulary-sharded calls keep the whole batch's slice logits between the two phases: "
+                          "%zu bytes of workspace are not available", at.layout.total);
+      return ORDA_ERR_OOM;
+    }
+    used = plan;
+    have = true;
+  } else {
+    // Rung 0 is the resolver's plan itself (a Fixed chunk size keeps its row
+    // count); after an allocation failure the ladder doubles the chunk count
+    // along chunk_doubling_schedule, as the upstream dispatcher does.
+    have = try_alloc_cb(plan.num_chunks, plan.chunk_size, &at) == 0;
+    if (have) used = plan;
+  }
   if (!have) {
     for (size_t nc : chunk_doubling_schedule(bt, plan.num_chunks, std::max(limit, plan.num_chunks))) {
       if (nc <= plan.num_chunks) continue;
@@ -338,15 +401,24 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
   int* status = ctx->d_words;
 
   cudaError_t e;
-  if ((e = cudaMemsetAsync(ctx->d_words, 0, 2 * sizeof(int), st)) != cudaSuccess) return cuda_fail(e, "memset", err, len);
-  if (tflags && (e = cudaMemsetAsync(tflags, 0, v, st)) != cudaSuccess) return cuda_fail(e, "memset", err, len);
   const long long denom_override = shard ? shard->global_non_ignore : 0;
-  {
+  if (vphase != 2) {
+    if ((e = cudaMemsetAsync(ctx->d_words, 0, 2 * sizeof(int), st)) != cudaSuccess)
+      return cuda_fail(e, "memset", err, len);
+    if (tflags && (e = cudaMemsetAsync(tflags, 0, v, st)) != cudaSuccess) return cuda_fail(e, "memset", err, len);
     Phase ph_prep(ctx, 5, st);
     ph_prep.launched();
-    launch_label_prep(in.labels, static_cast<long long>(bt), static_cast<long long>(v), o.ignore_index,
+    // labels are checked against the full vocabulary; a slice's target rows
+    // are the labels that fall in it
+    launch_label_prep(in.labels, static_cast<long long>(bt),
+                      vphase ? vc->v_total : static_cast<long long>(v), o.ignore_index,
                       o.reduction == ORDA_REDUCTION_SUM, denom_override, ctx->d_words + 1, ctx->d_mean_scale,
-                      tflags, status, st);
+                      vphase ? nullptr : tflags, status, st);
+    if (vphase && tflags) {
+      ph_prep.launched();
+      launch_target_flags(in.labels, static_cast<long long>(bt), static_cast<long long>(v), o.ignore_index, tflags,
+                          st, vc->v0);
+    }
   }
 
   const float inv_t = 1.0f / f.temperature;
@@ -363,7 +435,7 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
                                                                    s * in.ld_t_logits * t_esz);
       const long long t_ld = live_teacher ? static_cast<long long>(L.ldv) : in.ld_t_logits;
       const int t_bf16 = live_teacher ? 0 : static_cast<int>(in.t_logits_bf16);
-      {
+      if (vphase != 2) {
         Phase ph_fwd(ctx, 0, st);
         // ---- teacher logits + statistics (Tied / Separate)
         if (f.teacher_rows) {
@@ -411,11 +483,11 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
       // ---- row pass: teacher statistics (given logits), losses, logit gradients
       {
         Phase ph_rows(ctx, 1, st);
-        if (f.need_teacher && !live_teacher) {
+        if (vphase != 2 && f.need_teacher && !live_teacher) {
           ph_rows.launched();
           launch_teacher_stats(t_rows, t_ld, t_bf16, static_cast<int>(n), static_cast<int>(v), inv_t, rec_own_t, st);
         }
-        ph_rows.launched(kRowLaunches);
+        ph_rows.launched(vphase == 1 ? 1 : kRowLaunches);
         RowArgs r{};
         r.n = static_cast<int>(n);
         r.v = static_cast<int>(v);
@@ -449,10 +521,20 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
         r.nseg = static_cast<int>(L.nseg);
         r.row_const = row_const;
         r.num_sms = ctx->num_sms;
-        launch_rows(r, st);
+        if (vphase) {
+          r.v_total = static_cast<int>(vc->v_total);
+          r.v0 = vc->v0;
+          r.world = vc->world;
+          r.partials_out = vphase == 1 ? vc->partials_out + s * kVocabTuple : nullptr;
+          r.partials_in = vphase == 2 ? vc->partials_in : nullptr;
+        }
+        if (vphase == 1) launch_vocab_partials(r, st);
+        else if (vphase == 2) launch_vocab_rows(r, st);
+        else launch_rows(r, st);
         if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(e, "row kernels", err, len);
       }
     }
+    if (vphase == 1) continue;  // the backward phase follows the exchange of the partials
     const long long rows_g = static_cast<long long>(g1 - g0);
     const long long vv = static_cast<long long>(v);
     // ---- dgrad: grad_h rows = mean_scale * dlogits @ W
@@ -543,12 +625,23 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
         return cuda_fail(e, why ? why : "teacher wgrad GEMM", err, len);
     }
   }
+  if (vphase == 1) {
+    if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(e, "vocabulary forward phase", err, len);
+    std::memcpy(ctx->vocab_layout, &L, sizeof(WsLayout));
+    ctx->vocab_bt = bt;
+    ctx->vocab_v = v;
+    ctx->vocab_h = h;
+    ctx->vocab_plan = used;
+    ctx->vocab_ready = true;
+    ctx->last_stream = st;
+    return ORDA_OK;
+  }
   {
     Phase ph(ctx, 5, st);
     ph.launched();
     const double t_sq = static_cast<double>(f.temperature * f.temperature);
     launch_finalize(nll_s, nll_t, kl_base, s_part, static_cast<int>(L.nseg), t_sq, static_cast<long long>(bt),
-                    ctx->d_mean_scale, f.w_s, f.w_t, f.kd, out.scalars, st);
+                    ctx->d_mean_scale, f.w_s, f.w_t, f.kd, out.scalars, st, vphase == 2 ? vc->include_rows : 1);
   }
   if (f.quant) {
     Phase ph(ctx, 4, st);
@@ -556,8 +649,9 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
     const uint64_t seed = o.config.has_stochastic_seed ? o.config.stochastic_seed : 0;
     launch_quant(out.grad_weight, static_cast<long long>(v), static_cast<long long>(h),
                  static_cast<long long>(out.ld_grad_weight), tflags, o.config.stochastic_rounding, seed,
-                 out.grad_weight_q, out.grad_weight_scale, st);
+                 out.grad_weight_q, out.grad_weight_scale, st, vphase == 2 ? vc->v0 : 0);
   }
+  if (vphase == 2) ctx->vocab_ready = false;
   if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(e, "kernel launch", err, len);
   ctx->last_stream = st;
   return ORDA_OK;
@@ -831,16 +925,11 @@ static bool dev_mat_ok(const OrdaDeviceMat& m, bool need_bf16) {
   return true;
 }
 
-int orda_distillation_loss_device(OrdaContext* ctx, const OrdaDeviceMat* student_hidden, const OrdaDeviceMat* weight,
-                                  const int64_t* labels, size_t bt, const OrdaDeviceTeacher* teacher,
-                                  const OrdaLossOptions* opts, const OrdaDeviceOutputs* out,
-                                  const OrdaShardOptions* shard, void* stream, OrdaChunkPlan* plan_out, char* err,
-                                  size_t err_len) {
-  if (!ctx || !student_hidden || !weight || !labels || !teacher || !opts || !out) {
-    set_error(err, err_len, "null argument");
-    return ORDA_ERR_INVALID;
-  }
-  std::lock_guard<std::mutex> lock(ctx->mu);
+// Validates the device-entry arguments (shapes, scalars, dtypes, alignment)
+// and describes the inputs for run_device.
+static int build_dev_inputs(const OrdaDeviceMat* student_hidden, const OrdaDeviceMat* weight, const int64_t* labels,
+                            size_t bt, const OrdaDeviceTeacher* teacher, const OrdaLossOptions* opts, DevInputs* out_in,
+                            char* err, size_t err_len) {
   const Shape2 sh{student_hidden->rows, student_hidden->cols}, w{weight->rows, weight->cols};
   const Shape2 th{teacher->hidden.rows, teacher->hidden.cols}, tw{teacher->weight.rows, teacher->weight.cols},
       tl{teacher->logits.rows, teacher->logits.cols};
@@ -855,7 +944,7 @@ int orda_distillation_loss_device(OrdaContext* ctx, const OrdaDeviceMat* student
     set_error(err, err_len, "student_hidden and weight must be bf16, 16-byte aligned, with ld*2 a multiple of 16");
     return ORDA_ERR_INVALID;
   }
-  DevInputs in;
+  DevInputs& in = *out_in;
   in.bt = bt;
   in.h = h;
   in.v = v;
@@ -891,8 +980,68 @@ int orda_distillation_loss_device(OrdaContext* ctx, const OrdaDeviceMat* student
     in.ld_t_logits = static_cast<long long>(teacher->logits.ld);
     in.t_logits_bf16 = teacher->logits.dtype == ORDA_DTYPE_BF16;
   }
+  return ORDA_OK;
+}
+
+int orda_distillation_loss_device(OrdaContext* ctx, const OrdaDeviceMat* student_hidden, const OrdaDeviceMat* weight,
+                                  const int64_t* labels, size_t bt, const OrdaDeviceTeacher* teacher,
+                                  const OrdaLossOptions* opts, const OrdaDeviceOutputs* out,
+                                  const OrdaShardOptions* shard, void* stream, OrdaChunkPlan* plan_out, char* err,
+                                  size_t err_len) {
+  if (!ctx || !student_hidden || !weight || !labels || !teacher || !opts || !out) {
+    set_error(err, err_len, "null argument");
+    return ORDA_ERR_INVALID;
+  }
+  std::lock_guard<std::mutex> lock(ctx->mu);
+  DevInputs in;
+  if (int rc = build_dev_inputs(student_hidden, weight, labels, bt, teacher, opts, &in, err, err_len)) return rc;
   cudaSetDevice(ctx->device);
   return run_device(ctx, in, *opts, *out, shard, static_cast<cudaStream_t>(stream), plan_out, err, err_len);
+}
+
+int orda_vocab_forward_device(OrdaContext* ctx, const OrdaDeviceMat* student_hidden, const OrdaDeviceMat* weight_slice,
+                              const int64_t* labels, size_t bt, const OrdaDeviceTeacher* teacher,
+                              const OrdaLossOptions* opts, const OrdaVocabShard* vs, float* row_partials, void* stream,
+                              char* err, size_t err_len) {
+  if (!ctx || !student_hidden || !weight_slice || !labels || !teacher || !opts || !vs || !row_partials) {
+    set_error(err, err_len, "null argument");
+    return ORDA_ERR_INVALID;
+  }
+  std::lock_guard<std::mutex> lock(ctx->mu);
+  DevInputs in;
+  if (int rc = build_dev_inputs(student_hidden, weight_slice, labels, bt, teacher, opts, &in, err, err_len)) return rc;
+  cudaSetDevice(ctx->device);
+  VocabCall vc;
+  vc.phase = 1;
+  vc.v_total = vs->v_total;
+  vc.v0 = vs->v0;
+  vc.world = vs->world;
+  vc.partials_out = row_partials;
+  OrdaDeviceOutputs none{};
+  return run_device(ctx, in, *opts, none, nullptr, static_cast<cudaStream_t>(stream), nullptr, err, err_len, &vc);
+}
+
+int orda_vocab_backward_device(OrdaContext* ctx, const OrdaDeviceMat* student_hidden,
+                               const OrdaDeviceMat* weight_slice, const int64_t* labels, size_t bt,
+                               const OrdaDeviceTeacher* teacher, const OrdaLossOptions* opts, const OrdaVocabShard* vs,
+                               const float* all_partials, const OrdaDeviceOutputs* out, void* stream,
+                               OrdaChunkPlan* plan_out, char* err, size_t err_len) {
+  if (!ctx || !student_hidden || !weight_slice || !labels || !teacher || !opts || !vs || !all_partials || !out) {
+    set_error(err, err_len, "null argument");
+    return ORDA_ERR_INVALID;
+  }
+  std::lock_guard<std::mutex> lock(ctx->mu);
+  DevInputs in;
+  if (int rc = build_dev_inputs(student_hidden, weight_slice, labels, bt, teacher, opts, &in, err, err_len)) return rc;
+  cudaSetDevice(ctx->device);
+  VocabCall vc;
+  vc.phase = 2;
+  vc.v_total = vs->v_total;
+  vc.v0 = vs->v0;
+  vc.world = vs->world;
+  vc.include_rows = vs->include_rows;
+  vc.partials_in = all_partials;
+  return run_device(ctx, in, *opts, *out, nullptr, static_cast<cudaStream_t>(stream), plan_out, err, err_len, &vc);
 }
 
 int orda_quantize_grad_w_device(OrdaContext* ctx, float* grad_w, size_t v, size_t h, size_t ld, const int64_t* labels,

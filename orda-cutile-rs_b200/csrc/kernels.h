@@ -100,13 +100,30 @@ struct RowArgs {
   int nseg;               // column segments of the gradient pass
   void* row_const;        // [n] x 32 B scratch: per-row constants (stats -> gradient kernel)
   int num_sms;
+  // Vocabulary-sharded calls: this rank's logits cover vocabulary rows
+  // [v0, v0 + v) of v_total (0 = not sharded: v_total = v, v0 = 0).
+  int v_total;
+  long long v0;
+  float* partials_out;       // phase 1: [n][kVocabTuple] partial row statistics of the slice
+  const float* partials_in;  // phase 2: [world][n][kVocabTuple] every rank's partials, by rank
+  int world;
 };
+// Partial row statistics of one vocabulary slice: student (m, sum e^(x-m),
+// sum e^((x-m)/T), sum x), teacher (same), the label's student and teacher
+// logits and 1 when the label column lies in the slice (else 0), one pad.
+constexpr int kVocabTuple = 12;
 // Two launches: the per-row statistics kernel and the gradient kernel.
 constexpr int kRowLaunches = 2;
 constexpr size_t kRowConstBytes = 32;
 // Columns per CTA of the gradient pass (256 threads x 8 columns x 4 steps).
 constexpr int kGradSegCols = 8192;
 void launch_rows(const RowArgs& a, cudaStream_t stream);
+// Vocabulary-sharded phase 1: merges the slice's records of every row into
+// one partial tuple (partials_out).
+void launch_vocab_partials(const RowArgs& a, cudaStream_t stream);
+// Vocabulary-sharded phase 2: merges every rank's tuple of each row (rank
+// order), per-row losses and constants, then the slice's gradient pass.
+void launch_vocab_rows(const RowArgs& a, cudaStream_t stream);
 
 // Teacher statistics pre-pass over given teacher logits (Precomputed mode):
 // one (max, sum e^(t-m), sum e^((t-m)/T), sum t) record per row.
@@ -120,10 +137,13 @@ void launch_label_prep(const int64_t* labels, long long bt, long long v, int64_t
                        int* status, cudaStream_t stream);
 
 // Final deterministic reduction of per-row losses into the four scalars:
-// KL_row = (kl_base + sum over segments of s_part) * T^2.
+// KL_row = (kl_base + sum over segments of s_part) * T^2. include_rows = 0
+// leaves out the per-row terms (NLLs, KL base) and keeps only this rank's
+// KL cross-term segments: the partial scalars of one vocabulary slice, which
+// add up over the ranks when exactly one rank includes the rows.
 void launch_finalize(const float* nll_s, const float* nll_t, const double* kl_base, const float* s_part, int nseg,
                      double t_sq, long long bt, const float* mean_scale, float w_s, float w_t, float kd,
-                     float* scalars, cudaStream_t stream);
+                     float* scalars, cudaStream_t stream, int include_rows = 1);
 
 // f32 -> bf16 (round to nearest even) into a padded row-major buffer.
 void launch_f32_to_bf16(const float* src, long long rows, long long cols, uint16_t* dst, long long ld,

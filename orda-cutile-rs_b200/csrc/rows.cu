@@ -140,31 +140,38 @@ struct RowConst {
   int pad0, pad1;
 };
 
-// ---- one CTA per row: merge records, per-row losses, constants.
-__global__ void __launch_bounds__(ROW_THREADS) row_stats_kernel(const RowArgs a) {
-  __shared__ double sh[3 * 32];
-  const int i = blockIdx.x;
-  const double inv_t = static_cast<double>(a.inv_t);
-  const bool want_t = a.need_kl || a.teacher_ce;
+__device__ __forceinline__ int vocab_total(const RowArgs& a) { return a.v_total > 0 ? a.v_total : a.v; }
 
-  const Acc own = merge_row(a.rec_own, i, a.n_parts, inv_t, sh);
-  const Acc ts = want_t ? merge_row(a.rec_own_t, i, a.n_parts_t, inv_t, sh) : Acc{0.0, 1.0, 1.0, 0.0};
-  if (threadIdx.x != 0) return;
-
+// Row i's label: ignored (ignore_index or out of [0, V): range errors are
+// reported by the label pass) or its global column.
+__device__ __forceinline__ bool row_label(const RowArgs& a, int i, long long& y) {
   const int64_t y64 = a.labels[i];
-  int ignored = y64 == a.ignore_index;
-  if (!ignored && (y64 < 0 || y64 >= a.v)) ignored = 1;  // range errors are reported by the label pass
-  const int y = ignored ? 0 : static_cast<int>(y64);
+  y = static_cast<long long>(y64);
+  return y64 == a.ignore_index || y64 < 0 || y64 >= vocab_total(a);
+}
+
+__device__ __forceinline__ double teacher_value(const RowArgs& a, long long i, long long col) {
+  if (a.teacher_is_bf16) {
+    const uint16_t b = static_cast<const uint16_t*>(a.teacher)[i * a.ld_teacher + col];
+    return static_cast<double>(__uint_as_float(static_cast<uint32_t>(b) << 16));
+  }
+  return static_cast<double>(static_cast<const float*>(a.teacher)[i * a.ld_teacher + col]);
+}
+
+// Per-row losses and constants of row i from its merged statistics (own:
+// student, ts: teacher) and the student / teacher logits at the label
+// (x_y, t_y; unused for ignored rows). y_local is the label's column in this
+// rank's logits, or -1 when another rank holds it. Smoothing uses the full
+// vocabulary (alpha / V_total).
+__device__ void finish_row(const RowArgs& a, int i, const Acc& own, const Acc& ts, bool ignored, double x_y,
+                           double t_y, int y_local) {
+  const double inv_t = static_cast<double>(a.inv_t);
   const double alpha = static_cast<double>(a.alpha);
-  const double vd = static_cast<double>(a.v);
-  const float* xs = a.logits_s + static_cast<long long>(i) * a.ldl;
+  const double vd = static_cast<double>(vocab_total(a));
 
   const double lse_s1 = own.m + log(own.d1);
   double nll_s = 0.0;
-  if (!ignored) {
-    const double x_y = static_cast<double>(xs[y]);
-    nll_s = alpha > 0.0 ? lse_s1 - (1.0 - alpha) * x_y - (alpha / vd) * own.sx : lse_s1 - x_y;
-  }
+  if (!ignored) nll_s = alpha > 0.0 ? lse_s1 - (1.0 - alpha) * x_y - (alpha / vd) * own.sx : lse_s1 - x_y;
   a.nll_s_rows[i] = static_cast<float>(nll_s);
 
   double lse_sT = 0.0, lse_tT = 0.0;
@@ -178,16 +185,7 @@ __global__ void __launch_bounds__(ROW_THREADS) row_stats_kernel(const RowArgs a)
   if (a.teacher_ce) {
     lse_t1 = ts.m + log(ts.d1);
     double nll_t = 0.0;
-    if (!ignored) {
-      double t_y;
-      if (a.teacher_is_bf16) {
-        const uint16_t b = static_cast<const uint16_t*>(a.teacher)[static_cast<long long>(i) * a.ld_teacher + y];
-        t_y = static_cast<double>(__uint_as_float(static_cast<uint32_t>(b) << 16));
-      } else {
-        t_y = static_cast<double>(static_cast<const float*>(a.teacher)[static_cast<long long>(i) * a.ld_teacher + y]);
-      }
-      nll_t = alpha > 0.0 ? lse_t1 - (1.0 - alpha) * t_y - (alpha / vd) * ts.sx : lse_t1 - t_y;
-    }
+    if (!ignored) nll_t = alpha > 0.0 ? lse_t1 - (1.0 - alpha) * t_y - (alpha / vd) * ts.sx : lse_t1 - t_y;
     a.nll_t_rows[i] = static_cast<float>(nll_t);
   } else {
     a.nll_t_rows[i] = 0.0f;
@@ -198,10 +196,96 @@ __global__ void __launch_bounds__(ROW_THREADS) row_stats_kernel(const RowArgs a)
   rc.c_sT = static_cast<float>(lse_sT * static_cast<double>(LOG2E_F));
   rc.c_tT = static_cast<float>(lse_tT * static_cast<double>(LOG2E_F));
   rc.c_t1 = static_cast<float>(lse_t1 * static_cast<double>(LOG2E_F));
-  rc.y = y;
+  rc.y = ignored ? 0 : y_local;
   rc.ignored = ignored;
   rc.pad0 = rc.pad1 = 0;
   reinterpret_cast<RowConst*>(a.row_const)[i] = rc;
+}
+
+// ---- one CTA per row: merge records, per-row losses, constants.
+__global__ void __launch_bounds__(ROW_THREADS) row_stats_kernel(const RowArgs a) {
+  __shared__ double sh[3 * 32];
+  const int i = blockIdx.x;
+  const double inv_t = static_cast<double>(a.inv_t);
+  const bool want_t = a.need_kl || a.teacher_ce;
+
+  const Acc own = merge_row(a.rec_own, i, a.n_parts, inv_t, sh);
+  const Acc ts = want_t ? merge_row(a.rec_own_t, i, a.n_parts_t, inv_t, sh) : Acc{0.0, 1.0, 1.0, 0.0};
+  if (threadIdx.x != 0) return;
+  long long y;
+  const bool ignored = row_label(a, i, y);
+  double x_y = 0.0, t_y = 0.0;
+  if (!ignored) {
+    x_y = static_cast<double>(a.logits_s[static_cast<long long>(i) * a.ldl + y]);
+    if (a.teacher_ce) t_y = teacher_value(a, i, y);
+  }
+  finish_row(a, i, own, ts, ignored, x_y, t_y, static_cast<int>(y));
+}
+
+// ---- vocabulary-sharded phase 1, one CTA per row: the slice's statistics
+// of the row as one tuple, with the label's logits if the slice holds it.
+__global__ void __launch_bounds__(ROW_THREADS) vocab_partials_kernel(const RowArgs a) {
+  __shared__ double sh[3 * 32];
+  const int i = blockIdx.x;
+  const double inv_t = static_cast<double>(a.inv_t);
+  const bool want_t = a.need_kl || a.teacher_ce;
+  const Acc own = merge_row(a.rec_own, i, a.n_parts, inv_t, sh);
+  const Acc ts = want_t ? merge_row(a.rec_own_t, i, a.n_parts_t, inv_t, sh) : Acc{0.0, 1.0, 1.0, 0.0};
+  if (threadIdx.x != 0) return;
+  long long y;
+  const bool ignored = row_label(a, i, y);
+  const long long yl = y - a.v0;
+  float x_y = 0.0f, t_y = 0.0f, has_y = 0.0f;
+  if (!ignored && yl >= 0 && yl < a.v) {
+    x_y = a.logits_s[static_cast<long long>(i) * a.ldl + yl];
+    if (a.teacher_ce) t_y = static_cast<float>(teacher_value(a, i, yl));
+    has_y = 1.0f;
+  }
+  float4* out = reinterpret_cast<float4*>(a.partials_out + static_cast<long long>(i) * kVocabTuple);
+  out[0] = make_float4(static_cast<float>(own.m), static_cast<float>(own.d1), static_cast<float>(own.dT),
+                       static_cast<float>(own.sx));
+  out[1] = make_float4(static_cast<float>(ts.m), static_cast<float>(ts.d1), static_cast<float>(ts.dT),
+                       static_cast<float>(ts.sx));
+  out[2] = make_float4(x_y, t_y, has_y, 0.0f);
+}
+
+// ---- vocabulary-sharded phase 2, one thread per row: merges the ranks'
+// tuples in rank order (f64), then the same per-row losses and constants as
+// row_stats_kernel with the label column made local to this rank's slice.
+__global__ void __launch_bounds__(128) vocab_merge_kernel(const RowArgs a) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= a.n) return;
+  const double inv_t = static_cast<double>(a.inv_t);
+  const long long stride = static_cast<long long>(a.n) * kVocabTuple;
+  const float* base = a.partials_in + static_cast<long long>(i) * kVocabTuple;
+  double ms = -INFINITY, mt = -INFINITY;
+  for (int r = 0; r < a.world; ++r) {
+    ms = fmax(ms, static_cast<double>(base[r * stride + 0]));
+    mt = fmax(mt, static_cast<double>(base[r * stride + 4]));
+  }
+  Acc own{ms, 0.0, 0.0, 0.0}, ts{mt, 0.0, 0.0, 0.0};
+  double x_y = 0.0, t_y = 0.0;
+  for (int r = 0; r < a.world; ++r) {
+    const float* q = base + r * stride;
+    const double m_r = q[0], mt_r = q[4];
+    own.d1 += static_cast<double>(q[1]) * exp(m_r - ms);
+    own.dT += static_cast<double>(q[2]) * exp((m_r - ms) * inv_t);
+    own.sx += static_cast<double>(q[3]);
+    if (a.need_kl || a.teacher_ce) {
+      ts.d1 += static_cast<double>(q[5]) * exp(mt_r - mt);
+      ts.dT += static_cast<double>(q[6]) * exp((mt_r - mt) * inv_t);
+      ts.sx += static_cast<double>(q[7]);
+    }
+    if (q[10] != 0.0f) {
+      x_y = q[8];
+      t_y = q[9];
+    }
+  }
+  if (!(a.need_kl || a.teacher_ce)) ts = Acc{0.0, 1.0, 1.0, 0.0};
+  long long y;
+  const bool ignored = row_label(a, i, y);
+  const long long yl = y - a.v0;
+  finish_row(a, i, own, ts, ignored, x_y, t_y, (yl >= 0 && yl < a.v) ? static_cast<int>(yl) : -1);
 }
 
 // Scalars shared by every element of the gradient pass.
@@ -454,17 +538,20 @@ __global__ void target_flags_kernel(const int64_t* labels, long long bt, long lo
 __global__ void __launch_bounds__(1024) finalize_kernel(const float* nll_s, const float* nll_t,
                                                         const double* kl_base, const float* s_part, int nseg,
                                                         double t_sq, long long bt, const float* mean_scale,
-                                                        float w_s, float w_t, float kd, float* scalars) {
+                                                        float w_s, float w_t, float kd, float* scalars,
+                                                        int include_rows) {
   __shared__ double sh[3][32];
   double s0 = 0.0, s1 = 0.0, s2 = 0.0;
   for (long long r = threadIdx.x; r < bt; r += blockDim.x) {
-    s0 += static_cast<double>(nll_s[r]);
-    s1 += static_cast<double>(nll_t[r]);
+    if (include_rows) {
+      s0 += static_cast<double>(nll_s[r]);
+      s1 += static_cast<double>(nll_t[r]);
+    }
     if (nseg > 0) {
       // ignored rows have kl_base 0 and no cross-term segments
       double cross = 0.0;
       for (int k = 0; k < nseg; ++k) cross += static_cast<double>(s_part[r * nseg + k]);
-      s2 += (kl_base[r] + cross) * t_sq;
+      s2 += ((include_rows ? kl_base[r] : 0.0) + cross) * t_sq;
     }
   }
   for (int off = 16; off > 0; off >>= 1) {
@@ -521,17 +608,36 @@ void launch_grad(const RowArgs& a, const GradScalars& g, cudaStream_t stream) {
   else row_grad_kernel<VEC, false, false><<<grid, GRAD_THREADS, 0, stream>>>(a, g);
 }
 
+void launch_row_grad(const RowArgs& a, cudaStream_t stream);
+
 }  // namespace
 
 void launch_rows(const RowArgs& a, cudaStream_t stream) {
   if (a.n <= 0) return;
   row_stats_kernel<<<a.n, ROW_THREADS, 0, stream>>>(a);
+  launch_row_grad(a, stream);
+}
+
+void launch_vocab_partials(const RowArgs& a, cudaStream_t stream) {
+  if (a.n <= 0) return;
+  vocab_partials_kernel<<<a.n, ROW_THREADS, 0, stream>>>(a);
+}
+
+void launch_vocab_rows(const RowArgs& a, cudaStream_t stream) {
+  if (a.n <= 0) return;
+  vocab_merge_kernel<<<(a.n + 127) / 128, 128, 0, stream>>>(a);
+  launch_row_grad(a, stream);
+}
+
+namespace {
+
+void launch_row_grad(const RowArgs& a, cudaStream_t stream) {
   GradScalars g;
   g.ws = a.w_s;
   g.wt = a.w_t;
   g.kdT = a.need_kl ? a.kd * a.temperature : 0.0f;
   const double alpha = static_cast<double>(a.alpha);
-  g.eps = static_cast<float>(alpha / static_cast<double>(a.v));
+  g.eps = static_cast<float>(alpha / static_cast<double>(a.v_total > 0 ? a.v_total : a.v));
   const float one_minus_a = static_cast<float>(1.0 - alpha);
   g.ws_tgt = a.w_s * one_minus_a;
   g.wt_tgt = a.w_t * one_minus_a;
@@ -546,6 +652,8 @@ void launch_rows(const RowArgs& a, cudaStream_t stream) {
   if (vec) launch_grad<true>(a, g, stream);
   else launch_grad<false>(a, g, stream);
 }
+
+}  // namespace
 
 void launch_teacher_stats(const void* teacher, long long ld, int is_bf16, int n, int v, float inv_t, float* rec,
                           cudaStream_t stream) {
@@ -569,9 +677,9 @@ void launch_target_flags(const int64_t* labels, long long bt, long long v, int64
 
 void launch_finalize(const float* nll_s, const float* nll_t, const double* kl_base, const float* s_part, int nseg,
                      double t_sq, long long bt, const float* mean_scale, float w_s, float w_t, float kd,
-                     float* scalars, cudaStream_t stream) {
+                     float* scalars, cudaStream_t stream, int include_rows) {
   finalize_kernel<<<1, 1024, 0, stream>>>(nll_s, nll_t, kl_base, s_part, nseg, t_sq, bt, mean_scale, w_s, w_t, kd,
-                                          scalars);
+                                          scalars, include_rows);
 }
 
 void launch_f32_to_bf16(const float* src, long long rows, long long cols, uint16_t* dst, long long ld,

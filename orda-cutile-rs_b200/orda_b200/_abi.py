@@ -130,6 +130,13 @@ class OrdaShardOptions(C.Structure):
                 ("scatter_grad_weight", C.c_int32)]
 
 
+VOCAB_TUPLE = 12  # ORDA_VOCAB_TUPLE
+
+
+class OrdaVocabShard(C.Structure):
+    _fields_ = [("v_total", C.c_int64), ("v0", C.c_int64), ("world", C.c_int32), ("include_rows", C.c_int32)]
+
+
 class OrdaIpcHandle(C.Structure):
     _fields_ = [("bytes", C.c_ubyte * 64)]  # opaque; c_ubyte so no NUL truncation
 
@@ -198,6 +205,16 @@ SIGNATURES = {
     "orda_context_phase_times": (C.c_int, [C.c_void_p, C.POINTER(C.c_double), C.POINTER(C.c_uint64)]),
     "orda_context_reset_timing": (None, [C.c_void_p]),
     "orda_context_launch_count": (C.c_uint64, [C.c_void_p]),
+    "orda_vocab_forward_device": (
+        C.c_int,
+        [C.c_void_p, C.POINTER(OrdaDeviceMat), C.POINTER(OrdaDeviceMat), C.c_void_p, C.c_size_t,
+         C.POINTER(OrdaDeviceTeacher), C.POINTER(OrdaLossOptions), C.POINTER(OrdaVocabShard), C.c_void_p, C.c_void_p,
+         C.c_char_p, C.c_size_t]),
+    "orda_vocab_backward_device": (
+        C.c_int,
+        [C.c_void_p, C.POINTER(OrdaDeviceMat), C.POINTER(OrdaDeviceMat), C.c_void_p, C.c_size_t,
+         C.POINTER(OrdaDeviceTeacher), C.POINTER(OrdaLossOptions), C.POINTER(OrdaVocabShard), C.c_void_p,
+         C.POINTER(OrdaDeviceOutputs), C.c_void_p, C.POINTER(OrdaChunkPlan), C.c_char_p, C.c_size_t]),
     "orda_context_slots_create": (
         C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_size_t, C.c_size_t, C.POINTER(OrdaIpcHandle), C.c_char_p,
                   C.c_size_t]),

@@ -144,6 +144,65 @@ class DeviceLossResult:
     chunk_plan: ChunkPlan
 
 
+def _teacher_struct(teacher_mode, teacher_hidden, teacher_weight, teacher_logits):
+    t = _abi.OrdaDeviceTeacher()
+    t.mode = int(teacher_mode)
+    t.hidden = dev_mat(teacher_hidden)
+    t.weight = dev_mat(teacher_weight)
+    t.logits = dev_mat(teacher_logits)
+    return t
+
+
+def _outputs(opts, teacher_mode, bt, h, v, ht, dev, out, want_int8, with_grad_weight=True):
+    """Output tensors (from `out` or newly allocated) and their C struct."""
+    w_t = opts.teacher_ce_weight
+    if w_t is None:
+        w_t = 1.0 if teacher_mode == TeacherMode.Tied else 0.0
+    live = teacher_mode in (TeacherMode.Tied, TeacherMode.Separate)
+    out = dict(out or {})
+    f32 = dict(device=dev, dtype=torch.float32)
+    gsh = out.get("grad_student_hidden")
+    if gsh is None:
+        gsh = torch.empty(bt, h, **f32)
+    gw = out.get("grad_weight") if with_grad_weight else None
+    if gw is None and with_grad_weight:
+        gw = torch.empty(v, h, **f32)
+    gth = out.get("grad_teacher_hidden")
+    if gth is None and w_t > 0 and live:
+        gth = torch.empty(bt, ht, **f32)
+    gtw = out.get("grad_teacher_weight")
+    if gtw is None and w_t > 0 and teacher_mode == TeacherMode.Separate:
+        gtw = torch.empty(v, ht, **f32)
+    q = out.get("grad_weight_q")
+    sc = out.get("grad_weight_scale")
+    if want_int8 and opts.config.quantize_grad_weight:
+        if q is None:
+            q = torch.empty(v, h, device=dev, dtype=torch.int8)
+        if sc is None:
+            sc = torch.empty(v, **f32)
+    scal = out.get("scalars")
+    if scal is None:
+        scal = torch.empty(4, **f32)
+    o = _abi.OrdaDeviceOutputs()
+    o.grad_student_hidden = gsh.data_ptr()
+    o.ld_grad_student_hidden = gsh.stride(0)
+    if gw is not None:
+        o.grad_weight = gw.data_ptr()
+        o.ld_grad_weight = gw.stride(0)
+    if gth is not None:
+        o.grad_teacher_hidden = gth.data_ptr()
+        o.ld_grad_teacher_hidden = gth.stride(0)
+    if gtw is not None:
+        o.grad_teacher_weight = gtw.data_ptr()
+        o.ld_grad_teacher_weight = gtw.stride(0)
+    o.grad_weight_q = _ptr(q)
+    o.grad_weight_scale = _ptr(sc)
+    o.scalars = scal.data_ptr()
+    tensors = dict(scalars=scal, grad_student_hidden=gsh, grad_weight=gw, grad_teacher_hidden=gth,
+                   grad_teacher_weight=gtw, grad_weight_q=q, grad_weight_scale=sc)
+    return o, tensors
+
+
 def distillation_loss_device(
     ctx: DeviceContext,
     student_hidden: torch.Tensor,
@@ -165,61 +224,12 @@ def distillation_loss_device(
     With scatter_grad_weight the grad_W partial goes to the slot buffers
     (see DeviceContext.slots_create) and the returned grad_weight is None."""
     opts = opts or LossOptions()
-    dev = student_hidden.device
     bt, h = student_hidden.shape
     v = weight.shape[0]
-    w_t = opts.teacher_ce_weight
-    if w_t is None:
-        w_t = 1.0 if teacher_mode == TeacherMode.Tied else 0.0
-    live = teacher_mode in (TeacherMode.Tied, TeacherMode.Separate)
     ht = teacher_hidden.shape[1] if teacher_mode == TeacherMode.Separate else h
-    out = dict(out or {})
-    f32 = dict(device=dev, dtype=torch.float32)
-    gsh = out.get("grad_student_hidden")
-    if gsh is None:
-        gsh = torch.empty(bt, h, **f32)
-    gw = out.get("grad_weight")
-    if gw is None and not scatter_grad_weight:
-        gw = torch.empty(v, h, **f32)
-    if scatter_grad_weight:
-        gw = None
-    gth = out.get("grad_teacher_hidden")
-    if gth is None and w_t > 0 and live:
-        gth = torch.empty(bt, ht, **f32)
-    gtw = out.get("grad_teacher_weight")
-    if gtw is None and w_t > 0 and teacher_mode == TeacherMode.Separate:
-        gtw = torch.empty(v, ht, **f32)
-    q = out.get("grad_weight_q")
-    sc = out.get("grad_weight_scale")
-    if want_int8 and opts.config.quantize_grad_weight:
-        if q is None:
-            q = torch.empty(v, h, device=dev, dtype=torch.int8)
-        if sc is None:
-            sc = torch.empty(v, **f32)
-    scal = out.get("scalars")
-    if scal is None:
-        scal = torch.empty(4, **f32)
-
-    t = _abi.OrdaDeviceTeacher()
-    t.mode = int(teacher_mode)
-    t.hidden = dev_mat(teacher_hidden)
-    t.weight = dev_mat(teacher_weight)
-    t.logits = dev_mat(teacher_logits)
-    o = _abi.OrdaDeviceOutputs()
-    o.grad_student_hidden = gsh.data_ptr()
-    o.ld_grad_student_hidden = gsh.stride(0)
-    if gw is not None:
-        o.grad_weight = gw.data_ptr()
-        o.ld_grad_weight = gw.stride(0)
-    if gth is not None:
-        o.grad_teacher_hidden = gth.data_ptr()
-        o.ld_grad_teacher_hidden = gth.stride(0)
-    if gtw is not None:
-        o.grad_teacher_weight = gtw.data_ptr()
-        o.ld_grad_teacher_weight = gtw.stride(0)
-    o.grad_weight_q = _ptr(q)
-    o.grad_weight_scale = _ptr(sc)
-    o.scalars = scal.data_ptr()
+    o, tensors = _outputs(opts, teacher_mode, bt, h, v, ht, student_hidden.device, out, want_int8,
+                          with_grad_weight=not scatter_grad_weight)
+    t = _teacher_struct(teacher_mode, teacher_hidden, teacher_weight, teacher_logits)
     shard = _abi.OrdaShardOptions(int(global_non_ignore), int(skip_quantize), int(scatter_grad_weight))
     plan = _abi.OrdaChunkPlan()
     buf = _abi.err_buf()
@@ -239,16 +249,79 @@ def distillation_loss_device(
         len(buf),
     )
     _check(rc, buf)
-    return DeviceLossResult(
-        scalars=scal,
-        grad_student_hidden=gsh,
-        grad_weight=gw,
-        grad_teacher_hidden=gth,
-        grad_teacher_weight=gtw,
-        grad_weight_q=q,
-        grad_weight_scale=sc,
-        chunk_plan=ChunkPlan(int(plan.chunk_size), int(plan.num_chunks)),
-    )
+    return DeviceLossResult(chunk_plan=ChunkPlan(int(plan.chunk_size), int(plan.num_chunks)), **tensors)
+
+
+def vocab_forward_device(
+    ctx: DeviceContext,
+    student_hidden: torch.Tensor,
+    weight_slice: torch.Tensor,
+    labels: torch.Tensor,
+    teacher_mode: TeacherMode,
+    v_total: int,
+    v0: int,
+    teacher_hidden: Optional[torch.Tensor] = None,
+    teacher_weight_slice: Optional[torch.Tensor] = None,
+    teacher_logits_slice: Optional[torch.Tensor] = None,
+    opts: Optional[LossOptions] = None,
+    partials: Optional[torch.Tensor] = None,
+    stream=None,
+) -> torch.Tensor:
+    """`orda_vocab_forward_device`: logits of this rank's vocabulary rows
+    [v0, v0 + len(weight_slice)); returns the per-row partial statistics
+    [bt, VOCAB_TUPLE] to all-gather."""
+    opts = opts or LossOptions()
+    bt = student_hidden.shape[0]
+    if partials is None:
+        partials = torch.empty(bt, _abi.VOCAB_TUPLE, device=student_hidden.device, dtype=torch.float32)
+    t = _teacher_struct(teacher_mode, teacher_hidden, teacher_weight_slice, teacher_logits_slice)
+    vs = _abi.OrdaVocabShard(int(v_total), int(v0), 1, 0)
+    buf = _abi.err_buf()
+    rc = _lib().orda_vocab_forward_device(
+        ctx.handle, C.byref(dev_mat(student_hidden)), C.byref(dev_mat(weight_slice)), labels.data_ptr(),
+        labels.numel(), C.byref(t), C.byref(opts._c()), C.byref(vs), partials.data_ptr(), _stream(stream), buf,
+        len(buf))
+    _check(rc, buf)
+    return partials
+
+
+def vocab_backward_device(
+    ctx: DeviceContext,
+    student_hidden: torch.Tensor,
+    weight_slice: torch.Tensor,
+    labels: torch.Tensor,
+    teacher_mode: TeacherMode,
+    v_total: int,
+    v0: int,
+    all_partials: torch.Tensor,
+    include_rows: bool,
+    teacher_hidden: Optional[torch.Tensor] = None,
+    teacher_weight_slice: Optional[torch.Tensor] = None,
+    teacher_logits_slice: Optional[torch.Tensor] = None,
+    opts: Optional[LossOptions] = None,
+    out: Optional[dict] = None,
+    want_int8: bool = False,
+    stream=None,
+) -> DeviceLossResult:
+    """`orda_vocab_backward_device`: all_partials [world, bt, VOCAB_TUPLE]
+    are every rank's tuples by rank. grad_weight (and grad_teacher_weight)
+    hold this slice's rows; grad_student_hidden, grad_teacher_hidden and
+    scalars are this rank's partial sums (add them over the ranks)."""
+    opts = opts or LossOptions()
+    bt, h = student_hidden.shape
+    v = weight_slice.shape[0]
+    ht = teacher_hidden.shape[1] if teacher_mode == TeacherMode.Separate else h
+    o, tensors = _outputs(opts, teacher_mode, bt, h, v, ht, student_hidden.device, out, want_int8)
+    t = _teacher_struct(teacher_mode, teacher_hidden, teacher_weight_slice, teacher_logits_slice)
+    vs = _abi.OrdaVocabShard(int(v_total), int(v0), int(all_partials.shape[0]), int(include_rows))
+    plan = _abi.OrdaChunkPlan()
+    buf = _abi.err_buf()
+    rc = _lib().orda_vocab_backward_device(
+        ctx.handle, C.byref(dev_mat(student_hidden)), C.byref(dev_mat(weight_slice)), labels.data_ptr(),
+        labels.numel(), C.byref(t), C.byref(opts._c()), C.byref(vs), all_partials.data_ptr(), C.byref(o),
+        _stream(stream), C.byref(plan), buf, len(buf))
+    _check(rc, buf)
+    return DeviceLossResult(chunk_plan=ChunkPlan(int(plan.chunk_size), int(plan.num_chunks)), **tensors)
 
 
 def gemm_bf16(

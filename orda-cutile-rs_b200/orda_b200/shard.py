@@ -15,6 +15,9 @@ oracle as compute).
 
 SlotReduceScatter replaces the NCCL reduce-scatter of grad_W on one node:
 the wgrad GEMM writes each owner's rows into the owner's memory itself.
+
+vocab_sharded_step is the other partitioning, for the largest vocabularies:
+W is split by vocabulary rows and every rank sees all tokens.
 """
 from __future__ import annotations
 
@@ -162,3 +165,49 @@ class SlotReduceScatter:
         dist.all_reduce(self._token, group=self.group)
         return ShardResult(scalars=scalars, grad_student_hidden=gsh, grad_weight_slice=grad_weight_slice,
                            vocab_range=(self.v0, self.v1))
+
+
+# ------------------------------------------------------------------ vocabulary sharding
+
+def vocab_slice_bounds(v_total: int, world: int, rank: int, align: int = 8) -> tuple[int, int]:
+    """Vocabulary rows [v0, v1) held by `rank` when V is sharded: near-equal
+    contiguous slices whose starts are multiples of `align` (so a bf16 column
+    slice of teacher logits stays 16-byte aligned)."""
+    n = -(-v_total // world)
+    n = -(-n // align) * align
+    v0 = min(rank * n, v_total)
+    v1 = min(v0 + n, v_total)
+    if v1 <= v0:
+        raise ValueError(f"V={v_total} leaves rank {rank} of {world} an empty slice")
+    return v0, v1
+
+
+def vocab_sharded_step(ctx, student_hidden, weight_slice, labels, teacher_mode, v_total: int, v0: int,
+                       teacher_hidden=None, teacher_weight_slice=None, teacher_logits_slice=None, opts=None,
+                       out: Optional[dict] = None, want_int8: bool = False, stream=None, group=None):
+    """One vocabulary-sharded step (tensor parallel over the output head).
+
+    Every rank holds all rows of the hidden states and labels and the
+    vocabulary rows [v0, v0 + len(weight_slice)) of W (of a Separate
+    teacher's W, or those columns of Precomputed teacher logits). The ranks
+    exchange one small tuple of row statistics per row (all-gather) between
+    the two device phases, then sum grad_hidden and the scalars (all-reduce).
+    grad_weight of the result is this rank's slice, complete; grad_hidden and
+    the scalars are the full-vocabulary values on every rank.
+    """
+    from .device import vocab_backward_device, vocab_forward_device
+
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    kw = dict(teacher_hidden=teacher_hidden, teacher_weight_slice=teacher_weight_slice,
+              teacher_logits_slice=teacher_logits_slice, opts=opts, stream=stream)
+    part = vocab_forward_device(ctx, student_hidden, weight_slice, labels, teacher_mode, v_total, v0, **kw)
+    every = torch.empty((world,) + tuple(part.shape), device=part.device, dtype=part.dtype)
+    dist.all_gather_into_tensor(every, part, group=group)
+    res = vocab_backward_device(ctx, student_hidden, weight_slice, labels, teacher_mode, v_total, v0, every,
+                                include_rows=(rank == 0), out=out, want_int8=want_int8, **kw)
+    dist.all_reduce(res.scalars, group=group)
+    dist.all_reduce(res.grad_student_hidden, group=group)
+    if res.grad_teacher_hidden is not None:
+        dist.all_reduce(res.grad_teacher_hidden, group=group)
+    return res

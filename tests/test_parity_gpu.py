@@ -304,13 +304,24 @@ def _subset_case(ob, cfg, rows, gen):
         t = ob.Teacher.Precomputed(ob.Mat.from_array(bf16_round(tl.numpy())))
         opts = ob.LossOptions(kd_weight=0.4, temperature=1.5, config=ob.KernelConfig(quantize_grad_weight=True))
         return ob.Mat.from_array(bf16_round(hs.numpy())), ob.Mat.from_array(bf16_round(w.numpy())), labs, t, opts
+    if cfg == "c5":
+        bt, h, v = rows, 8192, 152064
+        hs = torch.randn(bt, h, generator=gen)
+        ht = hs + 0.1 * torch.randn(bt, h, generator=gen)
+        w = 0.02 * torch.randn(v, h, generator=gen)
+        labs = torch.randint(0, v, (bt,), generator=gen).tolist()
+        t = ob.Teacher.Tied(ob.Mat.from_array(bf16_round(ht.numpy())))
+        opts = ob.LossOptions(kd_weight=0.4, temperature=1.5)
+        return ob.Mat.from_array(bf16_round(hs.numpy())), ob.Mat.from_array(bf16_round(w.numpy())), labs, t, opts
     raise ValueError(cfg)
 
 
-@pytest.mark.parametrize("cfg,rows", [("c2", 64), ("c3", 16), ("c4", 16)])
+@pytest.mark.parametrize("cfg,rows", [("c2", 64), ("c3", 16), ("c4", 16), ("c5", 4)])
 def test_baseline_config_row_subsets_match_oracle(ob, oracle, cfg, rows):
-    """Full H and V of BASELINE configs c2-c4 on a row subset the oracle can
-    finish in seconds (c4 includes the INT8 grad_W round trip)."""
+    """Full H and V of BASELINE configs c2-c5 on a row subset the oracle can
+    finish in seconds (c4 includes the INT8 grad_W round trip; c5 is the
+    large-vocab Tied configuration, H=8192, V=152064, whose tail of 64 rows
+    past the last 128-row block exercises the ragged tile edges)."""
     gen = torch.Generator().manual_seed(7 + rows)
     s, w, labs, t, opts = _subset_case(ob, cfg, rows, gen)
     g = ob.distillation_loss(s, w, labs, t, opts)
