@@ -202,6 +202,132 @@ def run_reference_arm(args):
     return 0
 
 
+# ----------------------------------------------------- c5 (large vocabulary)
+
+C5 = dict(rows=8192, h=8192, v=152064, kd=0.4, temperature=1.5, w_std=0.02)
+
+
+def run_c5(args):
+    """BASELINE config c5: Tied teacher, H=8192, V=152064, 8192 rows per GPU
+    (weak scaling). --shard rows: each rank its own 8192 rows, grad_W
+    reduce-scatter fused into the wgrad GEMM. --shard vocab: every rank holds
+    all 8192*N rows and V/N vocabulary rows of W; one all-gather of per-row
+    statistics, all-reduce of grad_hidden and the scalars. No e2e / CPU
+    baseline (those are measured on the metric config c4)."""
+    import torch
+    import torch.distributed as dist
+
+    import orda_b200 as ob
+    from orda_b200 import shard
+    from orda_b200.device import DeviceContext, distillation_loss_device
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    h, v = C5["h"], C5["v"]
+    vocab = world > 1 and args.shard == "vocab"
+    rows = C5["rows"] * (world if vocab else 1)
+    gen = torch.Generator(device=dev).manual_seed(2000 + (0 if vocab else rank))
+    hs = torch.randn(rows, h, generator=gen, device=dev).bfloat16()
+    ht = (hs.float() + 0.1 * torch.randn(rows, h, generator=gen, device=dev)).bfloat16()
+    labels = torch.randint(0, v, (rows,), generator=gen, device=dev)
+    v0, v1 = shard.vocab_slice_bounds(v, world, rank) if vocab else (0, v)
+    wgen = torch.Generator(device=dev).manual_seed(7 + v0)
+    w = (C5["w_std"] * torch.randn(v1 - v0, h, generator=wgen, device=dev)).bfloat16()
+    opts = ob.LossOptions(kd_weight=C5["kd"], temperature=C5["temperature"])
+    ctx = DeviceContext(local)
+    stream = torch.cuda.current_stream(dev)
+    out = {"grad_student_hidden": torch.empty(rows, h, device=dev),
+           "grad_teacher_hidden": torch.empty(rows, h, device=dev), "scalars": torch.empty(4, device=dev)}
+    fused = None
+    if world > 1 and not vocab:
+        fused = shard.SlotReduceScatter(ctx, v, h)
+        gw_slice = torch.empty(v // world, h, device=dev)
+        n_global = shard.global_non_ignore(labels, -100)
+    else:
+        out["grad_weight"] = torch.empty(v1 - v0, h, device=dev)
+
+    def step():
+        if vocab:
+            return shard.vocab_sharded_step(ctx, hs, w, labels, ob.TeacherMode.Tied, v, v0, teacher_hidden=ht,
+                                            opts=opts, out=out, stream=stream)
+        if fused:
+            def compute(n):
+                r = distillation_loss_device(ctx, hs, w, labels, ob.TeacherMode.Tied, teacher_hidden=ht, opts=opts,
+                                             out=out, global_non_ignore=n, scatter_grad_weight=True, stream=stream)
+                return r.scalars, r.grad_student_hidden
+
+            return fused.step(compute, labels, -100, n_global, gw_slice, stream=stream)
+        return distillation_loss_device(ctx, hs, w, labels, ob.TeacherMode.Tied, teacher_hidden=ht, opts=opts,
+                                        out=out, stream=stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    ctx.check()
+    sampler = None
+    if rank == 0 and not args.no_clocks:
+        uuid = getattr(torch.cuda.get_device_properties(dev), "uuid", None)
+        sampler = ClockSampler(f"GPU-{uuid}" if uuid is not None else str(local))
+        sampler.start()
+        time.sleep(0.3)
+    ctx.reset_timing()
+    ctx.enable_timing(True)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms_total = ev0.elapsed_time(ev1)
+    phases = ctx.phase_times()
+    ctx.enable_timing(False)
+    clocks = sampler.stop() if sampler else None
+    ctx.check()
+    if world > 1:
+        t = torch.tensor([ms_total], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_total = float(t.item())
+    ms_step = ms_total / args.steps
+    tokens = C5["rows"] * world
+    peak, peak_sus, hbm, peak_kind = load_peaks()
+    # Tied teacher with teacher CE weight 1: 12 * rows * V * H per GPU
+    flops = 12.0 * C5["rows"] * v * h
+    gemm_ms = sum(phases[p][0] for p in ("logits_gemm", "dgrad_gemm", "wgrad_gemm")) / args.steps
+    achieved = flops / (gemm_ms / 1e3) / 1e12
+    if rank == 0:
+        line = {
+            "metric": "distillation fwd+bwd tokens/sec, c5 (Tied, H=8192, V=152064)", "value": tokens / (ms_step / 1e3),
+            "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "c5: Tied teacher, 8192 rows per GPU, H=8192, V=152064, kd=0.4, T=1.5",
+                       "parallelism": ("vocabulary sharded (V/N per GPU, all rows on every GPU)" if vocab else
+                                       "rows sharded, grad_W reduce-scatter fused into the wgrad GEMM"
+                                       if world > 1 else "single GPU")},
+            "phases_ms_per_step": {k: v_[0] / args.steps for k, v_ in phases.items()},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "kernel": "gemm_kernel (tcgen05 cta_group::2)",
+                         "gemm_ms_per_step": gemm_ms},
+            "step_tflops_per_gpu": flops / (ms_step / 1e3) / 1e12, "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    ctx.close()
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
 # --------------------------------------------------------------- our arm
 
 def run_ours(args):
@@ -471,6 +597,9 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-clocks", action="store_true")
+    ap.add_argument("--config", choices=["c4", "c5"], default="c4",
+                    help="c4: the metric configuration (default); c5: the large-vocabulary Tied configuration")
+    ap.add_argument("--shard", choices=["rows", "vocab"], default="rows", help="c5 with N > 1: partitioning")
     ap.add_argument("--reduce", choices=["fused", "nccl"], default="fused",
                     help="N > 1: grad_W reduce-scatter fused into the wgrad GEMM, or an NCCL reduce-scatter")
     args = ap.parse_args()
@@ -479,6 +608,8 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         return run_reference_arm(args)
+    if args.config == "c5":
+        return run_c5(args)
     return run_ours(args)
 
 
