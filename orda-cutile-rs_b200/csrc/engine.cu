@@ -865,9 +865,10 @@ int orda_reduce_slots_device(OrdaContext* ctx, float* grad_w_slice, size_t ld, c
   cudaSetDevice(ctx->device);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const long long slice = ctx->slot_slice, h = ctx->slot_h;
-  orda::launch_slot_reduce(ctx->slots, ctx->slot_world, slice, h, grad_w_slice, static_cast<long long>(ld), st);
-  ctx->launches += 1;
-  if (quantize) {
+  if (!quantize) {
+    orda::launch_slot_reduce(ctx->slots, ctx->slot_world, slice, h, grad_w_slice, static_cast<long long>(ld), st);
+    ctx->launches += 1;
+  } else {
     if (ensure_ws(ctx, round_up(static_cast<size_t>(slice), 256)) != cudaSuccess) {
       set_error(err, err_len, "device workspace allocation failed");
       return ORDA_ERR_OOM;
@@ -877,8 +878,16 @@ int orda_reduce_slots_device(OrdaContext* ctx, float* grad_w_slice, size_t ld, c
     if (e != cudaSuccess) return cuda_fail(e, "memset", err, err_len);
     const long long row0 = static_cast<long long>(ctx->slot_rank) * slice;
     orda::launch_target_flags(labels, static_cast<long long>(n_labels), slice, ignore_index, flags, st, row0);
-    orda::launch_quant(grad_w_slice, slice, h, static_cast<long long>(ld), flags, stochastic, seed, q, scale, st, row0);
-    ctx->launches += 2;
+    // one pass: rank-ordered sum and INT8 round trip of each row
+    if (orda::launch_slot_reduce_quant(ctx->slots, ctx->slot_world, slice, h, grad_w_slice,
+                                       static_cast<long long>(ld), flags, stochastic, seed, q, scale, row0, st)) {
+      ctx->launches += 2;
+    } else {
+      orda::launch_slot_reduce(ctx->slots, ctx->slot_world, slice, h, grad_w_slice, static_cast<long long>(ld), st);
+      orda::launch_quant(grad_w_slice, slice, h, static_cast<long long>(ld), flags, stochastic, seed, q, scale, st,
+                         row0);
+      ctx->launches += 3;
+    }
   }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "slot reduction", err, err_len);

@@ -161,6 +161,14 @@ void launch_quant(float* grad_w, long long v, long long h, long long ld, const u
 void launch_target_flags(const int64_t* labels, long long bt, long long v, int64_t ignore_index,
                          uint8_t* target_flags, cudaStream_t stream, long long row0 = 0);
 
+// launch_slot_reduce followed by launch_quant in one pass (the summed row
+// stays in shared memory). Returns false, launching nothing, when the row
+// does not fit (h % 4 != 0 or h > 12288); the caller then uses the two
+// kernels.
+bool launch_slot_reduce_quant(const float* slots, int world, long long slice, long long h, float* out, long long ld,
+                              const uint8_t* target_flags, int stochastic, uint64_t seed, int8_t* q, float* scale,
+                              long long row_offset, cudaStream_t stream);
+
 // out[r, :] = sum over k = 0..world-1 (in that order) of
 // slots[(k * slice + r) * h + :], for r < slice (fp32).
 void launch_slot_reduce(const float* slots, int world, long long slice, long long h, float* out, long long ld,

@@ -119,7 +119,75 @@ __global__ void __launch_bounds__(QT) slot_reduce_kernel(const float* __restrict
   }
 }
 
+// Rank-ordered sum of the world partials of one row fused with its INT8
+// round trip: the summed row is kept in shared memory (h floats), so the
+// slice is read once (the partials) and written once, and the values equal
+// slot_reduce_kernel followed by quant_kernel bit for bit.
+__global__ void __launch_bounds__(QT) slot_reduce_quant_kernel(const float* __restrict__ slots, int world,
+                                                               long long slice, long long h, float* out,
+                                                               long long ld, const uint8_t* target_flags,
+                                                               int stochastic, uint64_t seed, int8_t* q,
+                                                               float* scale, long long row_offset) {
+  extern __shared__ __align__(16) float xs[];  // h floats
+  __shared__ float sh[QT / 32];
+  const long long r = blockIdx.x;
+  const long long part = slice * h;
+  const float* srow = slots + r * h;
+  float amax = 0.0f;
+  for (long long c = threadIdx.x * 4; c < h; c += QT * 4) {
+    float4 acc = *reinterpret_cast<const float4*>(srow + c);
+    for (int k = 1; k < world; ++k) {
+      const float4 x = *reinterpret_cast<const float4*>(srow + k * part + c);
+      acc.x += x.x;
+      acc.y += x.y;
+      acc.z += x.z;
+      acc.w += x.w;
+    }
+    *reinterpret_cast<float4*>(xs + c) = acc;
+    amax = fmaxf(fmaxf(amax, fabsf(acc.x)), fmaxf(fabsf(acc.y), fmaxf(fabsf(acc.z), fabsf(acc.w))));
+  }
+  for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+  if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = amax;
+  __syncthreads();
+  amax = sh[0];
+#pragma unroll
+  for (int w = 1; w < QT / 32; ++w) amax = fmaxf(amax, sh[w]);
+
+  const float s = __fdiv_rn(fmaxf(amax, 1e-12f), 127.0f);
+  if (scale && threadIdx.x == 0) scale[r] = s;
+  const bool keep = target_flags && target_flags[r];
+  int8_t* qrow = q ? q + r * h : nullptr;
+  float* orow = out + r * ld;
+  for (long long c = threadIdx.x; c < h; c += QT) {
+    const float x = xs[c];
+    const float scaled = __fdiv_rn(x, s);
+    int8_t qi;
+    if (!stochastic) {
+      qi = to_i8(rintf(scaled));
+    } else {
+      const float fl = floorf(scaled);
+      const float frac = scaled - fl;
+      const float u = splitmix_uniform(seed, static_cast<uint64_t>(r + row_offset) * static_cast<uint64_t>(h) +
+                                                 static_cast<uint64_t>(c));
+      qi = to_i8(fl + (frac > u ? 1.0f : 0.0f));
+    }
+    if (qrow) qrow[c] = qi;
+    orow[c] = keep ? x : static_cast<float>(qi) * s;
+  }
+}
+
 }  // namespace
+
+bool launch_slot_reduce_quant(const float* slots, int world, long long slice, long long h, float* out, long long ld,
+                              const uint8_t* target_flags, int stochastic, uint64_t seed, int8_t* q, float* scale,
+                              long long row_offset, cudaStream_t stream) {
+  const size_t smem = static_cast<size_t>(h) * sizeof(float);
+  if (h % 4 != 0 || smem > 48 * 1024) return false;
+  if (slice <= 0) return true;
+  slot_reduce_quant_kernel<<<static_cast<unsigned>(slice), QT, smem, stream>>>(
+      slots, world, slice, h, out, ld, target_flags, stochastic, seed, q, scale, row_offset);
+  return true;
+}
 
 void launch_quant(float* grad_w, long long v, long long h, long long ld, const uint8_t* target_flags,
                   int stochastic, uint64_t seed, int8_t* q, float* scale, cudaStream_t stream,

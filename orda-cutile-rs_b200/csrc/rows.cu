@@ -346,13 +346,14 @@ __device__ __forceinline__ float block_sum_f(float v, float* sh) {
   return t;
 }
 
-// ---- grid (segment, row): gradients of one 8192-column segment of one row.
+// ---- grid (row, segment): gradients of one 8192-column segment of one row
+// (rows on grid x, which has no 65535 limit).
 // VEC: V % 8 == 0 and 16-byte aligned rows (8 columns per thread step).
 template <bool VEC, bool KL, bool TGRAD>
 __global__ void __launch_bounds__(GRAD_THREADS) row_grad_kernel(const RowArgs a, const GradScalars g) {
   __shared__ float sh[GRAD_THREADS / 32];
-  const int seg = blockIdx.x;
-  const long long row = blockIdx.y;
+  const int seg = blockIdx.y;
+  const long long row = blockIdx.x;
   const RowConst c = reinterpret_cast<const RowConst*>(a.row_const)[row];
   const float* xs = a.logits_s + row * a.ldl;
   uint16_t* gs_row = a.dlog_s + row * a.ldd;
@@ -600,7 +601,7 @@ __global__ void f32_to_bf16_kernel(const float* src, long long rows, long long c
 
 template <bool VEC>
 void launch_grad(const RowArgs& a, const GradScalars& g, cudaStream_t stream) {
-  const dim3 grid(static_cast<unsigned>((a.v + kGradSegCols - 1) / kGradSegCols), static_cast<unsigned>(a.n));
+  const dim3 grid(static_cast<unsigned>(a.n), static_cast<unsigned>((a.v + kGradSegCols - 1) / kGradSegCols));
   const bool kl = a.need_kl != 0, tg = a.teacher_grad != 0;
   if (kl && tg) row_grad_kernel<VEC, true, true><<<grid, GRAD_THREADS, 0, stream>>>(a, g);
   else if (kl) row_grad_kernel<VEC, true, false><<<grid, GRAD_THREADS, 0, stream>>>(a, g);
