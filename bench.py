@@ -48,6 +48,28 @@ def algorithmic_flops(bt, h, v):
     return 2.0 * bt * v * 3 * h
 
 
+def balanced_rows(total: int, speeds: list, quantum: int, lo: int, hi: int) -> list:
+    """Rows per rank proportional to each rank's measured rows/ms, in whole
+    `quantum`s within [lo, hi], summing to `total` (a multiple of quantum)."""
+    n = len(speeds)
+    units, lo_u, hi_u = total // quantum, lo // quantum, hi // quantum
+    want = [units * sp / sum(speeds) for sp in speeds]
+    got = [min(max(int(x), lo_u), hi_u) for x in want]
+    # hand out (or take back) the remaining quanta by largest (smallest) residual
+    order = sorted(range(n), key=lambda i: want[i] - got[i], reverse=True)
+    k = 0
+    while sum(got) != units and k < 4 * n * units:
+        i = order[k % n]
+        if sum(got) < units and got[i] < hi_u:
+            got[i] += 1
+        elif sum(got) > units and got[order[n - 1 - k % n]] > lo_u:
+            got[order[n - 1 - k % n]] -= 1
+        k += 1
+    if sum(got) != units:
+        raise ValueError("cannot balance rows within the bounds")
+    return [g * quantum for g in got]
+
+
 def load_peaks():
     p = REPO / "MEASURED_PEAKS.json"
     if p.exists():
@@ -351,18 +373,31 @@ def run_ours(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
 
     bt, h, v = args.rows, CFG["h"], CFG["v"]
+    # N > 1 with balancing: room for up to 25 % more rows on a faster GPU
+    balance = world > 1 and args.balance
+    cap = bt + (bt // 4 if balance else 0)
     gen = torch.Generator(device=dev).manual_seed(1000 + rank)
     wgen = torch.Generator(device=dev).manual_seed(7)
-    hs = torch.randn(bt, h, generator=gen, device=dev).bfloat16()
+    hs_all = torch.randn(cap, h, generator=gen, device=dev).bfloat16()
     w = (CFG["w_std"] * torch.randn(v, h, generator=wgen, device=dev)).bfloat16()
-    tl = torch.empty(bt, v, device=dev, dtype=torch.bfloat16)
-    for r0 in range(0, bt, 1024):  # generate in slabs to bound the fp32 temporary
-        tl[r0:r0 + 1024] = (CFG["teacher_std"] * torch.randn(min(1024, bt - r0), v, generator=gen, device=dev))
-    labels = torch.randint(0, v, (bt,), generator=gen, device=dev)
+    tl_all = torch.empty(cap, v, device=dev, dtype=torch.bfloat16)
+    for r0 in range(0, cap, 1024):  # generate in slabs to bound the fp32 temporary
+        tl_all[r0:r0 + 1024] = (CFG["teacher_std"] * torch.randn(min(1024, cap - r0), v, generator=gen, device=dev))
+    labels_all = torch.randint(0, v, (cap,), generator=gen, device=dev)
+    gsh_all = torch.empty(cap, h, device=dev)
     opts = ob.LossOptions(kd_weight=CFG["kd"], temperature=CFG["temperature"],
                           config=ob.KernelConfig(quantize_grad_weight=True))
-    out = {"grad_student_hidden": torch.empty(bt, h, device=dev), "grad_weight": torch.empty(v, h, device=dev),
-           "scalars": torch.empty(4, device=dev)}
+    out = {"grad_weight": torch.empty(v, h, device=dev), "scalars": torch.empty(4, device=dev)}
+
+    def use_rows(n):
+        """This rank's rows: the first n of the generated inputs."""
+        nonlocal hs, tl, labels
+        hs, tl, labels = hs_all[:n], tl_all[:n], labels_all[:n]
+        out["grad_student_hidden"] = gsh_all[:n]
+
+    hs = tl = labels = None
+    use_rows(bt)
+    rows_per_rank = None
     q = torch.empty(v // world, h, device=dev, dtype=torch.int8)
     qs = torch.empty(v // world, device=dev)
     stream = torch.cuda.current_stream(dev)
@@ -371,7 +406,8 @@ def run_ours(args):
 
     # N > 1: the grad_W reduce-scatter is fused into the wgrad GEMM (peer
     # stores into the owners' slot buffers) unless --reduce nccl
-    fused = shard.SlotReduceScatter(ctx, v, h) if world > 1 and args.reduce == "fused" else None
+    fused = (shard.SlotReduceScatter(ctx, v, h, label_capacity=cap)
+             if world > 1 and args.reduce == "fused" else None)
     gw_slice = torch.empty(v // world, h, device=dev) if fused else None
     if fused:
         del out["grad_weight"]  # the local full grad_W is never materialised
@@ -408,7 +444,7 @@ def run_ours(args):
             def quant(sl, shifted):
                 quantize_grad_w(ctx, sl, shifted, -100, False, 0, q, qs, stream=stream)
 
-            res = shard.row_sharded_step(compute, labels, -100, n_global, quantize=quant)
+            res = shard.row_sharded_step(compute, labels, -100, n_global, quantize=quant, label_capacity=cap)
         ev[1].record(stream)
         marks.append(ev)
         return res
@@ -417,10 +453,28 @@ def run_ours(args):
         step()
     torch.cuda.synchronize()
     ctx.check()
+    if balance:
+        # Power-capped GPUs of one node settle at different clocks, so equal
+        # row blocks finish at different times and every step waits for the
+        # slowest rank. Redistribute the global batch (8192 x N rows, as
+        # before) in proportion to each rank's rows per ms of device time in
+        # the warm-up steps after the first, then warm up again.
+        t_mine = statistics.mean(ev[4].elapsed_time(ev[0]) for ev in marks[1:])
+        tt = torch.tensor([t_mine], device=dev, dtype=torch.float64)
+        all_t = [torch.empty_like(tt) for _ in range(world)]
+        dist.all_gather(all_t, tt)
+        speeds = [bt / float(x) for x in all_t]
+        rows_per_rank = balanced_rows(bt * world, speeds, 16, bt - bt // 4, cap)
+        use_rows(rows_per_rank[rank])
+        n_global = shard.global_non_ignore(labels, -100)
+        for _ in range(args.warmup):
+            step()
+        torch.cuda.synchronize()
+        ctx.check()
 
     # ---------------- timed region
     sampler = None
-    if rank == 0 and not args.no_clocks:
+    if not args.no_clocks:  # every rank samples its own GPU; rank 0's is the line's `clocks`
         uuid = getattr(torch.cuda.get_device_properties(dev), "uuid", None)
         sampler = ClockSampler(f"GPU-{uuid}" if uuid is not None else str(local))
         sampler.start()
@@ -467,6 +521,13 @@ def run_ours(args):
         t = torch.tensor([ms_total], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms_total = float(t.item())
+        if clocks is not None or sampler is not None:
+            mine = torch.tensor([float((clocks or {}).get("sm_mhz") or 0.0), float((clocks or {}).get("power_w_max")
+                                                                                   or 0.0)], device=dev)
+            allc = [torch.empty_like(mine) for _ in range(world)]
+            dist.all_gather(allc, mine)
+            if rank_split is not None:
+                rank_split = [r + [round(float(c[0]), 1), round(float(c[1]), 1)] for r, c in zip(rank_split, allc)]
     ms_step = ms_total / args.steps
     tokens = bt * world
     value = tokens / (ms_step / 1e3)
@@ -498,6 +559,9 @@ def run_ours(args):
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": WORKLOAD if bt == CFG["bt"] else f"{WORKLOAD} [profiling size: {bt} rows]",
                    "global_batch": tokens, "seq_len": None, "rows_per_gpu": bt,
+                   "rows_per_rank": rows_per_rank,
+                   "balance": ("rows redistributed in proportion to each GPU's measured speed (warm-up); "
+                               "the global batch is unchanged") if rows_per_rank else None,
                    "parallelism": (f"rows sharded, grad_W reduce-scatter "
                                    f"({'fused into the wgrad GEMM' if args.reduce == 'fused' else 'NCCL'})"
                                    if world > 1 else "single GPU"),
@@ -505,14 +569,15 @@ def run_ours(args):
         "step_tflops_per_gpu": step_tflops, "step_frac_of_peak": step_tflops / peak,
         "phases_ms_per_step": {k: v_[0] / args.steps for k, v_ in phases.items()},
         "host_enqueue_ms_per_step": host_ms, "collective_ms_per_step": collective_ms,
-        "per_rank_ms": ({"fields": ["device_entry", "barrier_wait", "slot_reduce_quant"] if fused
-                         else ["device_entry"], "ranks": rank_split} if rank_split else None),
+        "per_rank_ms": ({"fields": (["device_entry", "barrier_wait", "slot_reduce_quant"] if fused
+                                    else ["device_entry"]) + ([] if args.no_clocks else ["sm_mhz", "power_w_max"]),
+                         "ranks": rank_split} if rank_split else None),
         "roofline": roofline, "gpu_launches": int(launches), "clocks": clocks,
     }
 
     # ---------------- e2e through the host-Mat C ABI (HOST buffers)
     if not args.no_e2e:
-        line["e2e"] = e2e_measure(args, ob, hs, w, tl, labels, opts, rank, world, dist)
+        line["e2e"] = e2e_measure(args, ob, hs_all[:bt], w, tl_all[:bt], labels_all[:bt], opts, rank, world, dist)
     else:
         line["e2e"] = None
 
@@ -600,6 +665,9 @@ def main():
     ap.add_argument("--config", choices=["c4", "c5"], default="c4",
                     help="c4: the metric configuration (default); c5: the large-vocabulary Tied configuration")
     ap.add_argument("--shard", choices=["rows", "vocab"], default="rows", help="c5 with N > 1: partitioning")
+    ap.add_argument("--balance", action="store_true",
+                    help="N > 1: redistribute rows to each GPU's speed measured in warm-up (off by default: "
+                         "warm-up clocks do not predict the power-capped steady state)")
     ap.add_argument("--reduce", choices=["fused", "nccl"], default="fused",
                     help="N > 1: grad_W reduce-scatter fused into the wgrad GEMM, or an NCCL reduce-scatter")
     args = ap.parse_args()

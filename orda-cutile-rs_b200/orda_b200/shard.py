@@ -44,6 +44,26 @@ def vocab_slice(v: int, world: int, rank: int) -> tuple[int, int]:
     return rank * n, (rank + 1) * n
 
 
+def gather_labels(labels_local: torch.Tensor, ignore_index: int, capacity: Optional[int] = None,
+                  group=None) -> torch.Tensor:
+    """Every rank's labels, concatenated by rank. Ranks may hold different
+    row counts: each contributes `capacity` entries (default: its own count,
+    which must then be equal on all ranks), padded with ignore_index, which
+    marks no target row."""
+    world = dist.get_world_size(group)
+    n = labels_local.numel()
+    cap = n if capacity is None else capacity
+    if n > cap:
+        raise ValueError(f"{n} labels exceed the gather capacity {cap}")
+    padded = labels_local
+    if n < cap:
+        padded = torch.full((cap,), ignore_index, dtype=labels_local.dtype, device=labels_local.device)
+        padded[:n] = labels_local
+    gathered = [torch.empty_like(padded) for _ in range(world)]
+    dist.all_gather(gathered, padded, group=group)
+    return torch.cat(gathered)
+
+
 def global_non_ignore(labels_local: torch.Tensor, ignore_index: int, group=None) -> int:
     cnt = (labels_local != ignore_index).sum().to(torch.int64).reshape(1)
     dist.all_reduce(cnt, group=group)
@@ -78,13 +98,15 @@ def row_sharded_step(
     n_global: int,
     quantize: Optional[Callable[[torch.Tensor, torch.Tensor], None]] = None,
     group=None,
+    label_capacity: Optional[int] = None,
 ) -> ShardResult:
     """One row-sharded step.
 
     compute(n_global) -> (scalars[4], grad_student_hidden, grad_weight) runs
     the local rows with the global denominator. quantize(grad_w_slice,
     labels_shifted) applies the INT8 round trip to the reduced slice, with
-    labels shifted so the slice's first row is 0.
+    labels shifted so the slice's first row is 0. label_capacity: the most
+    rows any rank holds, when ranks hold different row counts.
     """
     scalars, gsh, gw = compute(n_global)
     dist.all_reduce(scalars, group=group)
@@ -93,9 +115,7 @@ def row_sharded_step(
     rank = dist.get_rank(group)
     v0, v1 = vocab_slice(gw.shape[0], world, rank)
     if quantize is not None:
-        gathered = [torch.empty_like(labels_local) for _ in range(world)]
-        dist.all_gather(gathered, labels_local, group=group)
-        labels_all = torch.cat(gathered)
+        labels_all = gather_labels(labels_local, ignore_index, label_capacity, group)
         shifted = torch.where(labels_all == ignore_index, torch.full_like(labels_all, -1), labels_all - v0)
         quantize(sl, shifted)
     return ShardResult(scalars=scalars, grad_student_hidden=gsh, grad_weight_slice=sl, vocab_range=(v0, v1))
@@ -114,9 +134,12 @@ class SlotReduceScatter:
     INT8 round trip in the same pass.
     """
 
-    def __init__(self, ctx, v: int, h: int, group=None):
+    def __init__(self, ctx, v: int, h: int, group=None, label_capacity: Optional[int] = None):
+        """label_capacity: the most rows any rank holds in a step, when ranks
+        hold different row counts (labels are gathered padded to it)."""
         self.ctx = ctx
         self.group = group
+        self.label_capacity = label_capacity
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         self.v0, self.v1 = vocab_slice(v, self.world, self.rank)
@@ -148,9 +171,7 @@ class SlotReduceScatter:
         receives this rank's reduced (and, with quantize, dequantised) rows.
         marks (optional): two CUDA events, recorded after the barrier and
         after the reduction, for timing."""
-        gathered = [torch.empty_like(labels_local) for _ in range(self.world)]
-        dist.all_gather(gathered, labels_local, group=self.group)
-        labels_all = torch.cat(gathered)
+        labels_all = gather_labels(labels_local, ignore_index, self.label_capacity, self.group)
         scalars, gsh = compute(n_global)
         # the scalar all-reduce is also the barrier after which every rank's
         # partials have landed in this rank's slot buffer

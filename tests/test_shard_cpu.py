@@ -29,13 +29,13 @@ def _free_port():
     return p
 
 
-def _problem():
+def _problem(bt=12):
     sys.path.insert(0, str(REPO / "orda-cutile-rs_b200"))
     sys.path.insert(0, str(REPO / "oracle"))
     import oracle
     import orda_b200 as ob
 
-    bt, h, v = 12, 8, 16
+    h, v = 8, 16
     hs = oracle.lcg_fill(bt * h, 5, 0.5).reshape(bt, h)
     ht = oracle.lcg_fill(bt * h, 6, 0.5).reshape(bt, h)
     w = oracle.lcg_fill(v * h, 7, 0.4).reshape(v, h)
@@ -48,7 +48,7 @@ def _opts(ob, reduction, quant):
                           reduction=reduction, config=ob.KernelConfig(quantize_grad_weight=quant))
 
 
-def _worker(rank, world, port, quant, q):
+def _worker(rank, world, port, quant, q, bt=12):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     import datetime
@@ -64,8 +64,9 @@ def _worker(rank, world, port, quant, q):
 
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
     try:
-        bt, h, v, hs, ht, w, labels = _problem()
+        bt, h, v, hs, ht, w, labels = _problem(bt)
         r0, r1 = shard.shard_rows(bt, world, rank)
+        cap = shard.shard_rows(bt, world, 0)[1]  # rank 0 holds the most rows
         lab_local = torch.tensor(labels[r0:r1], dtype=torch.int64)
         n_global = shard.global_non_ignore(lab_local, -100)
 
@@ -84,15 +85,18 @@ def _worker(rank, world, port, quant, q):
             _q, _s, deq = oracle.quantize_grad_w(sl.numpy(), shifted.numpy(), -100)
             sl.copy_(torch.from_numpy(deq))
 
-        res = shard.row_sharded_step(compute, lab_local, -100, n_global, quantize=quantize if quant else None)
+        res = shard.row_sharded_step(compute, lab_local, -100, n_global, quantize=quantize if quant else None,
+                                     label_capacity=cap)
         q.put((rank, res.scalars.numpy(), res.grad_student_hidden.numpy(), res.grad_weight_slice.numpy().copy(),
                res.vocab_range, (r0, r1)))
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("quant", [False, True])
-def test_row_sharded_matches_single_rank(quant):
+@pytest.mark.parametrize("quant,bt", [(False, 12), (True, 12), (True, 13)])
+def test_row_sharded_matches_single_rank(quant, bt):
+    """bt=13 gives the ranks 7 and 6 rows: the label gather pads to the
+    larger count."""
     import torch.multiprocessing as mp
 
     sys.path.insert(0, str(REPO / "orda-cutile-rs_b200"))
@@ -104,7 +108,7 @@ def test_row_sharded_matches_single_rank(quant):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, quant, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, quant, q, bt)) for r in range(world)]
     for p in procs:
         p.start()
     results = sorted([q.get(timeout=120) for _ in range(world)], key=lambda x: x[0])
@@ -112,7 +116,7 @@ def test_row_sharded_matches_single_rank(quant):
         p.join(timeout=60)
         assert p.exitcode == 0
 
-    bt, h, v, hs, ht, w, labels = _problem()
+    bt, h, v, hs, ht, w, labels = _problem(bt)
     full = oracle.distillation_loss(ob.Mat.from_array(hs), ob.Mat.from_array(w), labels,
                                     ob.Teacher.Tied(ob.Mat.from_array(ht)), _opts(ob, ob.Reduction.Mean, quant))
     sc = results[0][1]
