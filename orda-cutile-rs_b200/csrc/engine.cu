@@ -485,7 +485,8 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
         Phase ph_rows(ctx, 1, st);
         if (vphase != 2 && f.need_teacher && !live_teacher) {
           ph_rows.launched();
-          launch_teacher_stats(t_rows, t_ld, t_bf16, static_cast<int>(n), static_cast<int>(v), inv_t, rec_own_t, st);
+          launch_teacher_stats(t_rows, t_ld, t_bf16, static_cast<int>(n), static_cast<int>(v), inv_t, rec_own_t, st,
+                               f.teacher_ce);
         }
         ph_rows.launched(vphase == 1 ? 1 : kRowLaunches);
         RowArgs r{};

@@ -126,9 +126,10 @@ void launch_vocab_partials(const RowArgs& a, cudaStream_t stream);
 void launch_vocab_rows(const RowArgs& a, cudaStream_t stream);
 
 // Teacher statistics pre-pass over given teacher logits (Precomputed mode):
-// one (max, sum e^(t-m), sum e^((t-m)/T), sum t) record per row.
+// one (max, sum e^(t-m), sum e^((t-m)/T), sum t) record per row. need_d1 =
+// false (no teacher CE term) skips sum e^(t-m) and records 1 in its place.
 void launch_teacher_stats(const void* teacher, long long ld, int is_bf16, int n, int v, float inv_t, float* rec,
-                          cudaStream_t stream);
+                          cudaStream_t stream, bool need_d1 = true);
 
 // Label pass: counts non-ignored labels, checks the range [0, v), marks
 // target rows (for the quantiser) and writes the mean scale.

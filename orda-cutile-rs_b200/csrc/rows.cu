@@ -426,7 +426,11 @@ __device__ __forceinline__ float teacher_at(const void* teacher, int is_bf16, lo
 }
 
 // ---- teacher statistics pre-pass over given teacher logits: one CTA per
-// row; every thread keeps four independent 16-byte loads in flight.
+// row; every thread keeps four independent 16-byte loads in flight. The
+// sums cost one exp2 each per element on the SFU, which bounds this kernel
+// before HBM does: NEED_D1 = false (no teacher CE term) skips sum e^(t-m)
+// and records d1 = 1.
+template <bool NEED_D1>
 __global__ void __launch_bounds__(ROW_THREADS) teacher_stats_kernel(const void* teacher, long long ld, int is_bf16,
                                                                     int v, float inv_t, float* rec) {
   __shared__ double sh[3 * 32];
@@ -456,7 +460,7 @@ __global__ void __launch_bounds__(ROW_THREADS) teacher_stats_kernel(const void* 
         for (int k = 0; k < 8; ++k) vm = fmaxf(vm, t[u][k]);
       if (vm > m) {
         const float dm = m - vm;  // -inf on the first block: factors 0
-        d1 *= fast_exp2(dm * LOG2E_F);
+        if (NEED_D1) d1 *= fast_exp2(dm * LOG2E_F);
         dT *= fast_exp2(dm * lt);
         m = vm;
       }
@@ -466,7 +470,7 @@ __global__ void __launch_bounds__(ROW_THREADS) teacher_stats_kernel(const void* 
         for (int k = 0; k < 8; ++k) {
           if (t[u][k] != -INFINITY) {
             const float x = t[u][k] - m;
-            d1 += fast_exp2(x * LOG2E_F);
+            if (NEED_D1) d1 += fast_exp2(x * LOG2E_F);
             dT += fast_exp2(x * lt);
             sx += t[u][k];
           }
@@ -476,7 +480,7 @@ __global__ void __launch_bounds__(ROW_THREADS) teacher_stats_kernel(const void* 
     for (int j = threadIdx.x; j < v; j += ROW_THREADS) m = fmaxf(m, teacher_at(teacher, is_bf16, row * ld + j));
     for (int j = threadIdx.x; j < v; j += ROW_THREADS) {
       const float t = teacher_at(teacher, is_bf16, row * ld + j);
-      d1 += fast_exp2((t - m) * LOG2E_F);
+      if (NEED_D1) d1 += fast_exp2((t - m) * LOG2E_F);
       dT += fast_exp2((t - m) * lt);
       sx += t;
     }
@@ -487,7 +491,7 @@ __global__ void __launch_bounds__(ROW_THREADS) teacher_stats_kernel(const void* 
   double sums[3] = {static_cast<double>(d1) * f1, static_cast<double>(dT) * fT, static_cast<double>(sx)};
   block_sum(sums, sh);
   if (threadIdx.x == 0)
-    reinterpret_cast<float4*>(rec)[row] = make_float4(static_cast<float>(M), static_cast<float>(sums[0]),
+    reinterpret_cast<float4*>(rec)[row] = make_float4(static_cast<float>(M), NEED_D1 ? static_cast<float>(sums[0]) : 1.0f,
                                                       static_cast<float>(sums[1]), static_cast<float>(sums[2]));
 }
 
@@ -657,9 +661,10 @@ void launch_row_grad(const RowArgs& a, cudaStream_t stream) {
 }  // namespace
 
 void launch_teacher_stats(const void* teacher, long long ld, int is_bf16, int n, int v, float inv_t, float* rec,
-                          cudaStream_t stream) {
+                          cudaStream_t stream, bool need_d1) {
   if (n <= 0) return;
-  teacher_stats_kernel<<<n, ROW_THREADS, 0, stream>>>(teacher, ld, is_bf16, v, inv_t, rec);
+  if (need_d1) teacher_stats_kernel<true><<<n, ROW_THREADS, 0, stream>>>(teacher, ld, is_bf16, v, inv_t, rec);
+  else teacher_stats_kernel<false><<<n, ROW_THREADS, 0, stream>>>(teacher, ld, is_bf16, v, inv_t, rec);
 }
 
 void launch_label_prep(const int64_t* labels, long long bt, long long v, int64_t ignore_index, int reduction_sum,

@@ -145,3 +145,17 @@ def test_shard_rows_and_vocab_slices():
     assert shard.vocab_slice(131072, 8, 3) == (49152, 65536)
     with pytest.raises(ValueError):
         shard.vocab_slice(152065, 8, 0)
+
+
+def test_vocab_slice_bounds_cover_the_vocabulary_once():
+    sys.path.insert(0, str(REPO / "orda-cutile-rs_b200"))
+    from orda_b200 import shard
+
+    for v, world in ((152064, 8), (131072, 8), (8192, 3), (1000, 4), (40, 2)):
+        b = [shard.vocab_slice_bounds(v, world, r) for r in range(world)]
+        assert b[0][0] == 0 and b[-1][1] == v
+        assert all(b[i][1] == b[i + 1][0] for i in range(world - 1))
+        assert all(v0 % 8 == 0 and v1 > v0 for v0, v1 in b)
+    assert shard.vocab_slice_bounds(152064, 8, 3) == (57024, 76032)
+    with pytest.raises(ValueError):
+        shard.vocab_slice_bounds(16, 4, 3)  # slices of 8: rank 2 ends the vocabulary
