@@ -159,3 +159,54 @@ def test_vocab_slice_bounds_cover_the_vocabulary_once():
     assert shard.vocab_slice_bounds(152064, 8, 3) == (57024, 76032)
     with pytest.raises(ValueError):
         shard.vocab_slice_bounds(16, 4, 3)  # slices of 8: rank 2 ends the vocabulary
+
+
+def _failing_worker(rank, world, port, q):
+    """Rank 1 fails before the step's first collective; rank 0 must end with
+    an error from the process-group timeout instead of waiting for good."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import datetime
+    import time
+
+    import torch
+    import torch.distributed as dist
+
+    sys.path.insert(0, str(REPO / "orda-cutile-rs_b200"))
+    from orda_b200 import shard
+
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    t0 = time.monotonic()
+    try:
+        if rank == 1:
+            raise RuntimeError("injected failure on rank 1")
+        lab = torch.zeros(4, dtype=torch.int64)
+
+        def compute(n):
+            return torch.zeros(4), torch.zeros(4, 2), torch.zeros(8, 2)
+
+        shard.row_sharded_step(compute, lab, -100, 8)
+        q.put((rank, "no error", time.monotonic() - t0))
+    except Exception as e:  # noqa: BLE001 - the test reports what the rank saw
+        q.put((rank, type(e).__name__, time.monotonic() - t0))
+
+
+def test_failed_rank_ends_the_step_with_an_error():
+    import torch.multiprocessing as mp
+
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_failing_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    seen = dict((r, (what, dt)) for r, what, dt in [q.get(timeout=120) for _ in range(world)])
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    assert seen[1][0] == "RuntimeError"
+    what, dt = seen[0]
+    assert what != "no error", "rank 0 completed a collective its peer never joined"
+    assert dt < 60.0
