@@ -164,19 +164,10 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
-// 2-D tiled bulk tensor load into this CTA's shared memory, completing on
-// `bar` with the box's byte count. x is the innermost coordinate; callers
-// keep x a multiple of 8 bf16 elements (16 bytes).
-__device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int32_t x,
-                                            int32_t y) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
-          smem_u32(smem_dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
-      : "memory");
-}
-
-// As tma_load_2d with an L2 cache policy. CG = 2: the load of one CTA of a
+// 2-D tiled bulk tensor load (x innermost, kept a multiple of 8 bf16
+// elements = 16 bytes) with an L2 cache policy. CG = 1: into this CTA's
+// shared memory, completing on `bar_cluster` (this CTA's barrier) with the
+// box's byte count. CG = 2: the load of one CTA of a
 // CTA pair, completing on the mbarrier at `bar_cluster` (a shared::cluster
 // address, normally the leader CTA's barrier); the data lands in this CTA's
 // shared memory. No multicast.
@@ -198,31 +189,9 @@ __device__ __forceinline__ void tma_load_2d_hint(void* smem_dst, const CUtensorM
   }
 }
 
-// Prefetch of a 2-D box into L2 (no shared-memory destination, no
-// completion tracking).
-__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* map, int32_t x, int32_t y) {
-  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
-                   reinterpret_cast<uint64_t>(map)),
-               "r"(x), "r"(y)
-               : "memory");
-}
-
 // 2-D tiled bulk tensor store (or element-wise add) from this CTA's shared
 // memory to global memory, tracked by the issuing thread's bulk group. The
 // box is clipped at the tensor bounds. x (innermost) stays 16-byte aligned.
-__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* smem_src, int32_t x, int32_t y) {
-  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
-                   reinterpret_cast<uint64_t>(map)),
-               "r"(smem_u32(smem_src)), "r"(x), "r"(y)
-               : "memory");
-}
-__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, const void* smem_src, int32_t x,
-                                                  int32_t y) {
-  asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
-                   reinterpret_cast<uint64_t>(map)),
-               "r"(smem_u32(smem_src)), "r"(x), "r"(y)
-               : "memory");
-}
 __device__ __forceinline__ void tma_store_2d_hint(const CUtensorMap* map, const void* smem_src, int32_t x, int32_t y,
                                                   uint64_t policy) {
   asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group.L2::cache_hint [%0, {%2, %3}], [%1], %4;" ::"l"(
