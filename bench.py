@@ -275,10 +275,14 @@ def run_c5(args):
     else:
         out["grad_weight"] = torch.empty(v1 - v0, h, device=dev)
 
+    # vocabulary-sharded: grad_hidden reduce-scattered by the dgrad GEMMs
+    # (each rank keeps its 8192 rows) unless --reduce nccl (all-reduce)
+    hslots = shard.HiddenSlots(ctx, rows, h, teacher=True) if vocab and args.reduce == "fused" else None
+
     def step():
         if vocab:
             return shard.vocab_sharded_step(ctx, hs, w, labels, ob.TeacherMode.Tied, v, v0, teacher_hidden=ht,
-                                            opts=opts, out=out, stream=stream)
+                                            opts=opts, out=out, stream=stream, hidden_slots=hslots)
         if fused:
             def compute(n):
                 r = distillation_loss_device(ctx, hs, w, labels, ob.TeacherMode.Tied, teacher_hidden=ht, opts=opts,
@@ -334,7 +338,9 @@ def run_c5(args):
             "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": "c5: Tied teacher, 8192 rows per GPU, H=8192, V=152064, kd=0.4, T=1.5",
-                       "parallelism": ("vocabulary sharded (V/N per GPU, all rows on every GPU)" if vocab else
+                       "parallelism": (("vocabulary sharded (V/N per GPU, all rows on every GPU), grad_hidden "
+                                        + ("reduce-scattered by the dgrad GEMMs" if hslots else "all-reduced"))
+                                       if vocab else
                                        "rows sharded, grad_W reduce-scatter fused into the wgrad GEMM"
                                        if world > 1 else "single GPU")},
             "phases_ms_per_step": {k: v_[0] / args.steps for k, v_ in phases.items()},

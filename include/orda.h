@@ -325,6 +325,15 @@ typedef struct OrdaVocabShard {
   int64_t v0;           /* first vocabulary row of this rank's slice */
   int32_t world;        /* ranks whose tuples phase 2 merges */
   int32_t include_rows; /* phase 2: 1 on exactly one rank */
+  int32_t scatter_grad_hidden; /* phase 2: 1 = the dgrad GEMMs write this rank's grad_hidden partial of
+                                  every owner's rows (owner r: rows [r*BT/world, (r+1)*BT/world))
+                                  straight into the owners' slot buffers (orda_context_slots_create
+                                  with slice_rows = BT/world, h = H, copies = 2 when teacher hidden
+                                  gradients exist, set 0 student, set 1 teacher); the grad_*_hidden
+                                  outputs are then not written. After a barrier across the ranks,
+                                  orda_reduce_slot_set_device gives each rank its reduced rows
+                                  (a reduce-scatter of grad_hidden over rows). */
+  int32_t pad;
 } OrdaVocabShard;
 ORDA_API int orda_vocab_forward_device(OrdaContext* ctx, const OrdaDeviceMat* student_hidden,
                                        const OrdaDeviceMat* weight_slice, const int64_t* labels, size_t bt,
@@ -344,8 +353,8 @@ ORDA_API int orda_vocab_backward_device(OrdaContext* ctx, const OrdaDeviceMat* s
  * split the rows across GPUs it replaces a separate NCCL reduce-scatter of
  * the fp32 grad_W.
  *   1. orda_context_slots_create: rank `rank` of `world` allocates its slot
- *      buffer, fp32 [world][slice_rows][h] (slice_rows = V / world), and gets
- *      its CUDA IPC handle;
+ *      buffer, `copies` sets of fp32 [world][slice_rows][h] (here one set,
+ *      slice_rows = V / world), and gets its CUDA IPC handle;
  *   2. the caller all-gathers the handles; orda_context_slots_attach maps the
  *      other ranks' buffers (handles indexed by rank);
  *   3. orda_distillation_loss_device with shard->scatter_grad_weight = 1: the
@@ -362,12 +371,17 @@ typedef struct OrdaIpcHandle {
   char bytes[64];
 } OrdaIpcHandle;
 ORDA_API int orda_context_slots_create(OrdaContext* ctx, int world, int rank, size_t slice_rows, size_t h,
-                                       OrdaIpcHandle* handle_out, char* err, size_t err_len);
+                                       int copies, OrdaIpcHandle* handle_out, char* err, size_t err_len);
 ORDA_API int orda_context_slots_attach(OrdaContext* ctx, const OrdaIpcHandle* handles, char* err, size_t err_len);
 ORDA_API int orda_reduce_slots_device(OrdaContext* ctx, float* grad_w_slice, size_t ld, const int64_t* labels,
                                       size_t n_labels, int64_t ignore_index, int quantize, int stochastic,
                                       uint64_t seed, int8_t* q, float* scale, void* stream, char* err,
                                       size_t err_len);
+/* Sum, in rank order, of the `world` partials in this rank's slot set
+ * `copy` into out [slice_rows, h] (ld >= h), with no quantisation: the
+ * reduce-scatter of grad_hidden of vocabulary-sharded calls. */
+ORDA_API int orda_reduce_slot_set_device(OrdaContext* ctx, int copy, float* out, size_t ld, void* stream, char* err,
+                                         size_t err_len);
 
 /* INT8 row-wise grad_W quantisation on the device: `quantize_grad_w` +
  * `dequantize_grad_w(.., 1.0)` (src/quant.rs:157-202). grad_w [V,H] fp32 is

@@ -72,6 +72,7 @@ struct OrdaContext {
   int slot_rank = -1;
   long long slot_slice = 0;
   long long slot_h = 0;
+  int slot_copies = 1;  // independent [world][slice][h] sets in one buffer
   float* slot_peer[orda::kMaxSlotRanks] = {};  // rank -> its slot buffer (IPC mapping for other ranks)
   bool slots_attached = false;
   // Vocabulary-sharded calls: the workspace layout and shapes of the last
@@ -268,7 +269,13 @@ struct VocabCall {
   const float* partials_in = nullptr;
   int world = 1;
   int include_rows = 1;
+  int scatter_hidden = 0;  // phase 2: dgrad rows go to their owners' slot buffers
 };
+
+// Rank r's slot set `copy` (each set is [world][slice][h] fp32).
+float* slot_set(const OrdaContext* ctx, int r, int copy) {
+  return ctx->slot_peer[r] + static_cast<long long>(copy) * ctx->slot_world * ctx->slot_slice * ctx->slot_h;
+}
 
 int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, const OrdaDeviceOutputs& out,
                const OrdaShardOptions* shard, cudaStream_t st, OrdaChunkPlan* plan_out, char* err, size_t len,
@@ -292,12 +299,23 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
   const bool scatter = shard && shard->scatter_grad_weight;
   f.quant = o.config.quantize_grad_weight != 0 && !(shard && shard->skip_quantize) && !scatter;
 
+  const bool scatter_hidden = vphase == 2 && vc->scatter_hidden;
+  if (scatter_hidden) {
+    const long long need = f.teacher_grad ? 2 : 1;
+    if (!ctx->slots_attached || ctx->slot_slice * ctx->slot_world != static_cast<long long>(in.bt) ||
+        ctx->slot_h != static_cast<long long>(in.h) || ctx->slot_copies < need ||
+        (f.teacher_grad && in.ht_dim != in.h)) {
+      set_error(err, len, "scatter_grad_hidden needs slot buffers of BT/world rows x H with %lld set(s) "
+                          "(orda_context_slots_create / _attach) and H_t == H", need);
+      return ORDA_ERR_INVALID;
+    }
+  }
   if (vphase == 1) {
     if (!vc->partials_out) {
       set_error(err, len, "row_partials output is required");
       return ORDA_ERR_INVALID;
     }
-  } else if (!out.grad_student_hidden || (!out.grad_weight && !scatter) || !out.scalars) {
+  } else if ((!out.grad_student_hidden && !scatter_hidden) || (!out.grad_weight && !scatter) || !out.scalars) {
     set_error(err, len, "grad_student_hidden, grad_weight and scalars outputs are required");
     return ORDA_ERR_INVALID;
   }
@@ -319,7 +337,7 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
       return ORDA_ERR_INVALID;
     }
   }
-  if (vphase != 1 && f.teacher_grad && !out.grad_teacher_hidden) {
+  if (vphase != 1 && !scatter_hidden && f.teacher_grad && !out.grad_teacher_hidden) {
     set_error(err, len, "grad_teacher_hidden output is required (teacher CE weight > 0 with a live teacher)");
     return ORDA_ERR_INVALID;
   }
@@ -539,7 +557,8 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
     const long long rows_g = static_cast<long long>(g1 - g0);
     const long long vv = static_cast<long long>(v);
     // ---- dgrad: grad_h rows = mean_scale * dlogits @ W
-    auto dgrad = [&](const uint16_t* dl, const MatRef& wmat, long long ncols, float* outp, size_t ldo) -> int {
+    auto dgrad = [&](const uint16_t* dl, const MatRef& wmat, long long ncols, float* outp, size_t ldo,
+                     int copy) -> int {
       Phase ph(ctx, 2, st);
       ph.launched();
       GemmDesc gd;
@@ -551,19 +570,30 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
       gd.N = ncols;
       gd.raster_n_fastest = true;
       gd.status = status;
-      gd.args.out0 = outp + g0 * ldo;
-      gd.args.ld0 = static_cast<long long>(ldo);
+      if (scatter_hidden) {
+        // vocabulary-sharded: this rank's partial of every owner's rows goes
+        // straight to the owner's slot set `copy` (a reduce-scatter over rows)
+        gd.args.scatter = 1;
+        gd.args.slot_rank = ctx->slot_rank;
+        gd.args.slot_slice = ctx->slot_slice;
+        gd.args.slot_ld = ctx->slot_h;
+        for (int r = 0; r < ctx->slot_world; ++r) gd.args.slot[r] = slot_set(ctx, r, copy);
+      } else {
+        gd.args.out0 = outp + g0 * ldo;
+        gd.args.ld0 = static_cast<long long>(ldo);
+      }
       gd.args.alpha_ptr = ctx->d_mean_scale;
       cudaError_t ee = gemm_launch(gd, ctx->num_sms, st, &why);
       if (ee != cudaSuccess) return cuda_fail(ee, why ? why : "dgrad GEMM", err, len);
       return ORDA_OK;
     };
-    if (int rc = dgrad(dlog_s, in.w, static_cast<long long>(h), out.grad_student_hidden, out.ld_grad_student_hidden))
+    if (int rc = dgrad(dlog_s, in.w, static_cast<long long>(h), out.grad_student_hidden, out.ld_grad_student_hidden,
+                       0))
       return rc;
     if (f.teacher_grad) {
       const MatRef& tw = in.mode == ORDA_TEACHER_TIED ? in.w : in.wt;
       const long long tn = static_cast<long long>(in.mode == ORDA_TEACHER_TIED ? h : ht);
-      if (int rc = dgrad(dlog_t, tw, tn, out.grad_teacher_hidden, out.ld_grad_teacher_hidden)) return rc;
+      if (int rc = dgrad(dlog_t, tw, tn, out.grad_teacher_hidden, out.ld_grad_teacher_hidden, 1)) return rc;
     }
     // ---- wgrad: grad_W (+)= mean_scale * dlogits^T @ hidden
     {
@@ -784,14 +814,16 @@ static void release_slots(OrdaContext* ctx) {
   ctx->slot_rank = -1;
   ctx->slot_slice = 0;
   ctx->slot_h = 0;
+  ctx->slot_copies = 1;
   ctx->slots_attached = false;
 }
 
-int orda_context_slots_create(OrdaContext* ctx, int world, int rank, size_t slice_rows, size_t h,
+int orda_context_slots_create(OrdaContext* ctx, int world, int rank, size_t slice_rows, size_t h, int copies,
                               OrdaIpcHandle* handle_out, char* err, size_t err_len) {
   if (!ctx || !handle_out || world < 1 || world > orda::kMaxSlotRanks || rank < 0 || rank >= world ||
-      slice_rows == 0 || h == 0) {
-    set_error(err, err_len, "invalid argument (world in [1, %d], rank in [0, world), slice_rows and h > 0)",
+      slice_rows == 0 || h == 0 || copies < 1 || copies > 4) {
+    set_error(err, err_len,
+              "invalid argument (world in [1, %d], rank in [0, world), slice_rows and h > 0, copies in [1, 4])",
               orda::kMaxSlotRanks);
     return ORDA_ERR_INVALID;
   }
@@ -800,11 +832,11 @@ int orda_context_slots_create(OrdaContext* ctx, int world, int rank, size_t slic
   cudaDeviceSynchronize();
   release_slots(ctx);
   void* p = nullptr;
-  cudaError_t e = cudaMalloc(&p, static_cast<size_t>(world) * slice_rows * h * sizeof(float));
+  const size_t bytes = static_cast<size_t>(copies) * world * slice_rows * h * sizeof(float);
+  cudaError_t e = cudaMalloc(&p, bytes);
   if (e != cudaSuccess) {
     cudaGetLastError();
-    set_error(err, err_len, "slot buffer allocation failed (%zu bytes)",
-              static_cast<size_t>(world) * slice_rows * h * sizeof(float));
+    set_error(err, err_len, "slot buffer allocation failed (%zu bytes)", bytes);
     return ORDA_ERR_OOM;
   }
   cudaIpcMemHandle_t hd;
@@ -820,6 +852,7 @@ int orda_context_slots_create(OrdaContext* ctx, int world, int rank, size_t slic
   ctx->slot_rank = rank;
   ctx->slot_slice = static_cast<long long>(slice_rows);
   ctx->slot_h = static_cast<long long>(h);
+  ctx->slot_copies = copies;
   return ORDA_OK;
 }
 
@@ -890,6 +923,24 @@ int orda_reduce_slots_device(OrdaContext* ctx, float* grad_w_slice, size_t ld, c
       ctx->launches += 3;
     }
   }
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "slot reduction", err, err_len);
+  ctx->last_stream = st;
+  return ORDA_OK;
+}
+
+int orda_reduce_slot_set_device(OrdaContext* ctx, int copy, float* out, size_t ld, void* stream, char* err,
+                                size_t err_len) {
+  if (!ctx || !out || !ctx->slots || copy < 0 || copy >= ctx->slot_copies || ld < static_cast<size_t>(ctx->slot_h)) {
+    set_error(err, err_len, "invalid argument (slot buffer, set index in range, output ld >= H)");
+    return ORDA_ERR_INVALID;
+  }
+  std::lock_guard<std::mutex> lock(ctx->mu);
+  cudaSetDevice(ctx->device);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  orda::launch_slot_reduce(ctx->slots + static_cast<long long>(copy) * ctx->slot_world * ctx->slot_slice * ctx->slot_h,
+                           ctx->slot_world, ctx->slot_slice, ctx->slot_h, out, static_cast<long long>(ld), st);
+  ctx->launches += 1;
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "slot reduction", err, err_len);
   ctx->last_stream = st;
@@ -1050,6 +1101,7 @@ int orda_vocab_backward_device(OrdaContext* ctx, const OrdaDeviceMat* student_hi
   vc.v0 = vs->v0;
   vc.world = vs->world;
   vc.include_rows = vs->include_rows;
+  vc.scatter_hidden = vs->scatter_grad_hidden;
   vc.partials_in = all_partials;
   return run_device(ctx, in, *opts, *out, nullptr, static_cast<cudaStream_t>(stream), plan_out, err, err_len, &vc);
 }

@@ -134,7 +134,8 @@ VOCAB_TUPLE = 12  # ORDA_VOCAB_TUPLE
 
 
 class OrdaVocabShard(C.Structure):
-    _fields_ = [("v_total", C.c_int64), ("v0", C.c_int64), ("world", C.c_int32), ("include_rows", C.c_int32)]
+    _fields_ = [("v_total", C.c_int64), ("v0", C.c_int64), ("world", C.c_int32), ("include_rows", C.c_int32),
+                ("scatter_grad_hidden", C.c_int32), ("pad", C.c_int32)]
 
 
 class OrdaIpcHandle(C.Structure):
@@ -216,8 +217,10 @@ SIGNATURES = {
          C.POINTER(OrdaDeviceTeacher), C.POINTER(OrdaLossOptions), C.POINTER(OrdaVocabShard), C.c_void_p,
          C.POINTER(OrdaDeviceOutputs), C.c_void_p, C.POINTER(OrdaChunkPlan), C.c_char_p, C.c_size_t]),
     "orda_context_slots_create": (
-        C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_size_t, C.c_size_t, C.POINTER(OrdaIpcHandle), C.c_char_p,
-                  C.c_size_t]),
+        C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_size_t, C.c_size_t, C.c_int, C.POINTER(OrdaIpcHandle),
+                  C.c_char_p, C.c_size_t]),
+    "orda_reduce_slot_set_device": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_size_t, C.c_void_p, C.c_char_p,
+                                              C.c_size_t]),
     "orda_context_slots_attach": (C.c_int, [C.c_void_p, C.POINTER(OrdaIpcHandle), C.c_char_p, C.c_size_t]),
     "orda_reduce_slots_device": (
         C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p, C.c_size_t, C.c_int64, C.c_int, C.c_int,

@@ -59,13 +59,14 @@ class DeviceContext:
     def launch_count(self) -> int:
         return int(_lib().orda_context_launch_count(self.handle))
 
-    def slots_create(self, world: int, rank: int, slice_rows: int, h: int) -> bytes:
-        """`orda_context_slots_create`: allocates this rank's slot buffer for
-        the fused grad_W reduce-scatter; returns its 64-byte IPC handle."""
+    def slots_create(self, world: int, rank: int, slice_rows: int, h: int, copies: int = 1) -> bytes:
+        """`orda_context_slots_create`: allocates this rank's slot buffer
+        (`copies` sets of [world][slice_rows][h] fp32) for the fused
+        reduce-scatters; returns its 64-byte IPC handle."""
         hd = _abi.OrdaIpcHandle()
         buf = _abi.err_buf()
-        _check(_lib().orda_context_slots_create(self.handle, world, rank, slice_rows, h, C.byref(hd), buf, len(buf)),
-               buf)
+        _check(_lib().orda_context_slots_create(self.handle, world, rank, slice_rows, h, copies, C.byref(hd), buf,
+                                                len(buf)), buf)
         return C.string_at(C.addressof(hd), C.sizeof(hd))
 
     def slots_attach(self, handles: list) -> None:
@@ -89,6 +90,12 @@ class DeviceContext:
             self.handle, grad_w_slice.data_ptr(), grad_w_slice.stride(0), labels.data_ptr(), labels.numel(),
             ignore_index, int(quantize), int(stochastic), seed, _ptr(q), _ptr(scale), _stream(stream), buf,
             len(buf)), buf)
+
+    def reduce_slot_set(self, copy: int, out: torch.Tensor, stream=None) -> None:
+        """`orda_reduce_slot_set_device`: rank-ordered sum of slot set `copy`."""
+        buf = _abi.err_buf()
+        _check(_lib().orda_reduce_slot_set_device(self.handle, copy, out.data_ptr(), out.stride(0), _stream(stream),
+                                                  buf, len(buf)), buf)
 
     def selftest_bounded_wait(self, limit_us: int = 50000, stream=None) -> None:
         """Runs the bounded-wait self-test kernel (a wait that expires)."""
@@ -135,8 +142,8 @@ def _stream(stream) -> int:
 @dataclass
 class DeviceLossResult:
     scalars: torch.Tensor  # device float[4]: loss, student_ce, teacher_ce, kl
-    grad_student_hidden: torch.Tensor
-    grad_weight: torch.Tensor
+    grad_student_hidden: Optional[torch.Tensor]
+    grad_weight: Optional[torch.Tensor]
     grad_teacher_hidden: Optional[torch.Tensor]
     grad_teacher_weight: Optional[torch.Tensor]
     grad_weight_q: Optional[torch.Tensor]
@@ -153,7 +160,7 @@ def _teacher_struct(teacher_mode, teacher_hidden, teacher_weight, teacher_logits
     return t
 
 
-def _outputs(opts, teacher_mode, bt, h, v, ht, dev, out, want_int8, with_grad_weight=True):
+def _outputs(opts, teacher_mode, bt, h, v, ht, dev, out, want_int8, with_grad_weight=True, with_grad_hidden=True):
     """Output tensors (from `out` or newly allocated) and their C struct."""
     w_t = opts.teacher_ce_weight
     if w_t is None:
@@ -161,14 +168,14 @@ def _outputs(opts, teacher_mode, bt, h, v, ht, dev, out, want_int8, with_grad_we
     live = teacher_mode in (TeacherMode.Tied, TeacherMode.Separate)
     out = dict(out or {})
     f32 = dict(device=dev, dtype=torch.float32)
-    gsh = out.get("grad_student_hidden")
-    if gsh is None:
+    gsh = out.get("grad_student_hidden") if with_grad_hidden else None
+    if gsh is None and with_grad_hidden:
         gsh = torch.empty(bt, h, **f32)
     gw = out.get("grad_weight") if with_grad_weight else None
     if gw is None and with_grad_weight:
         gw = torch.empty(v, h, **f32)
-    gth = out.get("grad_teacher_hidden")
-    if gth is None and w_t > 0 and live:
+    gth = out.get("grad_teacher_hidden") if with_grad_hidden else None
+    if gth is None and w_t > 0 and live and with_grad_hidden:
         gth = torch.empty(bt, ht, **f32)
     gtw = out.get("grad_teacher_weight")
     if gtw is None and w_t > 0 and teacher_mode == TeacherMode.Separate:
@@ -184,8 +191,9 @@ def _outputs(opts, teacher_mode, bt, h, v, ht, dev, out, want_int8, with_grad_we
     if scal is None:
         scal = torch.empty(4, **f32)
     o = _abi.OrdaDeviceOutputs()
-    o.grad_student_hidden = gsh.data_ptr()
-    o.ld_grad_student_hidden = gsh.stride(0)
+    if gsh is not None:
+        o.grad_student_hidden = gsh.data_ptr()
+        o.ld_grad_student_hidden = gsh.stride(0)
     if gw is not None:
         o.grad_weight = gw.data_ptr()
         o.ld_grad_weight = gw.stride(0)
@@ -275,7 +283,7 @@ def vocab_forward_device(
     if partials is None:
         partials = torch.empty(bt, _abi.VOCAB_TUPLE, device=student_hidden.device, dtype=torch.float32)
     t = _teacher_struct(teacher_mode, teacher_hidden, teacher_weight_slice, teacher_logits_slice)
-    vs = _abi.OrdaVocabShard(int(v_total), int(v0), 1, 0)
+    vs = _abi.OrdaVocabShard(int(v_total), int(v0), 1, 0, 0, 0)
     buf = _abi.err_buf()
     rc = _lib().orda_vocab_forward_device(
         ctx.handle, C.byref(dev_mat(student_hidden)), C.byref(dev_mat(weight_slice)), labels.data_ptr(),
@@ -302,6 +310,7 @@ def vocab_backward_device(
     out: Optional[dict] = None,
     want_int8: bool = False,
     stream=None,
+    scatter_grad_hidden: bool = False,
 ) -> DeviceLossResult:
     """`orda_vocab_backward_device`: all_partials [world, bt, VOCAB_TUPLE]
     are every rank's tuples by rank. grad_weight (and grad_teacher_weight)
@@ -311,9 +320,11 @@ def vocab_backward_device(
     bt, h = student_hidden.shape
     v = weight_slice.shape[0]
     ht = teacher_hidden.shape[1] if teacher_mode == TeacherMode.Separate else h
-    o, tensors = _outputs(opts, teacher_mode, bt, h, v, ht, student_hidden.device, out, want_int8)
+    o, tensors = _outputs(opts, teacher_mode, bt, h, v, ht, student_hidden.device, out, want_int8,
+                          with_grad_hidden=not scatter_grad_hidden)
     t = _teacher_struct(teacher_mode, teacher_hidden, teacher_weight_slice, teacher_logits_slice)
-    vs = _abi.OrdaVocabShard(int(v_total), int(v0), int(all_partials.shape[0]), int(include_rows))
+    vs = _abi.OrdaVocabShard(int(v_total), int(v0), int(all_partials.shape[0]), int(include_rows),
+                             int(scatter_grad_hidden), 0)
     plan = _abi.OrdaChunkPlan()
     buf = _abi.err_buf()
     rc = _lib().orda_vocab_backward_device(

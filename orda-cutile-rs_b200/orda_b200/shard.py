@@ -143,7 +143,7 @@ class SlotReduceScatter:
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         self.v0, self.v1 = vocab_slice(v, self.world, self.rank)
-        handle = ctx.slots_create(self.world, self.rank, self.v1 - self.v0, h)
+        handle = ctx.slots_create(self.world, self.rank, self.v1 - self.v0, h, 1)
         handles = [None] * self.world
         dist.all_gather_object(handles, handle, group=group)
         ctx.slots_attach(handles)
@@ -203,18 +203,48 @@ def vocab_slice_bounds(v_total: int, world: int, rank: int, align: int = 8) -> t
     return v0, v1
 
 
+class HiddenSlots:
+    """Slot buffers for the vocabulary-sharded grad_hidden reduce-scatter:
+    rank r owns hidden rows [r*BT/world, (r+1)*BT/world); set 0 receives the
+    student's partials, set 1 the teacher's (when teacher hidden gradients
+    exist). The dgrad GEMMs store each owner's rows into its buffer."""
+
+    def __init__(self, ctx, bt: int, h: int, teacher: bool, group=None):
+        self.ctx = ctx
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.r0, self.r1 = shard_rows(bt, self.world, self.rank)
+        if bt % self.world:
+            raise ValueError(f"BT={bt} must be divisible by the world size {self.world}")
+        self.teacher = teacher
+        handle = ctx.slots_create(self.world, self.rank, bt // self.world, h, 2 if teacher else 1)
+        handles = [None] * self.world
+        dist.all_gather_object(handles, handle, group=group)
+        ctx.slots_attach(handles)
+        dev = torch.device("cuda", torch.cuda.current_device())
+        self._token = torch.zeros(1, device=dev)
+        self.grad_student_hidden = torch.empty(self.r1 - self.r0, h, device=dev)
+        self.grad_teacher_hidden = torch.empty(self.r1 - self.r0, h, device=dev) if teacher else None
+        dist.barrier(group=group)
+
+
 def vocab_sharded_step(ctx, student_hidden, weight_slice, labels, teacher_mode, v_total: int, v0: int,
                        teacher_hidden=None, teacher_weight_slice=None, teacher_logits_slice=None, opts=None,
-                       out: Optional[dict] = None, want_int8: bool = False, stream=None, group=None):
+                       out: Optional[dict] = None, want_int8: bool = False, stream=None, group=None,
+                       hidden_slots: Optional[HiddenSlots] = None):
     """One vocabulary-sharded step (tensor parallel over the output head).
 
     Every rank holds all rows of the hidden states and labels and the
     vocabulary rows [v0, v0 + len(weight_slice)) of W (of a Separate
     teacher's W, or those columns of Precomputed teacher logits). The ranks
     exchange one small tuple of row statistics per row (all-gather) between
-    the two device phases, then sum grad_hidden and the scalars (all-reduce).
-    grad_weight of the result is this rank's slice, complete; grad_hidden and
-    the scalars are the full-vocabulary values on every rank.
+    the two device phases, then combine grad_hidden and the scalars.
+    grad_weight of the result is this rank's slice, complete; the scalars are
+    the full-vocabulary values on every rank. grad_hidden is all-reduced (the
+    full [BT, H] on every rank), or, with hidden_slots, reduce-scattered by
+    the dgrad GEMMs themselves: the result then holds this rank's rows
+    hidden_slots.r0:r1 of the full-vocabulary grad_hidden.
     """
     from .device import vocab_backward_device, vocab_forward_device
 
@@ -226,8 +256,20 @@ def vocab_sharded_step(ctx, student_hidden, weight_slice, labels, teacher_mode, 
     every = torch.empty((world,) + tuple(part.shape), device=part.device, dtype=part.dtype)
     dist.all_gather_into_tensor(every, part, group=group)
     res = vocab_backward_device(ctx, student_hidden, weight_slice, labels, teacher_mode, v_total, v0, every,
-                                include_rows=(rank == 0), out=out, want_int8=want_int8, **kw)
+                                include_rows=(rank == 0), out=out, want_int8=want_int8,
+                                scatter_grad_hidden=hidden_slots is not None, **kw)
+    # with hidden_slots this all-reduce is also the barrier after which every
+    # rank's grad_hidden partials have landed in the owners' slot buffers
     dist.all_reduce(res.scalars, group=group)
+    if hidden_slots is not None:
+        ctx.reduce_slot_set(0, hidden_slots.grad_student_hidden, stream=stream)
+        res.grad_student_hidden = hidden_slots.grad_student_hidden
+        if hidden_slots.teacher:
+            ctx.reduce_slot_set(1, hidden_slots.grad_teacher_hidden, stream=stream)
+            res.grad_teacher_hidden = hidden_slots.grad_teacher_hidden
+        # the slot buffers are read; the next step's GEMMs may write them
+        dist.all_reduce(hidden_slots._token, group=group)
+        return res
     dist.all_reduce(res.grad_student_hidden, group=group)
     if res.grad_teacher_hidden is not None:
         dist.all_reduce(res.grad_teacher_hidden, group=group)

@@ -147,7 +147,7 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, outdir):
+def _worker(rank, world, port, outdir, scatter=False):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     os.environ["NCCL_NVLS_ENABLE"] = "0"
@@ -169,18 +169,26 @@ def _worker(rank, world, port, outdir):
         hs, w, labels, kw, opts = _case(ob, mode, dev)
         v0, v1 = shard.vocab_slice_bounds(V, world, rank)
         with DeviceContext(rank) as ctx:
-            r = shard.vocab_sharded_step(ctx, hs, w[v0:v1], labels, mode, V, v0, opts=opts, **_slice_kw(kw, v0, v1))
+            slots = shard.HiddenSlots(ctx, BT, H, teacher=True) if scatter else None
+            rows = (slots.r0, slots.r1) if scatter else (0, BT)
+            # two steps in a row: the second reuses the slot buffers
+            for _ in range(2 if scatter else 1):
+                r = shard.vocab_sharded_step(ctx, hs, w[v0:v1], labels, mode, V, v0, opts=opts, hidden_slots=slots,
+                                             **_slice_kw(kw, v0, v1))
             torch.cuda.synchronize()
             ctx.check()
-        torch.save({"scalars": r.scalars.cpu(), "gsh": r.grad_student_hidden.cpu(),
-                    "gth": r.grad_teacher_hidden.cpu(), "gw": r.grad_weight.cpu(), "vocab": (v0, v1)},
-                   os.path.join(outdir, f"rank{rank}.pt"))
+            torch.save({"scalars": r.scalars.cpu(), "gsh": r.grad_student_hidden.cpu(),
+                        "gth": r.grad_teacher_hidden.cpu(), "gw": r.grad_weight.cpu(), "vocab": (v0, v1),
+                        "rows": rows}, os.path.join(outdir, f"rank{rank}.pt"))
     finally:
         dist.destroy_process_group()
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_vocab_sharded_two_gpus_match_single_gpu(ob, tmp_path):
+@pytest.mark.parametrize("scatter", [False, True])
+def test_vocab_sharded_two_gpus_match_single_gpu(ob, tmp_path, scatter):
+    """grad_hidden all-reduced (full on every rank), or reduce-scattered by
+    the dgrad GEMMs into the owners' slot buffers (each rank its rows)."""
     import torch.multiprocessing as mp
 
     from orda_b200.device import DeviceContext, distillation_loss_device
@@ -188,7 +196,7 @@ def test_vocab_sharded_two_gpus_match_single_gpu(ob, tmp_path):
     world = 2
     port = _free_port()
     ctxm = mp.get_context("spawn")
-    procs = [ctxm.Process(target=_worker, args=(r, world, port, str(tmp_path))) for r in range(world)]
+    procs = [ctxm.Process(target=_worker, args=(r, world, port, str(tmp_path), scatter)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
@@ -208,7 +216,8 @@ def test_vocab_sharded_two_gpus_match_single_gpu(ob, tmp_path):
     parts = [torch.load(tmp_path / f"rank{r}.pt") for r in range(world)]
     for p in parts:
         assert torch.allclose(p["scalars"], full.scalars.cpu(), rtol=1e-5, atol=1e-6)
-        assert rel_l2(p["gsh"].numpy(), full.grad_student_hidden.cpu().numpy()) < 1e-5
-        assert rel_l2(p["gth"].numpy(), full.grad_teacher_hidden.cpu().numpy()) < 1e-5
+        r0, r1 = p["rows"]
+        assert rel_l2(p["gsh"].numpy(), full.grad_student_hidden[r0:r1].cpu().numpy()) < 1e-5
+        assert rel_l2(p["gth"].numpy(), full.grad_teacher_hidden[r0:r1].cpu().numpy()) < 1e-5
         v0, v1 = p["vocab"]
         assert rel_l2(p["gw"].numpy(), full.grad_weight[v0:v1].cpu().numpy()) < 1e-5
