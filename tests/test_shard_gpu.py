@@ -113,10 +113,16 @@ def _worker(rank, world, port, outdir, mode="nccl"):
             sl = torch.full((nsl, H), float("nan"), device=hs.device)
             fused.step(compute_scatter, lab, -100, n_global, sl)
             raw["gw"] = sl.clone()
+            # stochastic rounding: draws indexed by the global grad_W row
+            q_st = torch.empty_like(q)
+            fused.step(compute_scatter, lab, -100, n_global, sl.clone(), quantize=True, stochastic=True, seed=99,
+                       q=q_st, scale=torch.empty_like(qs))
+            raw["q_st"] = q_st
             res = fused.step(compute_scatter, lab, -100, n_global, sl, quantize=True, q=q, scale=qs)
         torch.cuda.synchronize()
         ctx.check()
-        torch.save({"scalars": res.scalars.cpu(), "gsh": res.grad_student_hidden.cpu(), "gw": raw["gw"].cpu(),
+        torch.save({"q_st": raw["q_st"].cpu() if "q_st" in raw else None,
+                    "scalars": res.scalars.cpu(), "gsh": res.grad_student_hidden.cpu(), "gw": raw["gw"].cpu(),
                     "gw_dq": res.grad_weight_slice.cpu(), "q": q.cpu(), "qs": qs.cpu(), "rows": (r0, r1),
                     "vocab": res.vocab_range}, os.path.join(outdir, f"rank{rank}.pt"))
         ctx.close()
@@ -177,5 +183,18 @@ def test_row_sharded_two_gpus_match_single_gpu(ob, tmp_path, mode):
         dq = (p["q"].int() - q.cpu().int()).abs()
         assert int(dq.max()) <= 1
         assert torch.allclose(p["qs"], qs.cpu(), rtol=1e-5, atol=0)
+        if p["q_st"] is not None:
+            # the same slice rounded stochastically on one GPU, with the draw
+            # index offset by the slice's first global row
+            with DeviceContext(0) as ctx:
+                q2 = torch.empty(v1 - v0, H, device=dev, dtype=torch.int8)
+                full_q = torch.empty(V, H, device=dev, dtype=torch.int8)
+                gwf = gw_ref.clone().to(dev)
+                quantize_grad_w(ctx, gwf, labels.clone(), -100, True, 99, full_q, torch.empty(V, device=dev))
+                torch.cuda.synchronize()
+                q2.copy_(full_q[v0:v1])
+            d = (p["q_st"].int() - q2.cpu().int()).abs()
+            assert int(d.max()) <= 1
+            assert float((d == 0).float().mean()) >= 0.999
         # the dequantised slices then agree to within those code differences
         assert rel_l2(p["gw_dq"].numpy(), sl.cpu().numpy()) < 1e-3

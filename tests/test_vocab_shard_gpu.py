@@ -33,7 +33,7 @@ pytestmark = pytest.mark.gpu
 BT, H, HT, V = 256, 512, 384, 8192
 
 
-def _case(ob, mode, dev):
+def _case(ob, mode, dev, stochastic=False):
     g = torch.Generator(device=dev).manual_seed(31 + int(mode))
     hs = torch.randn(BT, H, generator=g, device=dev).bfloat16()
     w = (0.02 * torch.randn(V, H, generator=g, device=dev)).bfloat16()
@@ -49,7 +49,9 @@ def _case(ob, mode, dev):
         opts = ob.LossOptions(kd_weight=0.5, temperature=2.0, teacher_ce_weight=0.7)
     else:
         kw["teacher_logits"] = (2.0 ** 0.5 * torch.randn(BT, V, generator=g, device=dev)).bfloat16()
-        opts = ob.LossOptions(kd_weight=0.4, temperature=1.5, config=ob.KernelConfig(quantize_grad_weight=True))
+        cfg = (ob.KernelConfig(quantize_grad_weight=True, stochastic_rounding=True, stochastic_seed=12345)
+               if stochastic else ob.KernelConfig(quantize_grad_weight=True))
+        opts = ob.LossOptions(kd_weight=0.4, temperature=1.5, config=cfg)
     return hs, w, labels, kw, opts
 
 
@@ -84,14 +86,17 @@ def _check_against_full(ob, full, sc, gsh, gth, gw, gtw, q, qs):
         assert float(rel) < 1e-3
 
 
-@pytest.mark.parametrize("mode", ["Tied", "Separate", "Precomputed"])
+@pytest.mark.parametrize("mode", ["Tied", "Separate", "Precomputed", "PrecomputedStochastic"])
 @pytest.mark.parametrize("bounds", [[0, 2048, 5120, 8192], [0, 4096, 8192]])
 def test_vocab_shards_emulated_on_one_gpu_match_full(ob, mode, bounds):
+    """PrecomputedStochastic: stochastic INT8 rounding, whose draws are indexed
+    by the global grad_W row, so each slice must offset its rows by v0."""
     from orda_b200.device import DeviceContext, distillation_loss_device, vocab_backward_device, vocab_forward_device
 
-    mode = getattr(ob.TeacherMode, mode)
+    stochastic = mode.endswith("Stochastic")
+    mode = getattr(ob.TeacherMode, mode.replace("Stochastic", ""))
     dev = torch.device("cuda", 0)
-    hs, w, labels, kw, opts = _case(ob, mode, dev)
+    hs, w, labels, kw, opts = _case(ob, mode, dev, stochastic)
     quant = opts.config.quantize_grad_weight
     with DeviceContext(0) as ctx:
         full = distillation_loss_device(ctx, hs, w, labels, mode, opts=opts, want_int8=quant, **kw)
