@@ -231,6 +231,20 @@ ORDA_API int orda_context_phase_times(OrdaContext* ctx, double* ms_out, uint64_t
 ORDA_API void orda_context_reset_timing(OrdaContext* ctx);
 /* Total kernels this context has launched (all calls, timing on or off). */
 ORDA_API uint64_t orda_context_launch_count(const OrdaContext* ctx);
+/* Persisting-L2 carve-out for this context's device (cudaLimitPersistingL2CacheSize,
+ * a limit of the CUDA context: it ends with the process). The GEMMs load the
+ * operand that every tile re-reads (the hidden states when they take <= 64 MiB)
+ * with an evict-last policy; those lines stay resident only inside this
+ * carve-out, which CUDA sizes to 0 by default; after each such GEMM a small
+ * kernel returns those lines to normal priority. 64 MiB cut the DRAM traffic of
+ * a c4 step's GEMMs from 42 to 33 GB, but the bandwidth-bound row and INT8
+ * kernels ran about 1.3 ms per step slower with the carve-out in place, so the
+ * step got slower: off unless called (the carve-out is shared by every kernel
+ * of the process). The request is capped at the device maximum and rounded by
+ * the driver to its granularity; *granted receives the limit now in effect.
+ * orda_context_destroy restores the previous limit. */
+ORDA_API int orda_context_set_l2_persisting(OrdaContext* ctx, size_t bytes, size_t* granted, char* err,
+                                            size_t err_len);
 /* Failure-detection self-test: launches a one-warp kernel whose bounded
  * device wait (the same mechanism every kernel uses) on a barrier that nothing
  * completes gives up after limit_us microseconds (at most 1 s) and records a

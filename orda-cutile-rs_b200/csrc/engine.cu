@@ -75,6 +75,10 @@ struct OrdaContext {
   int slot_copies = 1;  // independent [world][slice][h] sets in one buffer
   float* slot_peer[orda::kMaxSlotRanks] = {};  // rank -> its slot buffer (IPC mapping for other ranks)
   bool slots_attached = false;
+  // Persisting-L2 limit set by orda_context_set_l2_persisting, and the
+  // value it replaced (restored by orda_context_destroy).
+  bool l2_set = false;
+  size_t l2_prev = 0;
   // Vocabulary-sharded calls: the workspace layout and shapes of the last
   // orda_vocab_forward_device, whose slice logits the backward phase reuses.
   bool vocab_ready = false;
@@ -457,7 +461,7 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
         Phase ph_fwd(ctx, 0, st);
         // ---- teacher logits + statistics (Tied / Separate)
         if (f.teacher_rows) {
-          ph_fwd.launched();
+          int nl = 0;  // the GEMM and, with an L2 carve-out, the demotion kernel
           GemmDesc gd;
           const MatRef& tw = in.mode == ORDA_TEACHER_TIED ? in.w : in.wt;
           const size_t kdim = in.mode == ORDA_TEACHER_TIED ? h : ht;
@@ -475,11 +479,14 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
           gd.args.n_parts = static_cast<int>(L.parts);
           gd.args.inv_t = inv_t;
           gd.args.own_dT = f.kd > 0.0f;
+          gd.demote_kept = ctx->l2_set;
+          gd.launches = &nl;
           if ((e = gemm_launch(gd, ctx->num_sms, st, &why)) != cudaSuccess)
             return cuda_fail(e, why ? why : "teacher logits GEMM", err, len);
+          ph_fwd.launched(nl);
         }
         // ---- student logits + statistics
-        ph_fwd.launched();
+        int nl = 0;  // the GEMM and, with an L2 carve-out, the demotion kernel
         GemmDesc gd;
         gd.a[0] = MatRef{static_cast<const uint16_t*>(in.hs.ptr) + s * in.hs.ld, static_cast<long long>(n),
                          static_cast<long long>(h), in.hs.ld};
@@ -495,8 +502,11 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
         gd.args.n_parts = static_cast<int>(L.parts);
         gd.args.inv_t = inv_t;
         gd.args.own_dT = f.kd > 0.0f;
+        gd.demote_kept = ctx->l2_set;
+        gd.launches = &nl;
         if ((e = gemm_launch(gd, ctx->num_sms, st, &why)) != cudaSuccess)
           return cuda_fail(e, why ? why : "student logits GEMM", err, len);
+        ph_fwd.launched(nl);
       }
       // ---- row pass: teacher statistics (given logits), losses, logit gradients
       {
@@ -598,7 +608,7 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
     // ---- wgrad: grad_W (+)= mean_scale * dlogits^T @ hidden
     {
       Phase ph(ctx, 3, st);
-      ph.launched();
+      int nl = 0;  // the GEMM and, with an L2 carve-out, the demotion kernel
       GemmDesc gd;
       gd.a_mn_major = true;
       gd.b_mn_major = true;
@@ -631,12 +641,15 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
       }
       gd.args.alpha_ptr = ctx->d_mean_scale;
       gd.args.beta = g0 > 0 ? 1.0f : 0.0f;
+      gd.demote_kept = ctx->l2_set;
+      gd.launches = &nl;
       if ((e = gemm_launch(gd, ctx->num_sms, st, &why)) != cudaSuccess)
         return cuda_fail(e, why ? why : "wgrad GEMM", err, len);
+      ph.launched(nl);
     }
     if (f.teacher_grad && in.mode == ORDA_TEACHER_SEPARATE) {
       Phase ph(ctx, 3, st);
-      ph.launched();
+      int nl = 0;  // the GEMM and, with an L2 carve-out, the demotion kernel
       GemmDesc gd;
       gd.a_mn_major = true;
       gd.b_mn_major = true;
@@ -652,8 +665,11 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
       gd.args.ld0 = static_cast<long long>(out.ld_grad_teacher_weight);
       gd.args.alpha_ptr = ctx->d_mean_scale;
       gd.args.beta = g0 > 0 ? 1.0f : 0.0f;
+      gd.demote_kept = ctx->l2_set;
+      gd.launches = &nl;
       if ((e = gemm_launch(gd, ctx->num_sms, st, &why)) != cudaSuccess)
         return cuda_fail(e, why ? why : "teacher wgrad GEMM", err, len);
+      ph.launched(nl);
     }
   }
   if (vphase == 1) {
@@ -947,10 +963,39 @@ int orda_reduce_slot_set_device(OrdaContext* ctx, int copy, float* out, size_t l
   return ORDA_OK;
 }
 
+int orda_context_set_l2_persisting(OrdaContext* ctx, size_t bytes, size_t* granted, char* err, size_t err_len) {
+  if (!ctx) {
+    set_error(err, err_len, "null context");
+    return ORDA_ERR_INVALID;
+  }
+  std::lock_guard<std::mutex> lock(ctx->mu);
+  cudaSetDevice(ctx->device);
+  int max_bytes = 0;
+  cudaError_t e = cudaDeviceGetAttribute(&max_bytes, cudaDevAttrMaxPersistingL2CacheSize, ctx->device);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute", err, err_len);
+  size_t prev = 0;
+  if ((e = cudaDeviceGetLimit(&prev, cudaLimitPersistingL2CacheSize)) != cudaSuccess)
+    return cuda_fail(e, "cudaDeviceGetLimit", err, err_len);
+  const size_t want = std::min(bytes, static_cast<size_t>(max_bytes > 0 ? max_bytes : 0));
+  if ((e = cudaDeviceSetLimit(cudaLimitPersistingL2CacheSize, want)) != cudaSuccess)
+    return cuda_fail(e, "cudaDeviceSetLimit", err, err_len);
+  if (!ctx->l2_set) {
+    ctx->l2_set = true;
+    ctx->l2_prev = prev;
+  }
+  // the driver rounds the carve-out to its own granularity: report what holds
+  size_t now = want;
+  if ((e = cudaDeviceGetLimit(&now, cudaLimitPersistingL2CacheSize)) != cudaSuccess)
+    return cuda_fail(e, "cudaDeviceGetLimit", err, err_len);
+  if (granted) *granted = now;
+  return ORDA_OK;
+}
+
 void orda_context_destroy(OrdaContext* ctx) {
   if (!ctx) return;
   cudaSetDevice(ctx->device);
   cudaDeviceSynchronize();
+  if (ctx->l2_set) cudaDeviceSetLimit(cudaLimitPersistingL2CacheSize, ctx->l2_prev);
   release_slots(ctx);
   cudaFree(ctx->ws);
   cudaFree(ctx->stage);
@@ -1162,8 +1207,11 @@ int orda_gemm_bf16_device(OrdaContext* ctx, const void* a, size_t lda, int a_kin
   cudaError_t e = cudaMemsetAsync(ctx->d_words, 0, sizeof(int), st);
   if (e != cudaSuccess) return cuda_fail(e, "memset", err, err_len);
   const char* why = nullptr;
-  ctx->launches += 1;
+  int nl = 0;
+  gd.demote_kept = ctx->l2_set;
+  gd.launches = &nl;
   e = gemm_launch(gd, ctx->num_sms, st, &why);
+  ctx->launches += static_cast<uint64_t>(nl);
   if (e != cudaSuccess) return cuda_fail(e, why ? why : "GEMM", err, err_len);
   ctx->last_stream = st;
   return ORDA_OK;

@@ -37,11 +37,12 @@
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
-#include <atomic>
 #include <mutex>
 
 #include "kernels.h"
@@ -565,6 +566,32 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
 }
 
+// Returns the L2 lines of a matrix (rows x row_bytes, row stride ld_bytes) to
+// normal eviction priority with applypriority; only whole 128-byte lines
+// inside each row are touched.
+__global__ void l2_demote_kernel(const uint8_t* base, long long rows, long long row_bytes, long long ld_bytes) {
+  const long long lines = row_bytes / 128 + 1;  // upper bound per row
+  const long long total = rows * lines;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long r = i / lines, l = i - r * lines;
+    const uintptr_t row0 = reinterpret_cast<uintptr_t>(base) + static_cast<uintptr_t>(r * ld_bytes);
+    const uintptr_t first = (row0 + 127) & ~uintptr_t(127);
+    const uintptr_t line = first + static_cast<uintptr_t>(l) * 128;
+    if (line + 128 <= row0 + static_cast<uintptr_t>(row_bytes))
+      asm volatile("applypriority.global.L2::evict_normal [%0], 128;" ::"l"(line) : "memory");
+  }
+}
+
+cudaError_t demote_operand(const MatRef& m, cudaStream_t stream) {
+  const long long lines = m.rows * (m.cols * 2 / 128 + 1);
+  if (lines <= 0) return cudaSuccess;
+  const long long blocks = std::min<long long>((lines + 255) / 256, 4096);
+  l2_demote_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(static_cast<const uint8_t*>(m.ptr), m.rows,
+                                                                      m.cols * 2, m.ld * 2);
+  return cudaGetLastError();
+}
+
 // ------------------------------------------------------------- host side
 
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
@@ -781,8 +808,18 @@ cudaError_t gemm_launch(const GemmDesc& d, int num_sms, cudaStream_t stream, con
     kp.tma_reduce = d.args.beta == 1.0f ? 1 : 0;
   }
   if (kp.num_tiles == 0) return cudaSuccess;
-  if (cg == 2) return dispatch<2>(d, maps, kp, num_sms, stream, why);
-  return dispatch<1>(d, maps, kp, num_sms, stream, why);
+  cudaError_t e = cg == 2 ? dispatch<2>(d, maps, kp, num_sms, stream, why)
+                          : dispatch<1>(d, maps, kp, num_sms, stream, why);
+  if (e != cudaSuccess) return e;
+  int n = 1;
+  if (d.demote_kept && (kp.pol_a == 2 || kp.pol_b == 2)) {
+    for (int s = 0; s < d.nseg && e == cudaSuccess; ++s) {
+      e = demote_operand(kp.pol_a == 2 ? d.a[s] : d.b[s], stream);
+      ++n;
+    }
+  }
+  if (d.launches) *d.launches += n;
+  return e;
 }
 
 }  // namespace orda

@@ -65,6 +65,11 @@ struct GemmDesc {
   Epi epi = Epi::Store;
   EpiArgs args;
   int* status = nullptr;  // device status word
+  // After the GEMM, return the L2 lines of an operand it loaded evict-last to
+  // normal priority (needed when a persisting-L2 carve-out is set: otherwise
+  // they stay pinned and shrink L2 for the kernels that follow).
+  bool demote_kept = false;
+  int* launches = nullptr;  // if set, incremented by the number of kernels launched
 };
 
 // Encodes the tensor maps and launches the persistent tcgen05 GEMM.

@@ -225,6 +225,8 @@ SIGNATURES = {
     "orda_reduce_slots_device": (
         C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p, C.c_size_t, C.c_int64, C.c_int, C.c_int,
                   C.c_uint64, C.c_void_p, C.c_void_p, C.c_void_p, C.c_char_p, C.c_size_t]),
+    "orda_context_set_l2_persisting": (C.c_int, [C.c_void_p, C.c_size_t, C.POINTER(C.c_size_t), C.c_char_p,
+                                                 C.c_size_t]),
     "orda_context_selftest_bounded_wait": (C.c_int, [C.c_void_p, C.c_uint32, C.c_void_p, C.c_char_p, C.c_size_t]),
     "orda_distillation_loss_device": (
         C.c_int,

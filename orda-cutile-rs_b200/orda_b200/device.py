@@ -97,6 +97,14 @@ class DeviceContext:
         _check(_lib().orda_reduce_slot_set_device(self.handle, copy, out.data_ptr(), out.stride(0), _stream(stream),
                                                   buf, len(buf)), buf)
 
+    def set_l2_persisting(self, nbytes: int) -> int:
+        """`orda_context_set_l2_persisting`: persisting-L2 carve-out for the
+        evict-last GEMM operands; returns the bytes granted."""
+        got = C.c_size_t()
+        buf = _abi.err_buf()
+        _check(_lib().orda_context_set_l2_persisting(self.handle, nbytes, C.byref(got), buf, len(buf)), buf)
+        return int(got.value)
+
     def selftest_bounded_wait(self, limit_us: int = 50000, stream=None) -> None:
         """Runs the bounded-wait self-test kernel (a wait that expires)."""
         buf = _abi.err_buf()

@@ -372,3 +372,34 @@ def test_end_to_end_int8_close_but_lossy(ob, oracle, c1):
     # quantiser on that same matrix
     _q, _s, deq = oracle.quantize_grad_w(exact.grad_weight.a, labs, -100)
     assert np.array_equal(deq.view(np.uint32), quant.grad_weight.a.view(np.uint32))
+
+
+def test_l2_persisting_carveout_keeps_results_and_is_restored(ob, c1):
+    """orda_context_set_l2_persisting changes where lines live in L2, not the
+    arithmetic: results are identical with and without it, and destroying the
+    context restores the process's previous limit."""
+    from cuda.bindings import runtime as cudart
+
+    from orda_b200.device import DeviceContext, distillation_loss_device
+
+    s, w, labs, t = c1
+    opts = ob.LossOptions(kd_weight=0.4, temperature=1.5)
+    args = (torch.from_numpy(s.a).cuda().bfloat16(), torch.from_numpy(w.a).cuda().bfloat16(),
+            torch.tensor(labs, dtype=torch.int64, device="cuda"), ob.TeacherMode.Tied)
+    kw = dict(teacher_hidden=torch.from_numpy(t.hidden.a).cuda().bfloat16(), opts=opts)
+    before = cudart.cudaDeviceGetLimit(cudart.cudaLimit.cudaLimitPersistingL2CacheSize)[1]
+    with DeviceContext(0) as ctx:
+        a = distillation_loss_device(ctx, *args, **kw)
+        torch.cuda.synchronize()
+    ctx = DeviceContext(0)
+    granted = ctx.set_l2_persisting(64 << 20)
+    assert granted > 0  # the driver rounds the request to its granularity
+    assert cudart.cudaDeviceGetLimit(cudart.cudaLimit.cudaLimitPersistingL2CacheSize)[1] == granted
+    b = distillation_loss_device(ctx, *args, **kw)
+    torch.cuda.synchronize()
+    ctx.check()
+    ctx.close()
+    assert cudart.cudaDeviceGetLimit(cudart.cudaLimit.cudaLimitPersistingL2CacheSize)[1] == before
+    assert torch.equal(a.scalars, b.scalars)
+    assert torch.equal(a.grad_weight, b.grad_weight)
+    assert torch.equal(a.grad_student_hidden, b.grad_student_hidden)
