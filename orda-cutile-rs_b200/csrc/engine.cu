@@ -83,6 +83,7 @@ struct OrdaContext {
   // orda_vocab_forward_device, whose slice logits the backward phase reuses.
   bool vocab_ready = false;
   size_t vocab_bt = 0, vocab_v = 0, vocab_h = 0;
+  int vocab_flags = 0;  // the options that shape the workspace layout
   OrdaChunkPlan vocab_plan{};
   size_t vocab_layout[24] = {};
 };
@@ -285,6 +286,9 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
                const OrdaShardOptions* shard, cudaStream_t st, OrdaChunkPlan* plan_out, char* err, size_t len,
                const VocabCall* vc = nullptr) {
   const int vphase = vc ? vc->phase : 0;
+  // any other call reuses the workspace that holds a vocabulary forward
+  // phase's slice logits: its backward phase must not run after this
+  if (vphase == 0) ctx->vocab_ready = false;
   Flags f{};
   f.w_s = o.student_ce_weight;
   f.w_t = o.has_teacher_ce_weight ? o.teacher_ce_weight : orda_default_teacher_ce_weight(in.mode);
@@ -359,12 +363,15 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
   AllocTry at{ctx, &in, &f, {}};
   OrdaChunkPlan used{};
   static_assert(sizeof(WsLayout) <= sizeof(ctx->vocab_layout), "saved layout");
+  const int layout_flags = (f.need_teacher ? 1 : 0) | (f.teacher_rows ? 2 : 0) | (f.teacher_grad ? 4 : 0) |
+                           (f.quant ? 8 : 0) | (f.kd > 0.0f ? 16 : 0) | (f.teacher_ce ? 32 : 0);
   bool have = false;
   if (vphase == 2) {
     // the forward phase's workspace, with its slice logits and statistics
-    if (!ctx->vocab_ready || ctx->vocab_bt != bt || ctx->vocab_v != v || ctx->vocab_h != h) {
+    if (!ctx->vocab_ready || ctx->vocab_bt != bt || ctx->vocab_v != v || ctx->vocab_h != h ||
+        ctx->vocab_flags != layout_flags) {
       set_error(err, len, "orda_vocab_backward_device must follow orda_vocab_forward_device on the same context "
-                          "with the same shapes");
+                          "with the same shapes and options");
       return ORDA_ERR_INVALID;
     }
     std::memcpy(&at.layout, ctx->vocab_layout, sizeof(WsLayout));
@@ -679,6 +686,7 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
     ctx->vocab_v = v;
     ctx->vocab_h = h;
     ctx->vocab_plan = used;
+    ctx->vocab_flags = layout_flags;
     ctx->vocab_ready = true;
     ctx->last_stream = st;
     return ORDA_OK;
@@ -919,6 +927,7 @@ int orda_reduce_slots_device(OrdaContext* ctx, float* grad_w_slice, size_t ld, c
     orda::launch_slot_reduce(ctx->slots, ctx->slot_world, slice, h, grad_w_slice, static_cast<long long>(ld), st);
     ctx->launches += 1;
   } else {
+    ctx->vocab_ready = false;  // the flags below overwrite the workspace
     if (ensure_ws(ctx, round_up(static_cast<size_t>(slice), 256)) != cudaSuccess) {
       set_error(err, err_len, "device workspace allocation failed");
       return ORDA_ERR_OOM;
@@ -1162,6 +1171,7 @@ int orda_quantize_grad_w_device(OrdaContext* ctx, float* grad_w, size_t v, size_
   cudaSetDevice(ctx->device);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   // target-row flags live in the context workspace
+  ctx->vocab_ready = false;
   if (ensure_ws(ctx, round_up(v, 256)) != cudaSuccess) {
     set_error(err, err_len, "device workspace allocation failed");
     return ORDA_ERR_OOM;

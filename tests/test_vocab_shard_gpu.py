@@ -140,6 +140,16 @@ def test_vocab_backward_requires_the_forward_phase(ob):
         with pytest.raises(ob.OrdaError, match="must follow orda_vocab_forward_device"):
             vocab_backward_device(ctx, hs, w[:4096], labels, ob.TeacherMode.Tied, V, 0, every, True, opts=opts,
                                   **_slice_kw(kw, 0, 4096))
+        # another call on the context between the phases reuses the workspace
+        # that held the slice logits: the backward phase is refused
+        from orda_b200.device import distillation_loss_device, vocab_forward_device
+
+        vocab_forward_device(ctx, hs, w[:4096], labels, ob.TeacherMode.Tied, V, 0, opts=opts, **_slice_kw(kw, 0, 4096))
+        distillation_loss_device(ctx, hs, w, labels, ob.TeacherMode.Tied, opts=opts, **kw)
+        with pytest.raises(ob.OrdaError, match="must follow orda_vocab_forward_device"):
+            vocab_backward_device(ctx, hs, w[:4096], labels, ob.TeacherMode.Tied, V, 0, every, True, opts=opts,
+                                  **_slice_kw(kw, 0, 4096))
+        torch.cuda.synchronize()
 
 
 # --------------------------------------------------------------- two GPUs
