@@ -198,3 +198,88 @@ def test_row_sharded_two_gpus_match_single_gpu(ob, tmp_path, mode):
             assert float((d == 0).float().mean()) >= 0.999
         # the dequantised slices then agree to within those code differences
         assert rel_l2(p["gw_dq"].numpy(), sl.cpu().numpy()) < 1e-3
+
+
+def _tied_worker(rank, world, port, outdir):
+    """Fused flow with a Tied teacher: the wgrad GEMM runs two K segments
+    (student and teacher rows) into the scattered grad_W partials."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    import datetime
+
+    import torch.distributed as dist
+
+    sys.path.insert(0, str(REPO / "orda-cutile-rs_b200"))
+    import orda_b200 as ob
+    from orda_b200 import shard
+    from orda_b200.device import DeviceContext, distillation_loss_device
+
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        hs, w, _tl, labels = _inputs(dev)
+        ht = (hs.float() + 0.1).bfloat16()
+        r0, r1 = shard.shard_rows(BT, world, rank)
+        lab = labels[r0:r1].contiguous()
+        n_global = shard.global_non_ignore(lab, -100)
+        opts = ob.LossOptions(kd_weight=0.4, temperature=1.5)
+        with DeviceContext(rank) as ctx:
+            fused = shard.SlotReduceScatter(ctx, V, H)
+
+            def compute(n):
+                r = distillation_loss_device(ctx, hs[r0:r1].contiguous(), w, lab, ob.TeacherMode.Tied,
+                                             teacher_hidden=ht[r0:r1].contiguous(), opts=opts, global_non_ignore=n,
+                                             scatter_grad_weight=True)
+                compute.gth = r.grad_teacher_hidden
+                return r.scalars, r.grad_student_hidden
+
+            sl = torch.empty(V // world, H, device=dev)
+            res = fused.step(compute, lab, -100, n_global, sl)
+            torch.cuda.synchronize()
+            ctx.check()
+            torch.save({"scalars": res.scalars.cpu(), "gsh": res.grad_student_hidden.cpu(), "gth": compute.gth.cpu(),
+                        "gw": sl.cpu(), "rows": (r0, r1), "vocab": res.vocab_range},
+                       os.path.join(outdir, f"rank{rank}.pt"))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_row_sharded_tied_fused_two_gpus_match_single_gpu(ob, tmp_path):
+    import torch.multiprocessing as mp
+
+    from conftest import rel_l2
+    from orda_b200.device import DeviceContext, distillation_loss_device
+
+    world = 2
+    port = _free_port()
+    ctxm = mp.get_context("spawn")
+    procs = [ctxm.Process(target=_tied_worker, args=(r, world, port, str(tmp_path))) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    codes = [p.exitcode for p in procs]
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    assert codes == [0, 0], f"rank exit codes {codes}"
+
+    dev = torch.device("cuda", 0)
+    hs, w, _tl, labels = _inputs(dev)
+    ht = (hs.float() + 0.1).bfloat16()
+    with DeviceContext(0) as ctx:
+        ref = distillation_loss_device(ctx, hs, w, labels, ob.TeacherMode.Tied, teacher_hidden=ht,
+                                       opts=ob.LossOptions(kd_weight=0.4, temperature=1.5))
+        torch.cuda.synchronize()
+    for r in range(world):
+        p = torch.load(tmp_path / f"rank{r}.pt")
+        assert torch.allclose(p["scalars"], ref.scalars.cpu(), rtol=1e-5, atol=1e-7)
+        r0, r1 = p["rows"]
+        assert rel_l2(p["gsh"].numpy(), ref.grad_student_hidden[r0:r1].cpu().numpy()) < 1e-5
+        assert rel_l2(p["gth"].numpy(), ref.grad_teacher_hidden[r0:r1].cpu().numpy()) < 1e-5
+        v0, v1 = p["vocab"]
+        assert rel_l2(p["gw"].numpy(), ref.grad_weight[v0:v1].cpu().numpy()) < 1e-5
