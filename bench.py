@@ -13,7 +13,11 @@ the 126 MB L2, so no flush is needed between steps.
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
 N>1 runs under torchrun (one rank per GPU, NCCL): rows are sharded across
-ranks (weak scaling, 8192 rows per GPU) with a reduce-scatter of grad_W.
+ranks (weak scaling, 8192 rows per GPU) and the grad_W reduce-scatter is fused
+into the wgrad GEMM (peer stores into the owners' slot buffers; `--reduce
+nccl` uses an NCCL reduce-scatter instead; `--balance` redistributes rows to
+the GPUs' measured speed). `--config c5` runs BASELINE configs[4] (Tied
+teacher, H=8192, V=152064) with `--shard rows` or `--shard vocab`.
 `--impl reference` times the reference's CPU path (the oracle restatement,
 all host threads) on a bounded row sample of the same workload.
 """
