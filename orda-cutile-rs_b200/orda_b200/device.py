@@ -9,7 +9,7 @@ from typing import Optional
 
 import torch
 
-from . import LossOptions, OrdaError, TeacherMode, ChunkPlan, _abi, _check
+from . import ChunkPlan, LossOptions, TeacherMode, _abi, _check
 from ._abi import load_library
 
 

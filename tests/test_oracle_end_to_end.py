@@ -10,7 +10,6 @@ Sum vs Mean and the INT8 round trip. Data comes from the reference's LCG
 from __future__ import annotations
 
 import numpy as np
-import pytest
 
 
 def _mat(ob, oracle, rows, cols, seed, scale):
