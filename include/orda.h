@@ -416,8 +416,10 @@ ORDA_API int orda_quantize_grad_w_device(OrdaContext* ctx, float* grad_w, size_t
  * Same arguments and results as orda_quantize_grad_w_device without the
  * context; runs on the current device. V above ORDA_NOALLOC_MAX_V is rejected.
  * All calls on a device share the array: calls that overlap on the GPU race,
- * so order them. The first call on each device looks up the array's device
- * address; make it before any CUDA stream capture. */
+ * so order them. Each call looks up the array's device address on the current
+ * device (no caching, so a device reset leaves nothing stale); the first call
+ * on a device also loads the library's device code there: make it before any
+ * CUDA stream capture. */
 #define ORDA_NOALLOC_MAX_V 262144
 ORDA_API int orda_quantize_grad_w_device_noalloc(float* grad_w, size_t v, size_t h, size_t ld, const int64_t* labels,
                                                  size_t bt, int64_t ignore_index, int stochastic, uint64_t seed,

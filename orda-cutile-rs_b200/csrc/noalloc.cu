@@ -16,13 +16,15 @@
 //   * All calls on a device share the one array. Each call clears the part it
 //     uses before use, but calls whose work overlaps on the GPU (different
 //     streams without ordering between them) race on it: order them.
-//   * The array's device address is looked up once per device, on the first
-//     call made with that device current; make that first call before any
+//   * Every call looks up the array's device address for the current device
+//     with cudaGetSymbolAddress (cheap, allocates nothing), so the address is
+//     never stale, also after cudaDeviceReset or a re-created primary
+//     context. The first call on a device also makes CUDA load this
+//     library's device code for that device: make that first call before any
 //     CUDA stream capture.
 #include <cuda_runtime.h>
 
 #include <cstdint>
-#include <mutex>
 
 #include "../../include/orda.h"
 #include "host_logic.h"
@@ -32,23 +34,14 @@ namespace {
 
 static __device__ __align__(256) uint8_t g_noalloc_target_flags[ORDA_NOALLOC_MAX_V];
 
-constexpr int kMaxDevices = 64;
-std::mutex g_noalloc_mu;
-void* g_noalloc_ptr[kMaxDevices] = {nullptr};
-
 // The host-side name of the array is only a stand-in: kernels must receive
 // the device address, which cudaGetSymbolAddress returns for the current
 // device.
-cudaError_t noalloc_scratch(int device, uint8_t** out) {
-  std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (device < 0 || device >= kMaxDevices) return cudaErrorInvalidDevice;
-  if (!g_noalloc_ptr[device]) {
-    void* p = nullptr;
-    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_target_flags);
-    if (e != cudaSuccess) return e;
-    g_noalloc_ptr[device] = p;
-  }
-  *out = static_cast<uint8_t*>(g_noalloc_ptr[device]);
+cudaError_t noalloc_scratch(uint8_t** out) {
+  void* p = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_target_flags);
+  if (e != cudaSuccess) return e;
+  *out = static_cast<uint8_t*>(p);
   return cudaSuccess;
 }
 
@@ -66,10 +59,8 @@ extern "C" int orda_quantize_grad_w_device_noalloc(float* grad_w, size_t v, size
                     ORDA_NOALLOC_MAX_V);
     return ORDA_ERR_INVALID;
   }
-  int device = 0;
-  cudaError_t e = cudaGetDevice(&device);
   uint8_t* flags = nullptr;
-  if (e == cudaSuccess) e = noalloc_scratch(device, &flags);
+  cudaError_t e = noalloc_scratch(&flags);
   if (e != cudaSuccess) {
     orda::set_error(err, err_len, "CUDA error looking up the no-allocation scratch: %s", cudaGetErrorString(e));
     return ORDA_ERR_CUDA;

@@ -21,11 +21,27 @@ W is split by vocabulary rows and every rank sees all tokens.
 """
 from __future__ import annotations
 
+import contextlib
 from dataclasses import dataclass
 from typing import Callable, Optional
 
 import torch
 import torch.distributed as dist
+
+
+def on_stream(stream):
+    """Makes `stream` torch's current stream for a block (None keeps the
+    current one). torch.distributed orders each NCCL collective after the work
+    queued on the current stream when the collective is issued, and makes the
+    current stream wait for it; running a step's collectives on the stream
+    that carries its device calls is what makes the all-reduce that serves as
+    a barrier come after this rank's peer stores, and the slot reduction come
+    after the barrier."""
+    if stream is None:
+        return contextlib.nullcontext()
+    if not isinstance(stream, torch.cuda.Stream):
+        stream = torch.cuda.ExternalStream(int(stream))
+    return torch.cuda.stream(stream)
 
 
 def shard_rows(bt_total: int, world: int, rank: int) -> tuple[int, int]:
@@ -170,7 +186,15 @@ class SlotReduceScatter:
         local rows with scatter_grad_weight; grad_weight_slice [V/world, H]
         receives this rank's reduced (and, with quantize, dequantised) rows.
         marks (optional): two CUDA events, recorded after the barrier and
-        after the reduction, for timing."""
+        after the reduction, for timing. stream: the stream the device calls
+        of `compute` use (default: the current stream); the step's
+        collectives run on it too."""
+        with on_stream(stream):
+            return self._step(compute, labels_local, ignore_index, n_global, grad_weight_slice, quantize,
+                              stochastic, seed, q, scale, stream, marks)
+
+    def _step(self, compute, labels_local, ignore_index, n_global, grad_weight_slice, quantize, stochastic, seed,
+              q, scale, stream, marks):
         labels_all = gather_labels(labels_local, ignore_index, self.label_capacity, self.group)
         scalars, gsh = compute(n_global)
         # the scalar all-reduce is also the barrier after which every rank's
@@ -244,8 +268,19 @@ def vocab_sharded_step(ctx, student_hidden, weight_slice, labels, teacher_mode, 
     the full-vocabulary values on every rank. grad_hidden is all-reduced (the
     full [BT, H] on every rank), or, with hidden_slots, reduce-scattered by
     the dgrad GEMMs themselves: the result then holds this rank's rows
-    hidden_slots.r0:r1 of the full-vocabulary grad_hidden.
+    hidden_slots.r0:r1 of the full-vocabulary grad_hidden. stream: the
+    stream of the device calls (default: the current stream); the
+    collectives run on it too.
     """
+    with on_stream(stream):
+        return _vocab_sharded_step(ctx, student_hidden, weight_slice, labels, teacher_mode, v_total, v0,
+                                   teacher_hidden, teacher_weight_slice, teacher_logits_slice, opts, out, want_int8,
+                                   stream, group, hidden_slots)
+
+
+def _vocab_sharded_step(ctx, student_hidden, weight_slice, labels, teacher_mode, v_total, v0, teacher_hidden,
+                        teacher_weight_slice, teacher_logits_slice, opts, out, want_int8, stream, group,
+                        hidden_slots):
     from .device import vocab_backward_device, vocab_forward_device
 
     world = dist.get_world_size(group)

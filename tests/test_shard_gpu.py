@@ -11,10 +11,12 @@ the same bf16 products in another order), and the INT8 codes of the slice
 within one code of the single-GPU ones (a scale computed from a grad_W row
 that differs in the last bits can move a value across a rounding boundary).
 
-Two variants: the NCCL reduce-scatter of the full local grad_W, and the fused
+Three variants: the NCCL reduce-scatter of the full local grad_W; the fused
 path in which the wgrad GEMM writes each owner's rows straight into the
 owner's slot buffer (CUDA IPC peer stores) and the owner sums the partials
-and quantises them in one pass.
+and quantises them in one pass; and the fused path driven on a side stream
+that is not torch's current stream (the barrier all-reduce must still follow
+the peer stores queued on that stream).
 
 Skipped unless two GPUs are visible. Ranks run as spawned processes with a
 short process-group timeout; NVLS is off so no rank binds multicast memory.
@@ -103,22 +105,31 @@ def _worker(rank, world, port, outdir, mode="nccl"):
             # row (the second reuses the buffers), first without the INT8 step to
             # keep the raw reduced slice, then with it
             fused = shard.SlotReduceScatter(ctx, V, H)
+            # "fused_side": every device call and collective of the steps runs
+            # on a stream that is not torch's current one (the step makes it
+            # current for its collectives)
+            st = torch.cuda.Stream(dev) if mode == "fused_side" else None
+            if st is not None:
+                st.wait_stream(torch.cuda.current_stream(dev))
+            hs_l, tl_l = hs[r0:r1].contiguous(), tl[r0:r1].contiguous()
 
             def compute_scatter(n):
-                r = distillation_loss_device(ctx, hs[r0:r1].contiguous(), w, lab, ob.TeacherMode.Precomputed,
-                                             teacher_logits=tl[r0:r1].contiguous(), opts=_opts(ob),
-                                             global_non_ignore=n, scatter_grad_weight=True)
+                r = distillation_loss_device(ctx, hs_l, w, lab, ob.TeacherMode.Precomputed, teacher_logits=tl_l,
+                                             opts=_opts(ob), global_non_ignore=n, scatter_grad_weight=True,
+                                             stream=st)
                 return r.scalars, r.grad_student_hidden
 
             sl = torch.full((nsl, H), float("nan"), device=hs.device)
-            fused.step(compute_scatter, lab, -100, n_global, sl)
+            fused.step(compute_scatter, lab, -100, n_global, sl, stream=st)
+            if st is not None:
+                st.synchronize()
             raw["gw"] = sl.clone()
             # stochastic rounding: draws indexed by the global grad_W row
             q_st = torch.empty_like(q)
             fused.step(compute_scatter, lab, -100, n_global, sl.clone(), quantize=True, stochastic=True, seed=99,
-                       q=q_st, scale=torch.empty_like(qs))
+                       q=q_st, scale=torch.empty_like(qs), stream=st)
             raw["q_st"] = q_st
-            res = fused.step(compute_scatter, lab, -100, n_global, sl, quantize=True, q=q, scale=qs)
+            res = fused.step(compute_scatter, lab, -100, n_global, sl, quantize=True, q=q, scale=qs, stream=st)
         torch.cuda.synchronize()
         ctx.check()
         torch.save({"q_st": raw["q_st"].cpu() if "q_st" in raw else None,
@@ -131,7 +142,7 @@ def _worker(rank, world, port, outdir, mode="nccl"):
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("mode", ["nccl", "fused"])
+@pytest.mark.parametrize("mode", ["nccl", "fused", "fused_side"])
 def test_row_sharded_two_gpus_match_single_gpu(ob, tmp_path, mode):
     import torch.multiprocessing as mp
 

@@ -3,8 +3,9 @@
 orda_quantize_grad_w_device_noalloc serves callers that cannot call
 cudaMalloc (allocator hooks, out-of-memory handlers, runtimes that forbid
 device allocations after start-up): its scratch is a fixed device array in
-the library instead of a context workspace. This test checks that its output
-equals the regular entry point's (orda_quantize_grad_w_device) on two calls in
+the library instead of a context workspace. These tests check that its output
+equals the regular entry point's (orda_quantize_grad_w_device) and, bit for
+bit, the oracle's restatement of the reference quantiser, each on two calls in
 a row, the second with different labels so stale scratch from the first call
 would show, and that a V above the stated limit is rejected.
 
@@ -66,6 +67,35 @@ def test_noalloc_quantizer_matches_regular_entry_twice(stochastic):
             tgt = sorted({int(t) for t in labels.tolist() if t != -100})
             kept = (got == base).all(dim=1).nonzero().flatten().tolist()
             assert set(tgt) <= set(kept)
+
+
+@pytest.mark.parametrize("stochastic", [False, True])
+def test_noalloc_quantizer_bit_exact_with_oracle(oracle, stochastic):
+    """The allocation-free entry against the oracle's restatement of
+    `quantize_grad_w` + `dequantize_grad_w` (src/quant.rs:157-202) directly:
+    INT8 codes, scales and the dequantised matrix bit-identical on the same
+    fp32 grad_W, on two calls in a row with different target rows."""
+    import orda_b200 as ob
+
+    lib = ob.load_library()
+    gen = torch.Generator().manual_seed(17)
+    v, h = 2053, 384
+    base = (torch.randn(v, h, generator=gen) * torch.rand(v, 1, generator=gen) ** 3 * 1e-3).numpy()
+    base[11, :] = 0.0  # amax 0: the scale comes from the 1e-12 floor
+    for call, n_labels in enumerate((700, 23)):
+        labels = torch.randint(0, v, (n_labels,), generator=gen)
+        labels[::6] = -100
+        seed = 4242 + call
+        q_ref, s_ref, deq_ref = oracle.quantize_grad_w(base, labels.numpy(), -100, stochastic=stochastic, seed=seed)
+        g = torch.from_numpy(base).cuda()
+        q = torch.empty(v, h, dtype=torch.int8, device="cuda")
+        s = torch.empty(v, device="cuda")
+        rc, msg = _call_noalloc(lib, g, labels.cuda(), stochastic, seed, q, s)
+        assert rc == 0, msg
+        torch.cuda.synchronize()
+        assert np.array_equal(q.cpu().numpy(), q_ref)
+        assert np.array_equal(s.cpu().numpy().view(np.uint32), s_ref.view(np.uint32))
+        assert np.array_equal(g.cpu().numpy().view(np.uint32), deq_ref.view(np.uint32))
 
 
 def test_noalloc_rejects_v_above_limit():
