@@ -200,6 +200,16 @@ ORDA_API int orda_distillation_loss(const OrdaMatF32* student_hidden, const Orda
                            size_t n_labels, const OrdaTeacher* teacher, const OrdaLossOptions* opts,
                            OrdaOutput* out, char* err, size_t err_len);
 ORDA_API void orda_output_free(OrdaOutput* out);
+/* Copy pipeline of orda_distillation_loss. The call overlaps its host<->device
+ * copies with the device work: the bf16 operands are copied first, then
+ * Precomputed teacher logits in row slabs of about `bytes` (whole chunks of
+ * the resolver's plan) when they exceed two slabs; each slab's forward and
+ * backward work runs while the next slab is copied, and grad_hidden rows are
+ * copied back as they are final. Results do not depend on the slab size
+ * beyond fp32 summation order of grad_W. 0 restores the default (512 MiB).
+ * Process-wide; no counterpart in the reference (src/api.rs:188-422 has no
+ * device copies). */
+ORDA_API void orda_set_host_slab_bytes(size_t bytes);
 
 /* ---------------------------------------------------------------------------
  * Device entry (replaces the GPU launcher src/cuda/launch.rs:51-158, which

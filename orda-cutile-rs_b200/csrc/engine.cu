@@ -24,6 +24,9 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
+#include <condition_variable>
+#include <functional>
 #include <map>
 #include <unordered_map>
 #include <cstdio>
@@ -32,6 +35,7 @@
 #include <memory>
 #include <mutex>
 #include <optional>
+#include <thread>
 #include <vector>
 
 #include "../../include/orda.h"
@@ -50,7 +54,9 @@ struct OrdaContext {
   size_t stage_bytes = 0;
   int inject_fail = 0;
   cudaStream_t last_stream = nullptr;
-  cudaStream_t own_stream = nullptr;
+  cudaStream_t own_stream = nullptr;  // host-Mat entry: compute stream
+  cudaStream_t copy_in = nullptr;     // host-Mat entry: host->device copies
+  cudaStream_t copy_out = nullptr;    // host-Mat entry: device->host copies
   std::mutex mu;
   // phase timing (see orda_context_enable_timing)
   bool timing = false;
@@ -277,6 +283,19 @@ struct VocabCall {
   int scatter_hidden = 0;  // phase 2: dgrad rows go to their owners' slot buffers
 };
 
+// Hooks through which the host-Mat entry overlaps its host<->device copies
+// with the device work: run_device calls them, on the host, at fixed points
+// of its launch order on the compute stream.
+struct HostPipe {
+  size_t group_rows = 0;  // > 0: forward and backward groups of this many rows (whole chunks)
+  // before the row pass of the forward group of rows [s, s + n) (its teacher
+  // logits must have landed); a non-zero return aborts the call
+  std::function<int(size_t s, size_t n)> before_rows;
+  // after the dgrad launches of the backward group [g0, g1) (its grad_hidden
+  // rows are final)
+  std::function<int(size_t g0, size_t g1)> after_dgrad;
+};
+
 // Rank r's slot set `copy` (each set is [world][slice][h] fp32).
 float* slot_set(const OrdaContext* ctx, int r, int copy) {
   return ctx->slot_peer[r] + static_cast<long long>(copy) * ctx->slot_world * ctx->slot_slice * ctx->slot_h;
@@ -284,7 +303,7 @@ float* slot_set(const OrdaContext* ctx, int r, int copy) {
 
 int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, const OrdaDeviceOutputs& out,
                const OrdaShardOptions* shard, cudaStream_t st, OrdaChunkPlan* plan_out, char* err, size_t len,
-               const VocabCall* vc = nullptr) {
+               const VocabCall* vc = nullptr, const HostPipe* hp = nullptr) {
   const int vphase = vc ? vc->phase : 0;
   // any other call reuses the workspace that holds a vocabulary forward
   // phase's slice logits: its backward phase must not run after this
@@ -390,10 +409,20 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
     used = plan;
     have = true;
   } else {
+    if (hp && hp->group_rows > 0) {
+      // the host entry's pipelined grouping (whole chunks), if it fits
+      const size_t gr = std::min(bt, round_up(hp->group_rows, plan.chunk_size));
+      const WsLayout c = make_layout(in, f, plan.chunk_size, gr, gr);
+      if (ensure_ws(ctx, c.total) == cudaSuccess) {
+        at.layout = c;
+        used = plan;
+        have = true;
+      }
+    }
     // Rung 0 is the resolver's plan itself (a Fixed chunk size keeps its row
     // count); after an allocation failure the ladder doubles the chunk count
     // along chunk_doubling_schedule, as the upstream dispatcher does.
-    have = try_alloc_cb(plan.num_chunks, plan.chunk_size, &at) == 0;
+    if (!have) have = try_alloc_cb(plan.num_chunks, plan.chunk_size, &at) == 0;
     if (have) used = plan;
   }
   if (!have) {
@@ -516,6 +545,9 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
         ph_fwd.launched(nl);
       }
       // ---- row pass: teacher statistics (given logits), losses, logit gradients
+      if (hp && hp->before_rows) {
+        if (int rc = hp->before_rows(s, n)) return rc;
+      }
       {
         Phase ph_rows(ctx, 1, st);
         if (vphase != 2 && f.need_teacher && !live_teacher) {
@@ -611,6 +643,9 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
       const MatRef& tw = in.mode == ORDA_TEACHER_TIED ? in.w : in.wt;
       const long long tn = static_cast<long long>(in.mode == ORDA_TEACHER_TIED ? h : ht);
       if (int rc = dgrad(dlog_t, tw, tn, out.grad_teacher_hidden, out.ld_grad_teacher_hidden, 1)) return rc;
+    }
+    if (hp && hp->after_dgrad) {
+      if (int rc = hp->after_dgrad(g0, g1)) return rc;
     }
     // ---- wgrad: grad_W (+)= mean_scale * dlogits^T @ hidden
     {
@@ -735,6 +770,9 @@ int check_status(OrdaContext* ctx, char* err, size_t len) {
   }
   return ORDA_OK;
 }
+
+// Teacher-logit slab of the host entry's copy pipeline (bytes).
+std::atomic<size_t> g_host_slab_bytes{size_t{512} << 20};
 
 std::mutex g_default_mu;
 OrdaContext* g_default_ctx[64] = {nullptr};
@@ -1010,7 +1048,8 @@ void orda_context_destroy(OrdaContext* ctx) {
   cudaFree(ctx->stage);
   cudaFree(ctx->d_words);
   cudaFree(ctx->d_mean_scale);
-  if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
+  for (cudaStream_t sp : {ctx->own_stream, ctx->copy_in, ctx->copy_out})
+    if (sp) cudaStreamDestroy(sp);
   for (auto& pe : ctx->pending) {
     cudaEventDestroy(pe.begin);
     cudaEventDestroy(pe.end);
@@ -1328,16 +1367,36 @@ int orda_distillation_loss(const OrdaMatF32* student_hidden, const OrdaMatF32* w
   }
   std::lock_guard<std::mutex> lock(ctx->mu);
   cudaSetDevice(ctx->device);
-  if (!ctx->own_stream) cudaStreamCreateWithFlags(&ctx->own_stream, cudaStreamNonBlocking);
-  cudaStream_t st = ctx->own_stream;
+  // compute, host->device and device->host streams
+  for (cudaStream_t* sp : {&ctx->own_stream, &ctx->copy_in, &ctx->copy_out})
+    if (!*sp) cudaStreamCreateWithFlags(sp, cudaStreamNonBlocking);
+  cudaStream_t st = ctx->own_stream, cin = ctx->copy_in, cout = ctx->copy_out;
 
   const OrdaTeacherMode mode = teacher->mode;
   const bool live = mode == ORDA_TEACHER_TIED || mode == ORDA_TEACHER_SEPARATE;
+  const bool pre = mode == ORDA_TEACHER_PRECOMPUTED;
   const size_t ht = mode == ORDA_TEACHER_SEPARATE ? teacher->hidden.cols : h;
   const bool tgrad = w_t > 0.0f && live;
   const size_t ldh = round_up(h, 8), ldht = round_up(ht, 8), ldtl = round_up(v, 4);
 
-  // staging layout
+  // Pipeline groups. Precomputed teacher logits (the largest input) are
+  // copied in row slabs of about kTeacherSlab bytes; the device runs the
+  // forward and backward work of a slab's rows (whole chunks of the
+  // resolver's plan) while the next slab is in flight, and each backward
+  // group's grad_hidden rows go back to the host while later slabs arrive.
+  const size_t kTeacherSlab = g_host_slab_bytes.load();
+  constexpr size_t kRingBytes = size_t{64} << 20;  // f32 staging of the bf16 inputs
+  const OrdaChunkPlan plan0 = resolve_chunk_size(bt, opts->chunk_size, true, v, opts->config.has_max_chunks != 0,
+                                                 opts->config.max_chunks);
+  size_t group_rows = 0;
+  if (pre && bt * v * 4 > 2 * kTeacherSlab && plan0.chunk_size > 0) {
+    size_t rows = kTeacherSlab / (v * 4) / plan0.chunk_size * plan0.chunk_size;
+    rows = std::max(rows, plan0.chunk_size);
+    if (rows < bt) group_rows = rows;
+  }
+  const size_t n_groups = group_rows ? ceil_div(bt, group_rows) : 1;
+
+  // device staging layout
   size_t off = 0;
   auto take = [&](size_t bytes) {
     const size_t o = off;
@@ -1346,13 +1405,13 @@ int orda_distillation_loss(const OrdaMatF32* student_hidden, const OrdaMatF32* w
   };
   const size_t o_hs = take(bt * ldh * 2), o_w = take(v * ldh * 2);
   const size_t o_ht = take(live ? bt * ldht * 2 : 0), o_wt = take(mode == ORDA_TEACHER_SEPARATE ? v * ldht * 2 : 0);
-  const size_t o_tl = take(mode == ORDA_TEACHER_PRECOMPUTED ? bt * ldtl * 4 : 0);
+  const size_t o_tl = take(pre ? bt * ldtl * 4 : 0);
   const size_t o_lab = take(bt * 8);
   const size_t o_ghs = take(bt * h * 4), o_gw = take(v * h * 4);
   const size_t o_ght = take(tgrad ? bt * ht * 4 : 0), o_gwt = take(tgrad && mode == ORDA_TEACHER_SEPARATE ? v * ht * 4 : 0);
   const size_t o_sc = take(4 * sizeof(float));
-  size_t tmp_elems = std::max({bt * h, v * h, live ? bt * ht : size_t{0}, mode == ORDA_TEACHER_SEPARATE ? v * ht : size_t{0}});
-  const size_t o_tmp = take(tmp_elems * 4);
+  const size_t ring_bytes = std::max(kRingBytes, std::max(h, ht) * 4);
+  const size_t o_ring = take(ring_bytes);
   if (ctx->stage_bytes < off) {
     cudaFree(ctx->stage);
     ctx->stage = nullptr;
@@ -1366,26 +1425,128 @@ int orda_distillation_loss(const OrdaMatF32* student_hidden, const OrdaMatF32* w
     ctx->stage_bytes = off;
   }
   uint8_t* S = static_cast<uint8_t*>(ctx->stage);
-  float* tmp = reinterpret_cast<float*>(S + o_tmp);
-  cudaError_t e;
-  auto upload_bf16 = [&](const OrdaMatF32& m, size_t ld, size_t o) -> cudaError_t {
-    cudaError_t ee = cudaMemcpyAsync(tmp, m.data, m.rows * m.cols * 4, cudaMemcpyHostToDevice, st);
-    if (ee != cudaSuccess) return ee;
-    launch_f32_to_bf16(tmp, static_cast<long long>(m.rows), static_cast<long long>(m.cols),
-                       reinterpret_cast<uint16_t*>(S + o), static_cast<long long>(ld), st);
-    return cudaGetLastError();
+
+  // library-owned page-locked outputs
+  auto host_mat = [&](size_t rows, size_t cols, OrdaMatOut& m) -> bool {
+    m.rows = rows;
+    m.cols = cols;
+    m.data = pinned_alloc(std::max<size_t>(rows * cols, 1) * 4);
+    return m.data != nullptr;
   };
-  if ((e = upload_bf16(*student_hidden, ldh, o_hs)) != cudaSuccess) return cuda_fail(e, "upload", err, err_len);
-  if ((e = upload_bf16(*weight, ldh, o_w)) != cudaSuccess) return cuda_fail(e, "upload", err, err_len);
-  if (live && (e = upload_bf16(teacher->hidden, ldht, o_ht)) != cudaSuccess) return cuda_fail(e, "upload", err, err_len);
-  if (mode == ORDA_TEACHER_SEPARATE && (e = upload_bf16(teacher->weight, ldht, o_wt)) != cudaSuccess)
-    return cuda_fail(e, "upload", err, err_len);
-  if (mode == ORDA_TEACHER_PRECOMPUTED) {
-    e = cudaMemcpy2DAsync(S + o_tl, ldtl * 4, teacher->logits.data, v * 4, v * 4, bt, cudaMemcpyHostToDevice, st);
-    if (e != cudaSuccess) return cuda_fail(e, "upload", err, err_len);
+  float* sc_host = pinned_alloc(4 * sizeof(float));
+  bool ok_alloc = sc_host && host_mat(bt, h, out->grad_student_hidden) && host_mat(v, h, out->grad_weight);
+  if (ok_alloc && tgrad) ok_alloc = host_mat(bt, ht, out->grad_teacher_hidden);
+  if (ok_alloc && tgrad && mode == ORDA_TEACHER_SEPARATE) ok_alloc = host_mat(v, ht, out->grad_teacher_weight);
+  if (!ok_alloc) {
+    pinned_release(sc_host);
+    orda_output_free(out);
+    set_error(err, err_len, "page-locked host allocation for the outputs failed");
+    return ORDA_ERR_OOM;
   }
-  if ((e = cudaMemcpyAsync(S + o_lab, labels, bt * 8, cudaMemcpyHostToDevice, st)) != cudaSuccess)
-    return cuda_fail(e, "upload", err, err_len);
+
+  // events, destroyed when the call ends
+  std::vector<cudaEvent_t> events;
+  auto mk_event = [&]() {
+    cudaEvent_t e = nullptr;
+    cudaEventCreateWithFlags(&e, cudaEventDisableTiming);
+    events.push_back(e);
+    return e;
+  };
+  cudaEvent_t ev_inputs = mk_event();
+  std::vector<cudaEvent_t> ev_teacher;
+  for (size_t k = 0; k < (pre ? n_groups : 0); ++k) ev_teacher.push_back(mk_event());
+
+  // ---- copier thread: every host->device copy on `cin`, in the order the
+  // device needs them (labels, the bf16 operands through the f32 ring and a
+  // conversion kernel, then the teacher-logit slabs), recording an event
+  // after each stage and announcing it. A separate thread keeps pageable
+  // sources (whose copies return only when consumed) from delaying the
+  // kernel launches of the main thread.
+  struct Feed {
+    std::mutex mu;
+    std::condition_variable cv;
+    size_t announced = 0;  // stages whose events are recorded
+    cudaError_t error = cudaSuccess;
+  } feed;
+  auto announce = [&feed](size_t n, cudaError_t e) {
+    std::lock_guard<std::mutex> lk(feed.mu);
+    feed.announced = n;
+    if (e != cudaSuccess && feed.error == cudaSuccess) feed.error = e;
+    feed.cv.notify_all();
+  };
+  float* ring = reinterpret_cast<float*>(S + o_ring);
+  std::thread copier([&]() {
+    cudaSetDevice(ctx->device);
+    cudaError_t e = cudaMemcpyAsync(S + o_lab, labels, bt * 8, cudaMemcpyHostToDevice, cin);
+    // f32 host rows -> ring -> bf16 device rows (one stream: each slab's copy
+    // follows the conversion of the previous one, so one ring buffer serves)
+    auto put_bf16 = [&](const OrdaMatF32& m, size_t ld, size_t o) {
+      const size_t per = std::max<size_t>(1, ring_bytes / (m.cols * 4));
+      for (size_t r0 = 0; r0 < m.rows && e == cudaSuccess; r0 += per) {
+        const size_t n = std::min(per, m.rows - r0);
+        e = cudaMemcpyAsync(ring, m.data + r0 * m.cols, n * m.cols * 4, cudaMemcpyHostToDevice, cin);
+        if (e != cudaSuccess) break;
+        launch_f32_to_bf16(ring, static_cast<long long>(n), static_cast<long long>(m.cols),
+                           reinterpret_cast<uint16_t*>(S + o) + r0 * ld, static_cast<long long>(ld), cin);
+        e = cudaGetLastError();
+      }
+    };
+    if (e == cudaSuccess) put_bf16(*student_hidden, ldh, o_hs);
+    if (e == cudaSuccess) put_bf16(*weight, ldh, o_w);
+    if (e == cudaSuccess && live) put_bf16(teacher->hidden, ldht, o_ht);
+    if (e == cudaSuccess && mode == ORDA_TEACHER_SEPARATE) put_bf16(teacher->weight, ldht, o_wt);
+    if (e == cudaSuccess) e = cudaEventRecord(ev_inputs, cin);
+    if (e != cudaSuccess) {
+      announce(SIZE_MAX, e);
+      return;
+    }
+    announce(1, cudaSuccess);
+    for (size_t k = 0; k < ev_teacher.size(); ++k) {
+      const size_t r0 = k * (group_rows ? group_rows : bt);
+      const size_t n = std::min(group_rows ? group_rows : bt, bt - r0);
+      e = cudaMemcpy2DAsync(S + o_tl + r0 * ldtl * 4, ldtl * 4, teacher->logits.data + r0 * v, v * 4, v * 4, n,
+                            cudaMemcpyHostToDevice, cin);
+      if (e == cudaSuccess) e = cudaEventRecord(ev_teacher[k], cin);
+      if (e != cudaSuccess) {
+        announce(SIZE_MAX, e);
+        return;
+      }
+      announce(k + 2, cudaSuccess);
+    }
+  });
+  // waits (host) until stage n is announced; then its event may be waited on
+  auto wait_stage = [&](size_t n) -> int {
+    std::unique_lock<std::mutex> lk(feed.mu);
+    feed.cv.wait(lk, [&] { return feed.announced >= n || feed.error != cudaSuccess; });
+    if (feed.error != cudaSuccess) return cuda_fail(feed.error, "host->device copy", err, err_len);
+    return ORDA_OK;
+  };
+  auto finish = [&](int rc) {
+    if (copier.joinable()) copier.join();
+    if (rc == ORDA_OK && feed.error != cudaSuccess) rc = cuda_fail(feed.error, "host->device copy", err, err_len);
+    if (rc == ORDA_OK) {
+      cudaError_t e = cudaStreamSynchronize(cout);
+      if (e != cudaSuccess) rc = cuda_fail(e, "device->host copy", err, err_len);
+    }
+    if (rc == ORDA_OK) rc = check_status(ctx, err, err_len);
+    if (rc != ORDA_OK) {
+      // nothing may still write into the outputs when they are released
+      cudaStreamSynchronize(cin);
+      cudaStreamSynchronize(st);
+      cudaStreamSynchronize(cout);
+    }
+    for (cudaEvent_t e : events) cudaEventDestroy(e);
+    if (rc == ORDA_OK) {
+      out->loss = sc_host[0];
+      out->student_ce = sc_host[1];
+      out->teacher_ce = sc_host[2];
+      out->kl = sc_host[3];
+    } else {
+      orda_output_free(out);
+    }
+    pinned_release(sc_host);
+    return rc;
+  };
 
   OrdaDeviceOutputs dout{};
   dout.grad_student_hidden = reinterpret_cast<float*>(S + o_ghs);
@@ -1414,44 +1575,57 @@ int orda_distillation_loss(const OrdaMatF32* student_hidden, const OrdaMatF32* w
   if (live) in.ht = MatRef{S + o_ht, static_cast<long long>(bt), static_cast<long long>(ht), static_cast<long long>(ldht)};
   if (mode == ORDA_TEACHER_SEPARATE)
     in.wt = MatRef{S + o_wt, static_cast<long long>(v), static_cast<long long>(ht), static_cast<long long>(ldht)};
-  if (mode == ORDA_TEACHER_PRECOMPUTED) {
+  if (pre) {
     in.t_logits = S + o_tl;
     in.ld_t_logits = static_cast<long long>(ldtl);
     in.t_logits_bf16 = false;
   }
-  OrdaChunkPlan plan{};
-  if (int rc = run_device(ctx, in, *opts, dout, nullptr, st, &plan, err, err_len)) return rc;
 
-  // download into library-owned host buffers
-  auto dl = [&](float* dsrc, size_t rows, size_t cols, OrdaMatOut& m) -> cudaError_t {
-    m.rows = rows;
-    m.cols = cols;
-    m.data = pinned_alloc(std::max<size_t>(rows * cols, 1) * 4);
-    if (!m.data) return cudaErrorMemoryAllocation;
-    return cudaMemcpyAsync(m.data, dsrc, rows * cols * 4, cudaMemcpyDeviceToHost, st);
+  if (int rc = wait_stage(1)) return finish(rc);
+  if (cudaError_t e = cudaStreamWaitEvent(st, ev_inputs, 0); e != cudaSuccess) return finish(cuda_fail(e, "event wait", err, err_len));
+  HostPipe hp;
+  hp.group_rows = group_rows;
+  if (pre) {
+    // the row pass of rows [s, s + n) needs the slabs that hold them (copies
+    // on one stream complete in order: the last slab's event covers all)
+    hp.before_rows = [&](size_t s0, size_t n) -> int {
+      const size_t k = group_rows ? (s0 + n - 1) / group_rows : 0;
+      if (int rc = wait_stage(k + 2)) return rc;
+      cudaError_t e = cudaStreamWaitEvent(st, ev_teacher[k], 0);
+      return e == cudaSuccess ? ORDA_OK : cuda_fail(e, "event wait", err, err_len);
+    };
+  }
+  hp.after_dgrad = [&](size_t g0, size_t g1) -> int {
+    cudaEvent_t ev = mk_event();
+    cudaError_t e = cudaEventRecord(ev, st);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(cout, ev, 0);
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(out->grad_student_hidden.data + g0 * h, dout.grad_student_hidden + g0 * h,
+                          (g1 - g0) * h * 4, cudaMemcpyDeviceToHost, cout);
+    if (e == cudaSuccess && tgrad)
+      e = cudaMemcpyAsync(out->grad_teacher_hidden.data + g0 * ht, dout.grad_teacher_hidden + g0 * ht,
+                          (g1 - g0) * ht * 4, cudaMemcpyDeviceToHost, cout);
+    return e == cudaSuccess ? ORDA_OK : cuda_fail(e, "device->host copy", err, err_len);
   };
-  float sc[4] = {0, 0, 0, 0};
-  e = dl(dout.grad_student_hidden, bt, h, out->grad_student_hidden);
-  if (e == cudaSuccess) e = dl(dout.grad_weight, v, h, out->grad_weight);
-  if (e == cudaSuccess && tgrad) e = dl(dout.grad_teacher_hidden, bt, ht, out->grad_teacher_hidden);
+  OrdaChunkPlan plan{};
+  if (int rc = run_device(ctx, in, *opts, dout, nullptr, st, &plan, err, err_len, nullptr, &hp)) return finish(rc);
+
+  // grad_W (after the INT8 round trip, if any) and the scalars
+  cudaEvent_t ev_done = mk_event();
+  cudaError_t e = cudaEventRecord(ev_done, st);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(cout, ev_done, 0);
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(out->grad_weight.data, dout.grad_weight, v * h * 4, cudaMemcpyDeviceToHost, cout);
   if (e == cudaSuccess && tgrad && mode == ORDA_TEACHER_SEPARATE)
-    e = dl(dout.grad_teacher_weight, v, ht, out->grad_teacher_weight);
-  if (e == cudaSuccess) e = cudaMemcpyAsync(sc, dout.scalars, sizeof sc, cudaMemcpyDeviceToHost, st);
-  if (e != cudaSuccess) {
-    orda_output_free(out);
-    return cuda_fail(e, "download", err, err_len);
-  }
-  if (int rc = check_status(ctx, err, err_len)) {
-    orda_output_free(out);
-    return rc;
-  }
-  out->loss = sc[0];
-  out->student_ce = sc[1];
-  out->teacher_ce = sc[2];
-  out->kl = sc[3];
+    e = cudaMemcpyAsync(out->grad_teacher_weight.data, dout.grad_teacher_weight, v * ht * 4, cudaMemcpyDeviceToHost,
+                        cout);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(sc_host, dout.scalars, 4 * sizeof(float), cudaMemcpyDeviceToHost, cout);
+  if (e != cudaSuccess) return finish(cuda_fail(e, "device->host copy", err, err_len));
   out->chunk_plan = plan;
-  return ORDA_OK;
+  return finish(ORDA_OK);
 }
+
+void orda_set_host_slab_bytes(size_t bytes) { g_host_slab_bytes.store(bytes ? bytes : (size_t{512} << 20)); }
 
 void orda_output_free(OrdaOutput* out) {
   if (!out) return;

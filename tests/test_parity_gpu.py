@@ -447,3 +447,40 @@ def test_edge_cases_match_oracle(ob, oracle, case):
         assert rel_l2(g.grad_weight.a[17], r.grad_weight.a[17]) < GRAD_REL_L2
         return
     assert_parity(g, r, case)
+
+
+# ------------------------------------------------- host entry copy pipeline
+
+@pytest.mark.parametrize("quantize", [False, True])
+def test_host_entry_slab_pipeline_matches_oracle(ob, oracle, quantize):
+    """orda_distillation_loss with the teacher-logit copy pipeline engaged
+    (slabs shrunk to 512 KiB, so 256 rows x V=4096 f32 run as 8 forward /
+    backward groups of 32 rows while later slabs are in flight): parity with
+    the oracle, and with the same call in one group (grad_W summed over the
+    groups in another fp32 order: rel-L2 1e-5)."""
+    lib = ob.load_library()
+    gen = torch.Generator().manual_seed(404)
+    bt, h, v = 256, 256, 4096
+    s = randn_mat(ob, bt, h, gen)
+    w = randn_mat(ob, v, h, gen, 0.05)
+    tl = ob.Mat.from_array((np.sqrt(2.0) * torch.randn(bt, v, generator=gen)).numpy())
+    labs = torch.randint(0, v, (bt,), generator=gen).tolist()
+    labs[3] = labs[100] = -100
+    t = ob.Teacher.Precomputed(tl)
+    opts = ob.LossOptions(kd_weight=0.4, temperature=1.5, label_smoothing=0.05, chunk_size=ob.ChunkSize.Fixed(32),
+                          config=ob.KernelConfig(quantize_grad_weight=quantize))
+    try:
+        lib.orda_set_host_slab_bytes(512 << 10)
+        piped = ob.distillation_loss(s, w, labs, t, opts)
+    finally:
+        lib.orda_set_host_slab_bytes(0)
+    whole = ob.distillation_loss(s, w, labs, t, opts)
+    assert piped.chunk_plan == ob.ChunkPlan(32, 8)
+    assert abs(piped.loss - whole.loss) <= 1e-6 * abs(whole.loss)
+    assert rel_l2(piped.grad_student_hidden.a, whole.grad_student_hidden.a) < 1e-6
+    if quantize:
+        # codes may move by one where the summation order changes a scale
+        assert rel_l2(piped.grad_weight.a, whole.grad_weight.a) < 1e-2
+    else:
+        assert rel_l2(piped.grad_weight.a, whole.grad_weight.a) < 1e-5
+    assert_parity(piped, oracle.distillation_loss(s, w, labs, t, opts, nthreads=NT), "pipelined")
