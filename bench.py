@@ -535,8 +535,9 @@ def run_ours(args):
 
     use_rows(bt)
     rows_per_rank = None
-    q = torch.empty(v // world, h, device=dev, dtype=torch.int8)
-    qs = torch.empty(v // world, device=dev)
+    vs0, vs1 = shard.vocab_slice(v, world, rank) if world > 1 else (0, v)
+    q = torch.empty(vs1 - vs0, h, device=dev, dtype=torch.int8)
+    qs = torch.empty(vs1 - vs0, device=dev)
     stream = torch.cuda.current_stream(dev)
     ctx = DeviceContext(D.local)
     n_global = bt * world if world == 1 else shard.global_non_ignore(labels, -100)
@@ -545,7 +546,7 @@ def run_ours(args):
     # stores into the owners' slot buffers) unless --reduce nccl
     fused = (shard.SlotReduceScatter(ctx, v, h, label_capacity=cap)
              if world > 1 and args.reduce == "fused" else None)
-    gw_slice = torch.empty(v // world, h, device=dev) if fused else None
+    gw_slice = torch.empty(vs1 - vs0, h, device=dev) if fused else None
     if fused:
         del out["grad_weight"]  # the local full grad_W is never materialised
     marks = []  # (after compute, end of step) events of the timed steps
@@ -784,9 +785,9 @@ def verify_c4_sharded(torch, ob, shard, D, ctx, fused, w, q, qs, args, rows=256)
     st = torch.cuda.current_stream(dev)
     sc_v = torch.empty(4, device=dev)
     gh = torch.empty(rows, h, device=dev)
-    sl_raw = torch.empty(v // world, h, device=dev)
-    sl_q = torch.empty(v // world, h, device=dev)
-    v0 = rank * (v // world)
+    v0, v1 = shard.vocab_slice(v, world, rank)
+    sl_raw = torch.empty(v1 - v0, h, device=dev)
+    sl_q = torch.empty(v1 - v0, h, device=dev)
     if fused:
         def compute(n):
             r = distillation_loss_device(ctx, hs, w, labels, ob.TeacherMode.Precomputed, teacher_logits=tl,
@@ -836,8 +837,8 @@ def verify_c4_sharded(torch, ob, shard, D, ctx, fused, w, q, qs, args, rows=256)
         ctx.check()
     for t in (gw_ref, q_ref, gh_ref, sc_ref):
         D.dist.broadcast(t, src=0)
-    ref_sl = gw_ref[v0:v0 + v // world]
-    dq = (q.int() - q_ref[v0:v0 + v // world].int()).abs()
+    ref_sl = gw_ref[v0:v1]
+    dq = (q.int() - q_ref[v0:v1].int()).abs()
     stats = D.sum(torch, [
         float(((sl_raw.double() - ref_sl.double()) ** 2).sum()), float((ref_sl.double() ** 2).sum()),
         float(((gh.double() - gh_ref[rank * rows:(rank + 1) * rows].double()) ** 2).sum()),
@@ -926,7 +927,8 @@ def e2e_sharded(torch, ob, shard, D, ctx, fused, hs, w, tl, labels, opts, args):
     for r0 in range(0, bt, 1024):
         tl_h[r0:r0 + 1024].copy_(tl[r0:r0 + 1024].float())
     lab_h = labels.cpu().pin_memory()
-    gw_h = torch.empty(v // world, h, pin_memory=True)
+    v0, v1 = shard.vocab_slice(v, world, D.rank)
+    gw_h = torch.empty(v1 - v0, h, pin_memory=True)
     gh_h = torch.empty(bt, h, pin_memory=True)
     sc_h = torch.empty(4, pin_memory=True)
     st = torch.cuda.current_stream(dev)
@@ -936,9 +938,9 @@ def e2e_sharded(torch, ob, shard, D, ctx, fused, hs, w, tl, labels, opts, args):
     lab_d = torch.empty(bt, dtype=torch.int64, device=dev)
     gh = torch.empty(bt, h, device=dev)
     sc = torch.empty(4, device=dev)
-    sl = torch.empty(v // world, h, device=dev)
-    q = torch.empty(v // world, h, device=dev, dtype=torch.int8)
-    qs = torch.empty(v // world, device=dev)
+    sl = torch.empty(v1 - v0, h, device=dev)
+    q = torch.empty(v1 - v0, h, device=dev, dtype=torch.int8)
+    qs = torch.empty(v1 - v0, device=dev)
     n_global = shard.global_non_ignore(labels, -100)
 
     def one():
@@ -982,7 +984,7 @@ def e2e_sharded(torch, ob, shard, D, ctx, fused, hs, w, tl, labels, opts, args):
     per = D.max(torch, statistics.mean(times))
     ctx.check()
     h2d = bt * h * 4 + v * h * 4 + bt * v * 4 + bt * 8
-    d2h = (v // world) * h * 4 + bt * h * 4 + 16
+    d2h = (v1 - v0) * h * 4 + bt * h * 4 + 16
     return {"value": bt * world / per, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
             "ms_per_step": per * 1e3, "scope": "sharded (per rank: its rows, W and its grad_W slice)",
             "api": "orda_b200.shard.SlotReduceScatter + orda_distillation_loss_device (f32 pinned host inputs)"}
@@ -1012,8 +1014,8 @@ def run_c5_part(torch, ob, shard, D, args, part):
            "grad_teacher_hidden": torch.empty(rows, h, device=dev), "scalars": torch.empty(4, device=dev)}
     fused = gw_slice = hslots = None
     if world > 1 and not vocab:
-        fused = shard.SlotReduceScatter(ctx, v, h)
-        gw_slice = torch.empty(v // world, h, device=dev)
+        fused = shard.SlotReduceScatter(ctx, v, h, int8_wire=args.int8_wire)
+        gw_slice = torch.empty(fused.v1 - fused.v0, h, device=dev)
         n_global = shard.global_non_ignore(labels, -100)
     else:
         out["grad_weight"] = torch.empty(v1 - v0, h, device=dev)
@@ -1032,7 +1034,8 @@ def run_c5_part(torch, ob, shard, D, args, part):
         if fused:
             def compute(n):
                 r = distillation_loss_device(ctx, hs, w, labels, ob.TeacherMode.Tied, teacher_hidden=ht, opts=opts,
-                                             out=out, global_non_ignore=n, scatter_grad_weight=True, stream=stream)
+                                             out=out, global_non_ignore=n, scatter_grad_weight=True, stream=stream,
+                                             int8_wire=args.int8_wire)
                 return r.scalars, r.grad_student_hidden
 
             return fused.step(compute, labels, -100, n_global, gw_slice, stream=stream)
@@ -1074,7 +1077,10 @@ def run_c5_part(torch, ob, shard, D, args, part):
             del out
             out = None
             torch.cuda.empty_cache()
-            res["parity"] = {"sharded_vs_one_gpu": verify_c5_sharded(torch, ob, shard, D, ctx, part, args)}
+            res["parity"] = {"sharded_vs_one_gpu": verify_c5_sharded(torch, ob, shard, D, ctx, part, args,
+                                                                     int8_wire=args.int8_wire and not vocab)}
+            if args.int8_wire and not vocab:
+                res["grad_w_exchange"] = "INT8 wire format (row-wise codes + fp32 scales)"
         res["parity"]["pass"] = all(p.get("pass", True) for p in res["parity"].values())
     ctx.close()
     del hs, ht, labels, w, out
@@ -1100,10 +1106,11 @@ def verify_c5_vocab_one_gpu(torch, ob, ctx, hs, ht, w, labels, opts, out, stream
     return res
 
 
-def verify_c5_sharded(torch, ob, shard, D, ctx, part, args, rows=256):
+def verify_c5_sharded(torch, ob, shard, D, ctx, part, args, rows=256, int8_wire=False):
     """One small c5 step (H, V of c5) through the sharded path of `part`
     against the whole problem on one GPU (rank 0 computes, then broadcasts):
-    scalars, this rank's grad_W rows and grad_hidden rows within 1e-5."""
+    scalars, this rank's grad_W rows and grad_hidden rows within 1e-5 (with
+    the INT8 wire format, grad_W within its stated 2e-2)."""
     from orda_b200.device import distillation_loss_device
 
     world, rank, dev = D.world, D.rank, D.dev
@@ -1124,17 +1131,18 @@ def verify_c5_sharded(torch, ob, shard, D, ctx, part, args, rows=256):
     else:
         hs, ht, labels = c5_rows(torch, rows, dev, 6000 + rank)
         w = c5_weight_slice(torch, 0, v, dev)
-        fused = shard.SlotReduceScatter(ctx, v, h)
+        fused = shard.SlotReduceScatter(ctx, v, h, int8_wire=int8_wire)
         n_global = shard.global_non_ignore(labels, -100)
         gth = {}
 
         def compute(n):
             r = distillation_loss_device(ctx, hs, w, labels, ob.TeacherMode.Tied, teacher_hidden=ht, opts=opts,
-                                         global_non_ignore=n, scatter_grad_weight=True, stream=st)
+                                         global_non_ignore=n, scatter_grad_weight=True, stream=st,
+                                         int8_wire=int8_wire)
             gth["t"] = r.grad_teacher_hidden
             return r.scalars, r.grad_student_hidden
 
-        v0, v1 = rank * (v // world), (rank + 1) * (v // world)
+        v0, v1 = shard.vocab_slice(v, world, rank)
         my_gw = torch.empty(v1 - v0, h, device=dev)
         res = fused.step(compute, labels, -100, n_global, my_gw, stream=st)
         r0, r1 = rank * rows, (rank + 1) * rows
@@ -1168,7 +1176,7 @@ def verify_c5_sharded(torch, ob, shard, D, ctx, part, args, rows=256):
         float(((my_gth.double() - gth_ref[r0:r1].double()) ** 2).sum()), float((gth_ref[r0:r1].double() ** 2).sum()),
     ])
     sc_err = D.max(torch, scalars_rel(res.scalars.cpu().numpy(), sc_ref.cpu().numpy()))
-    tol_w = grad_w_tol(2 * rows * world)  # Tied: student and teacher rows
+    tol_w = 2e-2 if int8_wire else grad_w_tol(2 * rows * world)  # Tied: student and teacher rows
     out = {"rows": rows * world, "scalars_rel": sc_err, "grad_weight_rel_l2": (stats[0] / stats[1]) ** 0.5,
            "grad_hidden_rel_l2": (stats[2] / stats[3]) ** 0.5,
            "grad_teacher_hidden_rel_l2": (stats[4] / stats[5]) ** 0.5, "tol": TOL["shard_rel"],
@@ -1222,6 +1230,9 @@ def main():
                          "warm-up clocks do not predict the power-capped steady state)")
     ap.add_argument("--reduce", choices=["fused", "nccl"], default="fused",
                     help="N > 1: grad_W reduce-scatter fused into the wgrad GEMM, or an NCCL reduce-scatter")
+    ap.add_argument("--int8-wire", action="store_true",
+                    help="--config c5 --shard rows, N > 1: grad_W partials exchanged as row-wise INT8 + scales "
+                         "(lossy; the verification then reports its error against the fp32 exchange)")
     args = ap.parse_args()
     if args.warmup < 3:
         print("note: at least 3 warm-up steps are required for a valid number; using 3", file=sys.stderr)

@@ -26,7 +26,7 @@
 extern "C" {
 #endif
 
-#define ORDA_ABI_VERSION 1
+#define ORDA_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define ORDA_API __attribute__((visibility("default")))
@@ -141,6 +141,24 @@ typedef struct OrdaOutput {
   OrdaMatOut grad_teacher_weight; /* data == NULL: None */
   OrdaChunkPlan chunk_plan;
 } OrdaOutput;
+
+/* ---------------------------------------------------------------------------
+ * Layout of this header's structs as compiled into the library
+ * ------------------------------------------------------------------------- */
+
+/* One entry per struct (field = "", offset 0, size = sizeof the struct)
+ * followed by one per field (offsetof, sizeof), in declaration order. */
+typedef struct OrdaFieldLayout {
+  const char* struct_name;
+  const char* field;
+  size_t offset;
+  size_t size;
+} OrdaFieldLayout;
+/* Points *out at the library's static table and returns its length. The
+ * bindings in other languages (the Rust #[repr(C)] mirrors that replace the
+ * reference crate's src/cuda/launch.rs, Python ctypes) are checked against
+ * it; no counterpart in the reference. */
+ORDA_API size_t orda_abi_layout(const OrdaFieldLayout** out);
 
 /* ---------------------------------------------------------------------------
  * Configuration helpers (pure host logic, no device needed)
@@ -308,6 +326,13 @@ typedef struct OrdaShardOptions {
                                   reduce-scatter with the GEMM; out->grad_weight is not written and may
                                   be NULL; implies skip_quantize. Finish with orda_reduce_slots_device
                                   after a cross-rank barrier. */
+  int32_t int8_wire;         /* with scatter_grad_weight: send each owner its rows of this rank's partial
+                                as row-wise INT8 codes + one fp32 scale per row (the quantize_rowwise_int8
+                                rules of src/quant.rs:97-117) instead of fp32: 4x fewer bytes over NVLink,
+                                but the reduced grad_W carries the quantisation error of every partial
+                                (not bit-identical to one device; see orda_reduce_slots_device). The
+                                partial is first written to a context buffer of V x H fp32. */
+  int32_t reserved;          /* 0 */
 } OrdaShardOptions;
 
 /* The timed path. Enqueues everything on `stream` (a cudaStream_t; NULL =
@@ -350,9 +375,9 @@ typedef struct OrdaVocabShard {
   int32_t world;        /* ranks whose tuples phase 2 merges */
   int32_t include_rows; /* phase 2: 1 on exactly one rank */
   int32_t scatter_grad_hidden; /* phase 2: 1 = the dgrad GEMMs write this rank's grad_hidden partial of
-                                  every owner's rows (owner r: rows [r*BT/world, (r+1)*BT/world))
+                                  every owner's rows (owner slices as orda_context_slots_create)
                                   straight into the owners' slot buffers (orda_context_slots_create
-                                  with slice_rows = BT/world, h = H, copies = 2 when teacher hidden
+                                  with total_rows = BT, h = H, copies = 2 when teacher hidden
                                   gradients exist, set 0 student, set 1 teacher); the grad_*_hidden
                                   outputs are then not written. After a barrier across the ranks,
                                   orda_reduce_slot_set_device gives each rank its reduced rows
@@ -377,8 +402,11 @@ ORDA_API int orda_vocab_backward_device(OrdaContext* ctx, const OrdaDeviceMat* s
  * split the rows across GPUs it replaces a separate NCCL reduce-scatter of
  * the fp32 grad_W.
  *   1. orda_context_slots_create: rank `rank` of `world` allocates its slot
- *      buffer, `copies` sets of fp32 [world][slice_rows][h] (here one set,
- *      slice_rows = V / world), and gets its CUDA IPC handle;
+ *      buffer for `total_rows` rows split over the owners (rank o owns rows
+ *      [o*slice, min((o+1)*slice, total_rows)) with slice = ceil(total_rows /
+ *      world) rounded up to 8; the last owner may hold fewer), `copies` sets
+ *      of fp32 [world][slice][h] (here one set, total_rows = V), and gets its
+ *      CUDA IPC handle;
  *   2. the caller all-gathers the handles; orda_context_slots_attach maps the
  *      other ranks' buffers (handles indexed by rank);
  *   3. orda_distillation_loss_device with shard->scatter_grad_weight = 1: the
@@ -386,24 +414,28 @@ ORDA_API int orda_vocab_backward_device(OrdaContext* ctx, const OrdaDeviceMat* s
  *      (o+1)*slice) into rank o's buffer, partial index = this rank;
  *   4. after a barrier across the ranks (e.g. an NCCL all-reduce of one value
  *      on the same stream), orda_reduce_slots_device sums the `world` partials
- *      of this rank's rows in rank order into grad_w_slice [slice_rows, h] and,
- *      if quantize, applies the INT8 round trip of orda_quantize_grad_w_device
- *      with the labels of all ranks (target rows are labels in this rank's
- *      row range; stochastic draws are indexed by the global row).
+ *      of this rank's rows in rank order into grad_w_slice [rows of this rank,
+ *      h] and, if quantize, applies the INT8 round trip of
+ *      orda_quantize_grad_w_device with the labels of all ranks (target rows
+ *      are labels in this rank's row range; stochastic draws are indexed by
+ *      the global row). int8_wire must match the scatter calls'
+ *      OrdaShardOptions.int8_wire: the partials are then dequantised (q * s)
+ *      before the sum; against fp32 partials the reduced rows differ by the
+ *      partials' quantisation error (relative L2 about 1e-2).
  * The buffers are released by orda_context_destroy or the next create. */
 typedef struct OrdaIpcHandle {
   char bytes[64];
 } OrdaIpcHandle;
-ORDA_API int orda_context_slots_create(OrdaContext* ctx, int world, int rank, size_t slice_rows, size_t h,
+ORDA_API int orda_context_slots_create(OrdaContext* ctx, int world, int rank, size_t total_rows, size_t h,
                                        int copies, OrdaIpcHandle* handle_out, char* err, size_t err_len);
 ORDA_API int orda_context_slots_attach(OrdaContext* ctx, const OrdaIpcHandle* handles, char* err, size_t err_len);
 ORDA_API int orda_reduce_slots_device(OrdaContext* ctx, float* grad_w_slice, size_t ld, const int64_t* labels,
                                       size_t n_labels, int64_t ignore_index, int quantize, int stochastic,
-                                      uint64_t seed, int8_t* q, float* scale, void* stream, char* err,
-                                      size_t err_len);
+                                      uint64_t seed, int8_t* q, float* scale, int int8_wire, void* stream,
+                                      char* err, size_t err_len);
 /* Sum, in rank order, of the `world` partials in this rank's slot set
- * `copy` into out [slice_rows, h] (ld >= h), with no quantisation: the
- * reduce-scatter of grad_hidden of vocabulary-sharded calls. */
+ * `copy` into out [rows of this rank, h] (ld >= h), with no quantisation:
+ * the reduce-scatter of grad_hidden of vocabulary-sharded calls. */
 ORDA_API int orda_reduce_slot_set_device(OrdaContext* ctx, int copy, float* out, size_t ld, void* stream, char* err,
                                          size_t err_len);
 

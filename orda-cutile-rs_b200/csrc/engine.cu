@@ -78,7 +78,12 @@ struct OrdaContext {
   int slot_rank = -1;
   long long slot_slice = 0;
   long long slot_h = 0;
+  long long slot_total = 0;  // rows over all owners (owner o: [o*slice, min((o+1)*slice, total)))
   int slot_copies = 1;  // independent [world][slice][h] sets in one buffer
+  // INT8 wire format: this rank's local fp32 grad_W partial before it is
+  // quantised into the owners' slots
+  float* wire_local = nullptr;
+  size_t wire_local_bytes = 0;
   float* slot_peer[orda::kMaxSlotRanks] = {};  // rank -> its slot buffer (IPC mapping for other ranks)
   bool slots_attached = false;
   // Persisting-L2 limit set by orda_context_set_l2_persisting, and the
@@ -301,6 +306,26 @@ float* slot_set(const OrdaContext* ctx, int r, int copy) {
   return ctx->slot_peer[r] + static_cast<long long>(copy) * ctx->slot_world * ctx->slot_slice * ctx->slot_h;
 }
 
+// The slot buffers read in the INT8 wire format: codes int8 [world][slice][h],
+// then scales f32 [world][slice] at the next 256-byte boundary (the fp32
+// buffer holds 4 bytes per element, so both fit for h >= 2).
+WireSlots wire_slots(const OrdaContext* ctx) {
+  WireSlots w;
+  const size_t codes = static_cast<size_t>(ctx->slot_world) * ctx->slot_slice * ctx->slot_h;
+  for (int r = 0; r < ctx->slot_world; ++r) {
+    uint8_t* b = reinterpret_cast<uint8_t*>(ctx->slot_peer[r]);
+    w.codes[r] = reinterpret_cast<int8_t*>(b);
+    w.scales[r] = reinterpret_cast<float*>(b + round_up(codes, 256));
+  }
+  return w;
+}
+
+// Rows of this rank's slice (the last owner may hold fewer than slot_slice).
+long long slot_rows_mine(const OrdaContext* ctx) {
+  const long long r0 = static_cast<long long>(ctx->slot_rank) * ctx->slot_slice;
+  return std::max(0ll, std::min(ctx->slot_slice, ctx->slot_total - r0));
+}
+
 int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, const OrdaDeviceOutputs& out,
                const OrdaShardOptions* shard, cudaStream_t st, OrdaChunkPlan* plan_out, char* err, size_t len,
                const VocabCall* vc = nullptr, const HostPipe* hp = nullptr) {
@@ -329,10 +354,10 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
   const bool scatter_hidden = vphase == 2 && vc->scatter_hidden;
   if (scatter_hidden) {
     const long long need = f.teacher_grad ? 2 : 1;
-    if (!ctx->slots_attached || ctx->slot_slice * ctx->slot_world != static_cast<long long>(in.bt) ||
+    if (!ctx->slots_attached || ctx->slot_total != static_cast<long long>(in.bt) ||
         ctx->slot_h != static_cast<long long>(in.h) || ctx->slot_copies < need ||
         (f.teacher_grad && in.ht_dim != in.h)) {
-      set_error(err, len, "scatter_grad_hidden needs slot buffers of BT/world rows x H with %lld set(s) "
+      set_error(err, len, "scatter_grad_hidden needs slot buffers made for BT rows x H with %lld set(s) "
                           "(orda_context_slots_create / _attach) and H_t == H", need);
       return ORDA_ERR_INVALID;
     }
@@ -357,11 +382,26 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
       set_error(err, len, "scatter_grad_weight needs slot buffers (orda_context_slots_create / _attach)");
       return ORDA_ERR_INVALID;
     }
-    if (static_cast<long long>(in.v) != ctx->slot_slice * ctx->slot_world ||
-        static_cast<long long>(in.h) != ctx->slot_h) {
+    if (static_cast<long long>(in.v) != ctx->slot_total || static_cast<long long>(in.h) != ctx->slot_h) {
       set_error(err, len, "slot buffers were made for V=%lld, H=%lld; this call has V=%zu, H=%zu",
-                ctx->slot_slice * ctx->slot_world, ctx->slot_h, in.v, in.h);
+                ctx->slot_total, ctx->slot_h, in.v, in.h);
       return ORDA_ERR_INVALID;
+    }
+  }
+  const bool wire = scatter && shard->int8_wire;
+  if (wire) {
+    // the local fp32 partial, quantised into the owners' slots after wgrad
+    const size_t need = in.v * in.h * sizeof(float);
+    if (ctx->wire_local_bytes < need) {
+      cudaFree(ctx->wire_local);
+      ctx->wire_local = nullptr;
+      ctx->wire_local_bytes = 0;
+      if (cudaMalloc(&ctx->wire_local, need) != cudaSuccess) {
+        cudaGetLastError();
+        set_error(err, len, "INT8 wire: %zu bytes for the local grad_W partial are not available", need);
+        return ORDA_ERR_OOM;
+      }
+      ctx->wire_local_bytes = need;
     }
   }
   if (vphase != 1 && !scatter_hidden && f.teacher_grad && !out.grad_teacher_hidden) {
@@ -669,7 +709,12 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
       gd.N = static_cast<long long>(h);
       gd.raster_n_fastest = true;
       gd.status = status;
-      if (scatter) {
+      if (wire) {
+        // INT8 wire: the local fp32 partial first (quantised into the owners'
+        // slots once complete)
+        gd.args.out0 = ctx->wire_local;
+        gd.args.ld0 = static_cast<long long>(h);
+      } else if (scatter) {
         // each owner's rows go straight to its slot buffer: the reduce-scatter
         // transfer overlaps this GEMM
         gd.args.scatter = 1;
@@ -713,6 +758,14 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
         return cuda_fail(e, why ? why : "teacher wgrad GEMM", err, len);
       ph.launched(nl);
     }
+  }
+  if (wire) {
+    // row-wise INT8 partials (and scales) into the owners' slots
+    Phase ph(ctx, 3, st);
+    ph.launched();
+    launch_quant_send(ctx->wire_local, static_cast<long long>(v), static_cast<long long>(h),
+                      static_cast<long long>(h), ctx->slot_slice, ctx->slot_rank, ctx->slot_world,
+                      wire_slots(ctx), st);
   }
   if (vphase == 1) {
     if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(e, "vocabulary forward phase", err, len);
@@ -876,17 +929,26 @@ static void release_slots(OrdaContext* ctx) {
   ctx->slot_rank = -1;
   ctx->slot_slice = 0;
   ctx->slot_h = 0;
+  ctx->slot_total = 0;
   ctx->slot_copies = 1;
   ctx->slots_attached = false;
 }
 
-int orda_context_slots_create(OrdaContext* ctx, int world, int rank, size_t slice_rows, size_t h, int copies,
+int orda_context_slots_create(OrdaContext* ctx, int world, int rank, size_t total_rows, size_t h, int copies,
                               OrdaIpcHandle* handle_out, char* err, size_t err_len) {
   if (!ctx || !handle_out || world < 1 || world > orda::kMaxSlotRanks || rank < 0 || rank >= world ||
-      slice_rows == 0 || h == 0 || copies < 1 || copies > 4) {
+      total_rows == 0 || h < 2 || copies < 1 || copies > 4) {
     set_error(err, err_len,
-              "invalid argument (world in [1, %d], rank in [0, world), slice_rows and h > 0, copies in [1, 4])",
+              "invalid argument (world in [1, %d], rank in [0, world), total_rows > 0, h >= 2, copies in [1, 4])",
               orda::kMaxSlotRanks);
+    return ORDA_ERR_INVALID;
+  }
+  // owner slices: ceil(total / world) rounded up to 8 rows; the last owner
+  // holds the remainder
+  const size_t slice_rows = round_up(ceil_div(total_rows, static_cast<size_t>(world)), 8);
+  if (static_cast<size_t>(world - 1) * slice_rows >= total_rows) {
+    set_error(err, err_len, "%zu rows leave rank %d of %d no rows in slices of %zu", total_rows, world - 1, world,
+              slice_rows);
     return ORDA_ERR_INVALID;
   }
   std::lock_guard<std::mutex> lock(ctx->mu);
@@ -914,6 +976,7 @@ int orda_context_slots_create(OrdaContext* ctx, int world, int rank, size_t slic
   ctx->slot_rank = rank;
   ctx->slot_slice = static_cast<long long>(slice_rows);
   ctx->slot_h = static_cast<long long>(h);
+  ctx->slot_total = static_cast<long long>(total_rows);
   ctx->slot_copies = copies;
   return ORDA_OK;
 }
@@ -951,7 +1014,7 @@ int orda_context_slots_attach(OrdaContext* ctx, const OrdaIpcHandle* handles, ch
 
 int orda_reduce_slots_device(OrdaContext* ctx, float* grad_w_slice, size_t ld, const int64_t* labels, size_t n_labels,
                              int64_t ignore_index, int quantize, int stochastic, uint64_t seed, int8_t* q, float* scale,
-                             void* stream, char* err, size_t err_len) {
+                             int int8_wire, void* stream, char* err, size_t err_len) {
   if (!ctx || !grad_w_slice || (n_labels > 0 && !labels) || !ctx->slots ||
       ld < static_cast<size_t>(ctx->slot_h)) {
     set_error(err, err_len, "invalid argument (slot buffer, output slice and its ld >= H)");
@@ -960,31 +1023,48 @@ int orda_reduce_slots_device(OrdaContext* ctx, float* grad_w_slice, size_t ld, c
   std::lock_guard<std::mutex> lock(ctx->mu);
   cudaSetDevice(ctx->device);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const long long slice = ctx->slot_slice, h = ctx->slot_h;
-  if (!quantize) {
-    orda::launch_slot_reduce(ctx->slots, ctx->slot_world, slice, h, grad_w_slice, static_cast<long long>(ld), st);
-    ctx->launches += 1;
-  } else {
+  const long long slice = ctx->slot_slice, h = ctx->slot_h, rows = slot_rows_mine(ctx);
+  const long long row0 = static_cast<long long>(ctx->slot_rank) * slice;
+  uint8_t* flags = nullptr;
+  if (quantize) {
     ctx->vocab_ready = false;  // the flags below overwrite the workspace
     if (ensure_ws(ctx, round_up(static_cast<size_t>(slice), 256)) != cudaSuccess) {
       set_error(err, err_len, "device workspace allocation failed");
       return ORDA_ERR_OOM;
     }
-    uint8_t* flags = static_cast<uint8_t*>(ctx->ws);
+    flags = static_cast<uint8_t*>(ctx->ws);
     cudaError_t e = cudaMemsetAsync(flags, 0, static_cast<size_t>(slice), st);
     if (e != cudaSuccess) return cuda_fail(e, "memset", err, err_len);
-    const long long row0 = static_cast<long long>(ctx->slot_rank) * slice;
-    orda::launch_target_flags(labels, static_cast<long long>(n_labels), slice, ignore_index, flags, st, row0);
-    // one pass: rank-ordered sum and INT8 round trip of each row
-    if (orda::launch_slot_reduce_quant(ctx->slots, ctx->slot_world, slice, h, grad_w_slice,
-                                       static_cast<long long>(ld), flags, stochastic, seed, q, scale, row0, st)) {
-      ctx->launches += 2;
-    } else {
-      orda::launch_slot_reduce(ctx->slots, ctx->slot_world, slice, h, grad_w_slice, static_cast<long long>(ld), st);
-      orda::launch_quant(grad_w_slice, slice, h, static_cast<long long>(ld), flags, stochastic, seed, q, scale, st,
-                         row0);
-      ctx->launches += 3;
+    orda::launch_target_flags(labels, static_cast<long long>(n_labels), rows, ignore_index, flags, st, row0);
+    ctx->launches += 1;
+  }
+  if (int8_wire) {
+    // dequantise the INT8 partials, sum them in rank order (and quantise)
+    WireSlots mine;
+    const WireSlots all = wire_slots(ctx);
+    mine.codes[0] = all.codes[ctx->slot_rank];
+    mine.scales[0] = all.scales[ctx->slot_rank];
+    if (!orda::launch_wire_reduce(mine, ctx->slot_world, slice, rows, h, grad_w_slice, static_cast<long long>(ld),
+                                  flags, quantize, stochastic, seed, q, scale, row0, st)) {
+      set_error(err, err_len, "INT8 wire: rows of H=%lld do not fit the reduction's shared memory", h);
+      return ORDA_ERR_INVALID;
     }
+    ctx->launches += 1;
+  } else if (!quantize) {
+    orda::launch_slot_reduce(ctx->slots, ctx->slot_world, slice, rows, h, grad_w_slice, static_cast<long long>(ld),
+                             st);
+    ctx->launches += 1;
+  } else if (orda::launch_slot_reduce_quant(ctx->slots, ctx->slot_world, slice, rows, h, grad_w_slice,
+                                            static_cast<long long>(ld), flags, stochastic, seed, q, scale, row0,
+                                            st)) {
+    // one pass: rank-ordered sum and INT8 round trip of each row
+    ctx->launches += 1;
+  } else {
+    orda::launch_slot_reduce(ctx->slots, ctx->slot_world, slice, rows, h, grad_w_slice, static_cast<long long>(ld),
+                             st);
+    orda::launch_quant(grad_w_slice, rows, h, static_cast<long long>(ld), flags, stochastic, seed, q, scale, st,
+                       row0);
+    ctx->launches += 2;
   }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "slot reduction", err, err_len);
@@ -1002,7 +1082,8 @@ int orda_reduce_slot_set_device(OrdaContext* ctx, int copy, float* out, size_t l
   cudaSetDevice(ctx->device);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   orda::launch_slot_reduce(ctx->slots + static_cast<long long>(copy) * ctx->slot_world * ctx->slot_slice * ctx->slot_h,
-                           ctx->slot_world, ctx->slot_slice, ctx->slot_h, out, static_cast<long long>(ld), st);
+                           ctx->slot_world, ctx->slot_slice, slot_rows_mine(ctx), ctx->slot_h, out,
+                           static_cast<long long>(ld), st);
   ctx->launches += 1;
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "slot reduction", err, err_len);
@@ -1046,6 +1127,7 @@ void orda_context_destroy(OrdaContext* ctx) {
   release_slots(ctx);
   cudaFree(ctx->ws);
   cudaFree(ctx->stage);
+  cudaFree(ctx->wire_local);
   cudaFree(ctx->d_words);
   cudaFree(ctx->d_mean_scale);
   for (cudaStream_t sp : {ctx->own_stream, ctx->copy_in, ctx->copy_out})

@@ -171,14 +171,35 @@ void launch_target_flags(const int64_t* labels, long long bt, long long v, int64
 // stays in shared memory). Returns false, launching nothing, when the row
 // does not fit (h % 4 != 0 or h > 12288); the caller then uses the two
 // kernels.
-bool launch_slot_reduce_quant(const float* slots, int world, long long slice, long long h, float* out, long long ld,
-                              const uint8_t* target_flags, int stochastic, uint64_t seed, int8_t* q, float* scale,
-                              long long row_offset, cudaStream_t stream);
+bool launch_slot_reduce_quant(const float* slots, int world, long long slice, long long rows, long long h, float* out,
+                              long long ld, const uint8_t* target_flags, int stochastic, uint64_t seed, int8_t* q,
+                              float* scale, long long row_offset, cudaStream_t stream);
 
 // out[r, :] = sum over k = 0..world-1 (in that order) of
-// slots[(k * slice + r) * h + :], for r < slice (fp32).
-void launch_slot_reduce(const float* slots, int world, long long slice, long long h, float* out, long long ld,
-                        cudaStream_t stream);
+// slots[(k * slice + r) * h + :], for r < rows <= slice (fp32).
+void launch_slot_reduce(const float* slots, int world, long long slice, long long rows, long long h, float* out,
+                        long long ld, cudaStream_t stream);
+
+// INT8 wire format of the row-sharded grad_W exchange. Each owner's slot
+// buffer, read as codes int8 [world][slice][h] followed (at a 256-byte
+// boundary) by scales f32 [world][slice]; codes[o] / scales[o] address owner
+// o's buffer (this rank's own, or a peer mapping).
+struct WireSlots {
+  int8_t* codes[kMaxSlotRanks] = {};
+  float* scales[kMaxSlotRanks] = {};
+};
+// Quantises each row of this rank's local fp32 grad_W partial (v rows,
+// row-wise INT8 by the quant.rs rules) into its owner's codes / scales at
+// partial index slot_rank.
+void launch_quant_send(const float* grad_w, long long v, long long h, long long ld, long long slice, int slot_rank,
+                       int world, const WireSlots& dst, cudaStream_t stream);
+// Owner side: out[r] = sum over k (rank order) of codes[k][r] * scales[k][r]
+// (fp32), r < rows, then (quantize) the INT8 round trip of quant_kernel in
+// the same pass. mine.codes[0] / mine.scales[0] are this rank's buffer.
+// Returns false when h > 12288 (the row does not fit shared memory).
+bool launch_wire_reduce(const WireSlots& mine, int world, long long slice, long long rows, long long h, float* out,
+                        long long ld, const uint8_t* target_flags, int quantize, int stochastic, uint64_t seed,
+                        int8_t* q, float* scale, long long row_offset, cudaStream_t stream);
 
 // One-warp kernel whose bounded wait on a never-completed mbarrier expires
 // after limit_ns and records DEV_TIMEOUT_SELFTEST in *status.

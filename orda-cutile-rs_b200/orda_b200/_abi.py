@@ -125,9 +125,13 @@ class OrdaDeviceOutputs(C.Structure):
     ]
 
 
+class OrdaFieldLayout(C.Structure):
+    _fields_ = [("struct_name", C.c_char_p), ("field", C.c_char_p), ("offset", C.c_size_t), ("size", C.c_size_t)]
+
+
 class OrdaShardOptions(C.Structure):
     _fields_ = [("global_non_ignore", C.c_int64), ("skip_quantize", C.c_int32),
-                ("scatter_grad_weight", C.c_int32)]
+                ("scatter_grad_weight", C.c_int32), ("int8_wire", C.c_int32), ("reserved", C.c_int32)]
 
 
 VOCAB_TUPLE = 12  # ORDA_VOCAB_TUPLE
@@ -198,6 +202,7 @@ SIGNATURES = {
     ),
     "orda_output_free": (None, [C.POINTER(OrdaOutput)]),
     "orda_set_host_slab_bytes": (None, [C.c_size_t]),
+    "orda_abi_layout": (C.c_size_t, [C.POINTER(C.POINTER(OrdaFieldLayout))]),
     "orda_context_create": (C.c_int, [C.c_int, C.POINTER(C.c_void_p), C.c_char_p, C.c_size_t]),
     "orda_context_destroy": (None, [C.c_void_p]),
     "orda_context_check": (C.c_int, [C.c_void_p, C.c_char_p, C.c_size_t]),
@@ -225,7 +230,7 @@ SIGNATURES = {
     "orda_context_slots_attach": (C.c_int, [C.c_void_p, C.POINTER(OrdaIpcHandle), C.c_char_p, C.c_size_t]),
     "orda_reduce_slots_device": (
         C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p, C.c_size_t, C.c_int64, C.c_int, C.c_int,
-                  C.c_uint64, C.c_void_p, C.c_void_p, C.c_void_p, C.c_char_p, C.c_size_t]),
+                  C.c_uint64, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_char_p, C.c_size_t]),
     "orda_context_set_l2_persisting": (C.c_int, [C.c_void_p, C.c_size_t, C.POINTER(C.c_size_t), C.c_char_p,
                                                  C.c_size_t]),
     "orda_context_selftest_bounded_wait": (C.c_int, [C.c_void_p, C.c_uint32, C.c_void_p, C.c_char_p, C.c_size_t]),

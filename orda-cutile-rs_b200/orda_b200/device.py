@@ -59,13 +59,14 @@ class DeviceContext:
     def launch_count(self) -> int:
         return int(_lib().orda_context_launch_count(self.handle))
 
-    def slots_create(self, world: int, rank: int, slice_rows: int, h: int, copies: int = 1) -> bytes:
-        """`orda_context_slots_create`: allocates this rank's slot buffer
-        (`copies` sets of [world][slice_rows][h] fp32) for the fused
-        reduce-scatters; returns its 64-byte IPC handle."""
+    def slots_create(self, world: int, rank: int, total_rows: int, h: int, copies: int = 1) -> bytes:
+        """`orda_context_slots_create`: allocates this rank's slot buffer for
+        `total_rows` rows split over the owners (shard.owner_rows; `copies`
+        sets of [world][slice][h] fp32) for the fused reduce-scatters;
+        returns its 64-byte IPC handle."""
         hd = _abi.OrdaIpcHandle()
         buf = _abi.err_buf()
-        _check(_lib().orda_context_slots_create(self.handle, world, rank, slice_rows, h, copies, C.byref(hd), buf,
+        _check(_lib().orda_context_slots_create(self.handle, world, rank, total_rows, h, copies, C.byref(hd), buf,
                                                 len(buf)), buf)
         return C.string_at(C.addressof(hd), C.sizeof(hd))
 
@@ -82,14 +83,16 @@ class DeviceContext:
 
     def reduce_slots(self, grad_w_slice: torch.Tensor, labels: torch.Tensor, ignore_index: int = -100,
                      quantize: bool = False, stochastic: bool = False, seed: int = 0,
-                     q: Optional[torch.Tensor] = None, scale: Optional[torch.Tensor] = None, stream=None) -> None:
+                     q: Optional[torch.Tensor] = None, scale: Optional[torch.Tensor] = None, stream=None,
+                     int8_wire: bool = False) -> None:
         """`orda_reduce_slots_device`: this rank's grad_W rows, summed over
-        the ranks' partials (and INT8 round trip when quantize)."""
+        the ranks' partials (and INT8 round trip when quantize); int8_wire
+        when the partials were sent in the INT8 wire format."""
         buf = _abi.err_buf()
         _check(_lib().orda_reduce_slots_device(
             self.handle, grad_w_slice.data_ptr(), grad_w_slice.stride(0), labels.data_ptr(), labels.numel(),
-            ignore_index, int(quantize), int(stochastic), seed, _ptr(q), _ptr(scale), _stream(stream), buf,
-            len(buf)), buf)
+            ignore_index, int(quantize), int(stochastic), seed, _ptr(q), _ptr(scale), int(int8_wire),
+            _stream(stream), buf, len(buf)), buf)
 
     def reduce_slot_set(self, copy: int, out: torch.Tensor, stream=None) -> None:
         """`orda_reduce_slot_set_device`: rank-ordered sum of slot set `copy`."""
@@ -235,10 +238,12 @@ def distillation_loss_device(
     want_int8: bool = False,
     stream=None,
     scatter_grad_weight: bool = False,
+    int8_wire: bool = False,
 ) -> DeviceLossResult:
     """`orda_distillation_loss_device`: bf16 device inputs, fp32 device grads.
     With scatter_grad_weight the grad_W partial goes to the slot buffers
-    (see DeviceContext.slots_create) and the returned grad_weight is None."""
+    (see DeviceContext.slots_create) and the returned grad_weight is None;
+    int8_wire sends it there as row-wise INT8 codes and scales."""
     opts = opts or LossOptions()
     bt, h = student_hidden.shape
     v = weight.shape[0]
@@ -246,7 +251,8 @@ def distillation_loss_device(
     o, tensors = _outputs(opts, teacher_mode, bt, h, v, ht, student_hidden.device, out, want_int8,
                           with_grad_weight=not scatter_grad_weight)
     t = _teacher_struct(teacher_mode, teacher_hidden, teacher_weight, teacher_logits)
-    shard = _abi.OrdaShardOptions(int(global_non_ignore), int(skip_quantize), int(scatter_grad_weight))
+    shard = _abi.OrdaShardOptions(int(global_non_ignore), int(skip_quantize), int(scatter_grad_weight),
+                                  int(int8_wire), 0)
     plan = _abi.OrdaChunkPlan()
     buf = _abi.err_buf()
     rc = _lib().orda_distillation_loss_device(

@@ -4,8 +4,8 @@ Each rank owns a contiguous block of the BT rows and a replica of W. Ranks
 compute their rows' loss terms and gradients with the global mean
 denominator (the token count of all ranks), so the per-rank scalar sums and
 grad_W partials add up to the single-GPU result. The only cross-rank traffic
-is one reduction of grad_W (reduce-scatter: rank r keeps vocabulary rows
-[r*V/N, (r+1)*V/N)), a 4-float all-reduce of the loss scalars and, for the
+is one reduction of grad_W (reduce-scatter: rank r keeps the vocabulary rows
+owner_rows(V, N, r)), a 4-float all-reduce of the loss scalars and, for the
 INT8 round trip, an all-gather of the labels so every rank knows the target
 rows of its vocabulary slice. grad_hidden stays local.
 
@@ -52,12 +52,23 @@ def shard_rows(bt_total: int, world: int, rank: int) -> tuple[int, int]:
     return start, start + base + (1 if rank < extra else 0)
 
 
+def owner_rows(total: int, world: int, rank: int, align: int = 8) -> tuple[int, int]:
+    """Rows [r0, r1) of `total` owned by `rank`: slices of ceil(total / world)
+    rows rounded up to `align` (so a bf16 or fp32 row block stays 16-byte
+    aligned), the last owner taking the remainder. The slot buffers of the
+    library (orda_context_slots_create) use the same rule."""
+    n = -(-total // world)
+    n = -(-n // align) * align
+    r0 = min(rank * n, total)
+    r1 = min(r0 + n, total)
+    if r1 <= r0:
+        raise ValueError(f"{total} rows leave rank {rank} of {world} no rows in slices of {n}")
+    return r0, r1
+
+
 def vocab_slice(v: int, world: int, rank: int) -> tuple[int, int]:
     """Vocabulary rows of grad_W owned by `rank` after the reduce-scatter."""
-    if v % world:
-        raise ValueError(f"V={v} must be divisible by the world size {world} for the reduce-scatter")
-    n = v // world
-    return rank * n, (rank + 1) * n
+    return owner_rows(v, world, rank)
 
 
 def gather_labels(labels_local: torch.Tensor, ignore_index: int, capacity: Optional[int] = None,
@@ -95,11 +106,12 @@ class ShardResult:
 
 
 def reduce_grad_weight(grad_w: torch.Tensor, group=None) -> torch.Tensor:
-    """Sum of grad_W over ranks, returning this rank's vocabulary slice."""
+    """Sum of grad_W over ranks, returning this rank's vocabulary slice
+    (NCCL reduce-scatter when the slices are equal, else an all-reduce)."""
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
     v0, v1 = vocab_slice(grad_w.shape[0], world, rank)
-    if dist.get_backend(group) == "nccl":
+    if dist.get_backend(group) == "nccl" and (v1 - v0) * world == grad_w.shape[0]:
         out = torch.empty(v1 - v0, grad_w.shape[1], dtype=grad_w.dtype, device=grad_w.device)
         dist.reduce_scatter_tensor(out, grad_w, group=group)
         return out
@@ -140,26 +152,31 @@ def row_sharded_step(
 class SlotReduceScatter:
     """The fused grad_W reduce-scatter over the GPUs of one node.
 
-    Every rank allocates a slot buffer fp32 [world][V/world][H] for the grad_W
-    rows it owns and maps the other ranks' buffers (CUDA IPC handles
-    exchanged with an all-gather). The device entry then runs with
-    scatter_grad_weight: its wgrad GEMM stores this rank's partial of every
-    owner's rows straight into that owner's buffer while the GEMM runs, so no
-    separate reduce-scatter pass over grad_W is left. After a barrier the
-    owner sums the partials in rank order (deterministic) and applies the
-    INT8 round trip in the same pass.
+    Every rank allocates a slot buffer fp32 [world][slice][H] for the grad_W
+    rows it owns (owner_rows: V need not divide by the world size) and maps
+    the other ranks' buffers (CUDA IPC handles exchanged with an all-gather).
+    The device entry then runs with scatter_grad_weight: its wgrad GEMM
+    stores this rank's partial of every owner's rows straight into that
+    owner's buffer while the GEMM runs, so no separate reduce-scatter pass
+    over grad_W is left. After a barrier the owner sums the partials in rank
+    order (deterministic) and applies the INT8 round trip in the same pass.
+
+    int8_wire (opt-in, lossy): the partials travel as row-wise INT8 codes and
+    scales (4x fewer bytes); the device calls must pass int8_wire=True too.
     """
 
-    def __init__(self, ctx, v: int, h: int, group=None, label_capacity: Optional[int] = None):
+    def __init__(self, ctx, v: int, h: int, group=None, label_capacity: Optional[int] = None,
+                 int8_wire: bool = False):
         """label_capacity: the most rows any rank holds in a step, when ranks
         hold different row counts (labels are gathered padded to it)."""
         self.ctx = ctx
         self.group = group
         self.label_capacity = label_capacity
+        self.int8_wire = int8_wire
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         self.v0, self.v1 = vocab_slice(v, self.world, self.rank)
-        handle = ctx.slots_create(self.world, self.rank, self.v1 - self.v0, h, 1)
+        handle = ctx.slots_create(self.world, self.rank, v, h, 1)
         handles = [None] * self.world
         dist.all_gather_object(handles, handle, group=group)
         ctx.slots_attach(handles)
@@ -183,7 +200,7 @@ class SlotReduceScatter:
         marks: Optional[list] = None,
     ) -> ShardResult:
         """compute(n_global) -> (scalars[4], grad_student_hidden) runs the
-        local rows with scatter_grad_weight; grad_weight_slice [V/world, H]
+        local rows with scatter_grad_weight; grad_weight_slice [v1 - v0, H]
         receives this rank's reduced (and, with quantize, dequantised) rows.
         marks (optional): two CUDA events, recorded after the barrier and
         after the reduction, for timing. stream: the stream the device calls
@@ -203,7 +220,7 @@ class SlotReduceScatter:
         if marks is not None:
             marks[0].record(stream)
         self.ctx.reduce_slots(grad_weight_slice, labels_all, ignore_index, quantize, stochastic, seed, q, scale,
-                              stream=stream)
+                              stream=stream, int8_wire=self.int8_wire)
         if marks is not None:
             marks[1].record(stream)
         # the slot buffers are read; the next step's GEMMs may write them
@@ -218,18 +235,12 @@ def vocab_slice_bounds(v_total: int, world: int, rank: int, align: int = 8) -> t
     """Vocabulary rows [v0, v1) held by `rank` when V is sharded: near-equal
     contiguous slices whose starts are multiples of `align` (so a bf16 column
     slice of teacher logits stays 16-byte aligned)."""
-    n = -(-v_total // world)
-    n = -(-n // align) * align
-    v0 = min(rank * n, v_total)
-    v1 = min(v0 + n, v_total)
-    if v1 <= v0:
-        raise ValueError(f"V={v_total} leaves rank {rank} of {world} an empty slice")
-    return v0, v1
+    return owner_rows(v_total, world, rank, align)
 
 
 class HiddenSlots:
     """Slot buffers for the vocabulary-sharded grad_hidden reduce-scatter:
-    rank r owns hidden rows [r*BT/world, (r+1)*BT/world); set 0 receives the
+    rank r owns hidden rows owner_rows(BT, world, r); set 0 receives the
     student's partials, set 1 the teacher's (when teacher hidden gradients
     exist). The dgrad GEMMs store each owner's rows into its buffer."""
 
@@ -238,11 +249,9 @@ class HiddenSlots:
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
-        self.r0, self.r1 = shard_rows(bt, self.world, self.rank)
-        if bt % self.world:
-            raise ValueError(f"BT={bt} must be divisible by the world size {self.world}")
+        self.r0, self.r1 = owner_rows(bt, self.world, self.rank)
         self.teacher = teacher
-        handle = ctx.slots_create(self.world, self.rank, bt // self.world, h, 2 if teacher else 1)
+        handle = ctx.slots_create(self.world, self.rank, bt, h, 2 if teacher else 1)
         handles = [None] * self.world
         dist.all_gather_object(handles, handle, group=group)
         ctx.slots_attach(handles)

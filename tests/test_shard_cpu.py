@@ -143,8 +143,15 @@ def test_shard_rows_and_vocab_slices():
     assert [shard.shard_rows(10, 3, r) for r in range(3)] == [(0, 4), (4, 7), (7, 10)]
     assert [shard.shard_rows(8192 * 8, 8, r) for r in (0, 7)] == [(0, 8192), (57344, 65536)]
     assert shard.vocab_slice(131072, 8, 3) == (49152, 65536)
+    # V not divisible by the world size: slices of ceil(V / N) rounded up to
+    # 8 rows, the last owner holds the rest (ceil(50257 / 8) = 6283 -> 6288;
+    # rank 7 holds 50257 - 7 x 6288 = 6241 rows)
+    b = [shard.vocab_slice(50257, 8, r) for r in range(8)]
+    assert b[0] == (0, 6288) and b[7] == (44016, 50257)
+    assert all(b[i][1] == b[i + 1][0] for i in range(7))
+    assert shard.vocab_slice(32001, 2, 1) == (16008, 32001)
     with pytest.raises(ValueError):
-        shard.vocab_slice(152065, 8, 0)
+        shard.owner_rows(17, 8, 7)  # slices of 8: ranks 3.. hold no rows
 
 
 def test_vocab_slice_bounds_cover_the_vocabulary_once():

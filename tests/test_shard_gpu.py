@@ -104,7 +104,8 @@ def _worker(rank, world, port, outdir, mode="nccl"):
             # fused: the wgrad GEMM writes the owners' slot buffers; two steps in a
             # row (the second reuses the buffers), first without the INT8 step to
             # keep the raw reduced slice, then with it
-            fused = shard.SlotReduceScatter(ctx, V, H)
+            wire = mode == "fused_wire"
+            fused = shard.SlotReduceScatter(ctx, V, H, int8_wire=wire)
             # "fused_side": every device call and collective of the steps runs
             # on a stream that is not torch's current one (the step makes it
             # current for its collectives)
@@ -116,7 +117,7 @@ def _worker(rank, world, port, outdir, mode="nccl"):
             def compute_scatter(n):
                 r = distillation_loss_device(ctx, hs_l, w, lab, ob.TeacherMode.Precomputed, teacher_logits=tl_l,
                                              opts=_opts(ob), global_non_ignore=n, scatter_grad_weight=True,
-                                             stream=st)
+                                             stream=st, int8_wire=wire)
                 return r.scalars, r.grad_student_hidden
 
             sl = torch.full((nsl, H), float("nan"), device=hs.device)
@@ -142,7 +143,7 @@ def _worker(rank, world, port, outdir, mode="nccl"):
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("mode", ["nccl", "fused", "fused_side"])
+@pytest.mark.parametrize("mode", ["nccl", "fused", "fused_side", "fused_wire"])
 def test_row_sharded_two_gpus_match_single_gpu(ob, tmp_path, mode):
     import torch.multiprocessing as mp
 
@@ -179,6 +180,15 @@ def test_row_sharded_two_gpus_match_single_gpu(ob, tmp_path, mode):
         r0, r1 = p["rows"]
         assert rel_l2(p["gsh"].numpy(), gsh_ref[r0:r1].numpy()) < 1e-5
         v0, v1 = p["vocab"]
+        if mode == "fused_wire":
+            # INT8 wire format: each partial carries its row-wise quantisation
+            # error (noise RMS about amax / (127 sqrt 12) per row, under 1 % of
+            # the row RMS): the stated tolerance is rel-L2 2e-2 on the reduced
+            # slice, before and after the INT8 round trip
+            e = rel_l2(p["gw"].numpy(), gw_ref[v0:v1].numpy())
+            assert 1e-5 < e < 2e-2, e
+            assert rel_l2(p["gw_dq"].numpy(), gw_ref[v0:v1].numpy()) < 2e-2
+            continue
         assert rel_l2(p["gw"].numpy(), gw_ref[v0:v1].numpy()) < 1e-5
         # INT8 slice: quantise the single-GPU slice the same way and compare codes
         from orda_b200.device import quantize_grad_w
@@ -211,9 +221,10 @@ def test_row_sharded_two_gpus_match_single_gpu(ob, tmp_path, mode):
         assert rel_l2(p["gw_dq"].numpy(), sl.cpu().numpy()) < 1e-3
 
 
-def _tied_worker(rank, world, port, outdir):
+def _tied_worker(rank, world, port, outdir, v=V):
     """Fused flow with a Tied teacher: the wgrad GEMM runs two K segments
-    (student and teacher rows) into the scattered grad_W partials."""
+    (student and teacher rows) into the scattered grad_W partials. v other
+    than V: the first v rows of W, so owners hold uneven slices."""
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     os.environ["NCCL_NVLS_ENABLE"] = "0"
@@ -232,13 +243,15 @@ def _tied_worker(rank, world, port, outdir):
                             device_id=dev)
     try:
         hs, w, _tl, labels = _inputs(dev)
+        w = w[:v]
+        labels = torch.where(labels >= v, labels % v, labels)
         ht = (hs.float() + 0.1).bfloat16()
         r0, r1 = shard.shard_rows(BT, world, rank)
         lab = labels[r0:r1].contiguous()
         n_global = shard.global_non_ignore(lab, -100)
         opts = ob.LossOptions(kd_weight=0.4, temperature=1.5)
         with DeviceContext(rank) as ctx:
-            fused = shard.SlotReduceScatter(ctx, V, H)
+            fused = shard.SlotReduceScatter(ctx, v, H)
 
             def compute(n):
                 r = distillation_loss_device(ctx, hs[r0:r1].contiguous(), w, lab, ob.TeacherMode.Tied,
@@ -247,7 +260,7 @@ def _tied_worker(rank, world, port, outdir):
                 compute.gth = r.grad_teacher_hidden
                 return r.scalars, r.grad_student_hidden
 
-            sl = torch.empty(V // world, H, device=dev)
+            sl = torch.empty(fused.v1 - fused.v0, H, device=dev)
             res = fused.step(compute, lab, -100, n_global, sl)
             torch.cuda.synchronize()
             ctx.check()
@@ -259,7 +272,9 @@ def _tied_worker(rank, world, port, outdir):
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_row_sharded_tied_fused_two_gpus_match_single_gpu(ob, tmp_path):
+@pytest.mark.parametrize("v", [V, V - 8])
+def test_row_sharded_tied_fused_two_gpus_match_single_gpu(ob, tmp_path, v):
+    """v = V - 8: not divisible by 16, owner slices of 4096 and 4088 rows."""
     import torch.multiprocessing as mp
 
     from conftest import rel_l2
@@ -268,7 +283,7 @@ def test_row_sharded_tied_fused_two_gpus_match_single_gpu(ob, tmp_path):
     world = 2
     port = _free_port()
     ctxm = mp.get_context("spawn")
-    procs = [ctxm.Process(target=_tied_worker, args=(r, world, port, str(tmp_path))) for r in range(world)]
+    procs = [ctxm.Process(target=_tied_worker, args=(r, world, port, str(tmp_path), v)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
@@ -281,6 +296,8 @@ def test_row_sharded_tied_fused_two_gpus_match_single_gpu(ob, tmp_path):
 
     dev = torch.device("cuda", 0)
     hs, w, _tl, labels = _inputs(dev)
+    w = w[:v]
+    labels = torch.where(labels >= v, labels % v, labels)
     ht = (hs.float() + 0.1).bfloat16()
     with DeviceContext(0) as ctx:
         ref = distillation_loss_device(ctx, hs, w, labels, ob.TeacherMode.Tied, teacher_hidden=ht,
