@@ -30,6 +30,8 @@ Besides the headline, the line carries:
   c5_vocab   the same configuration vocabulary-sharded (V/N rows of W per
              GPU, every GPU all 8192*N rows, grad_hidden reduce-scattered by
              the dgrad GEMMs); at N=1 the vocabulary phases on one GPU.
+  c4_fast    N=1: the c4 workload under Profile::Fast, with its agreement
+             with the Balanced call.
 Each c5 object has its own timing, roofline and parity.
 `--config c5` runs only c5 (`--shard rows|vocab`).
 `--impl reference` times the reference's CPU path (the oracle restatement,
@@ -689,6 +691,9 @@ def run_ours(args):
         parity.update(checks)
     else:
         line["cpu_baseline"] = None
+    # ---------------- Profile::Fast on the same workload (N=1)
+    if world == 1 and not args.no_fast:
+        line["c4_fast"] = run_c4_fast(torch, ob, D, ctx, hs, w, tl, labels, out, stream, args, raw_gw)
     del raw_gw
     if parity:
         parity["pass"] = all(p.get("pass", True) for p in parity.values() if isinstance(p, dict))
@@ -707,6 +712,56 @@ def run_ours(args):
     if rank == 0:
         print(json.dumps(line), flush=True)
     return 0
+
+
+def run_c4_fast(torch, ob, D, ctx, hs, w, tl, labels, ref_out, stream, args, raw_gw):
+    """Profile::Fast (fp16 logits storage, exact label logits, exp2 split
+    between SFU and FMA pipe) on the c4 workload: timing and roofline as the
+    headline, and its agreement with the Balanced call of the timed steps
+    (scalars, grad_hidden; grad_W before the INT8 round trip). The Fast
+    tolerances against the reference are stated in include/orda.h."""
+    from orda_b200.device import distillation_loss_device
+
+    h, v = CFG["h"], CFG["v"]
+    dev = hs.device
+    opts = ob.LossOptions(kd_weight=CFG["kd"], temperature=CFG["temperature"],
+                          config=ob.KernelConfig(quantize_grad_weight=True, fast_math=True))
+    out_f = {"grad_weight": torch.empty(v, h, device=dev), "grad_student_hidden": torch.empty(hs.shape[0], h, device=dev),
+             "scalars": torch.empty(4, device=dev), "grad_weight_q": torch.empty(v, h, device=dev, dtype=torch.int8),
+             "grad_weight_scale": torch.empty(v, device=dev)}
+
+    def step():
+        return distillation_loss_device(ctx, hs, w, labels, ob.TeacherMode.Precomputed, teacher_logits=tl, opts=opts,
+                                        out=out_f, want_int8=True, stream=stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    ctx.check()
+    ms, phases, clocks, launches, _ = timed(torch, D, stream, step, args.steps, ctx, clocks=not args.no_clocks)
+    ctx.check()
+    flops = algorithmic_flops(hs.shape[0], h, v)
+    res = {"profile": "Fast (KernelConfig.fast_math)", "value": hs.shape[0] / (ms / 1e3), "unit": "tokens/s",
+           "ms_per_step": ms, "steps": args.steps,
+           "phases_ms_per_step": {k: v_[0] / args.steps for k, v_ in phases.items()},
+           "roofline": gemm_roofline(phases, args.steps, flops, "gemm_kernel (tcgen05 cta_group::2, fp16 logits)"),
+           "gpu_launches": int(launches), "clocks": clocks}
+    if raw_gw is not None:
+        r = distillation_loss_device(ctx, hs, w, labels, ob.TeacherMode.Precomputed, teacher_logits=tl, opts=opts,
+                                     skip_quantize=True, stream=stream)
+        torch.cuda.synchronize()
+        res["vs_balanced"] = {
+            "scalars_rel": scalars_rel(out_f["scalars"].cpu().numpy(), ref_out["scalars"].cpu().numpy()),
+            "grad_hidden_rel_l2": rel_l2_dev(torch, out_f["grad_student_hidden"], ref_out["grad_student_hidden"]),
+            "grad_weight_rel_l2": rel_l2_dev(torch, r.grad_weight, raw_gw),
+            "tol": {"scalars_rel": 1e-3, "grad_rel_l2": 2e-2}}
+        vb = res["vs_balanced"]
+        vb["pass"] = (vb["scalars_rel"] <= 1e-3 and vb["grad_hidden_rel_l2"] <= 2e-2
+                      and vb["grad_weight_rel_l2"] <= 2e-2)
+        del r
+    del out_f
+    torch.cuda.empty_cache()
+    return res
 
 
 def c4_row_blocks(torch, ob, ctx, hs, w, tl, labels, opts, dev, stream, keep):
@@ -1222,6 +1277,7 @@ def main():
     ap.add_argument("--no-clocks", action="store_true")
     ap.add_argument("--no-parity", action="store_true")
     ap.add_argument("--no-c5", action="store_true", help="leave out the c5 sub-objects")
+    ap.add_argument("--no-fast", action="store_true", help="leave out the Profile::Fast sub-object (N=1)")
     ap.add_argument("--config", choices=["c4", "c5"], default="c4",
                     help="c4: the metric configuration with c5 sub-objects (default); c5: only c5")
     ap.add_argument("--shard", choices=["rows", "vocab"], default="rows", help="--config c5: partitioning")

@@ -82,7 +82,17 @@ typedef enum OrdaReduction { ORDA_REDUCTION_MEAN = 0, ORDA_REDUCTION_SUM = 1 } O
  * B200 path; Cpu is rejected (the library ships no CPU path). */
 typedef enum OrdaBackend { ORDA_BACKEND_AUTO = 0, ORDA_BACKEND_CPU = 1, ORDA_BACKEND_CUDA = 2 } OrdaBackend;
 
-/* `Profile` (src/config.rs:35-42). */
+/* `Profile` (src/config.rs:35-42). Fast (KernelConfig.fast_math = 1) stores
+ * the logits of the forward group as fp16 (saturated to the largest finite
+ * value) instead of fp32, takes the label logits of the losses from an exact
+ * fp32 dot product, and computes part of the exp2 work on the FMA pipe
+ * (exp2 by range reduction and a degree-6 polynomial). The softmax statistics
+ * still come from the fp32 GEMM accumulators, so the CE terms are as precise
+ * as with Balanced; the KL cross term and the logit gradients read the fp16
+ * logits. Stated tolerances against the reference: student and teacher CE
+ * 1e-4 relative, KL and loss 1e-3 relative, gradients relative L2 2e-2. The
+ * INT8 quantiser keeps IEEE divides in every profile (bit-exactness).
+ * Balanced and Debug keep fp32 logits. */
 typedef enum OrdaProfile { ORDA_PROFILE_BALANCED = 0, ORDA_PROFILE_FAST = 1, ORDA_PROFILE_DEBUG = 2 } OrdaProfile;
 
 /* `KernelConfig` (src/config.rs:46-63). Option<T> fields carry a has_ flag. */
@@ -283,6 +293,13 @@ ORDA_API int orda_context_selftest_bounded_wait(OrdaContext* ctx, uint32_t limit
 /* Test hook for the OOM ladder: the next `count` workspace allocations fail
  * as if cudaMalloc had returned cudaErrorMemoryAllocation. */
 ORDA_API void orda_context_inject_alloc_failures(OrdaContext* ctx, int count);
+/* Accuracy self-test of the two exp2 implementations of the kernels, on the
+ * current device and `stream`: y_fma[i] = 2^x[i] computed on the FMA pipe
+ * (the Fast profile's range-reduced polynomial), y_sfu[i] = the SFU's
+ * ex2.approx. x, y_fma, y_sfu: device arrays of n floats. No counterpart in
+ * the reference. */
+ORDA_API int orda_selftest_exp2(const float* x, float* y_fma, float* y_sfu, size_t n, void* stream, char* err,
+                                size_t err_len);
 
 /* Element type of a device matrix. Hidden states and weights are bf16 (the
  * tensor-core operand type); Precomputed teacher logits may be bf16 or f32. */

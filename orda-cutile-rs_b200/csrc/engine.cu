@@ -117,11 +117,14 @@ struct DevInputs {
 struct Flags {
   float w_s, w_t, kd, temperature, alpha;
   bool need_teacher, teacher_rows, teacher_grad, teacher_ce, quant;
+  // Profile::Fast (KernelConfig::fast_math): fp16 logits storage, exact label
+  // logits from a dot-product kernel, part of the exp2 work on the FMA pipe
+  bool fast;
 };
 
 struct WsLayout {
   size_t logits = 0, rec_own = 0, rec_own_t = 0, dlog_s = 0, dlog_t = 0, nll_s = 0, nll_t = 0, kl_base = 0,
-         s_part = 0, flags = 0, row_const = 0, total = 0;
+         s_part = 0, flags = 0, row_const = 0, x_label = 0, t_label = 0, total = 0;
   size_t ldv = 0, ldd = 0, parts = 0, parts_t = 0, nseg = 0, cs = 0, fwd_rows = 0, group_rows = 0;
 };
 
@@ -146,7 +149,7 @@ WsLayout make_layout(const DevInputs& in, const Flags& f, size_t cs, size_t fwd_
     off = round_up(off + bytes, 256);
     return o;
   };
-  L.logits = take((f.teacher_rows ? 2 : 1) * fwd_rows * L.ldv * sizeof(float));
+  L.logits = take((f.teacher_rows ? 2 : 1) * fwd_rows * L.ldv * (f.fast ? 2 : 4));
   L.rec_own = take(fwd_rows * L.parts * 16);
   L.rec_own_t = take(f.need_teacher ? fwd_rows * L.parts_t * 16 : 0);
   L.dlog_s = take(group_rows * L.ldd * 2);
@@ -157,6 +160,8 @@ WsLayout make_layout(const DevInputs& in, const Flags& f, size_t cs, size_t fwd_
   L.s_part = take(in.bt * L.nseg * sizeof(float));
   L.flags = take(f.quant ? in.v : 0);
   L.row_const = take(fwd_rows * kRowConstBytes);
+  L.x_label = take(f.fast ? fwd_rows * sizeof(float) : 0);
+  L.t_label = take(f.fast && f.teacher_rows && f.teacher_ce ? fwd_rows * sizeof(float) : 0);
   L.total = off;
   return L;
 }
@@ -348,6 +353,7 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
   f.teacher_rows = f.need_teacher && live_teacher;
   f.teacher_grad = f.w_t > 0.0f && live_teacher;
   f.teacher_ce = f.w_t > 0.0f;
+  f.fast = o.config.fast_math != 0;
   const bool scatter = shard && shard->scatter_grad_weight;
   f.quant = o.config.quantize_grad_weight != 0 && !(shard && shard->skip_quantize) && !scatter;
 
@@ -422,7 +428,8 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
   AllocTry at{ctx, &in, &f, {}};
   OrdaChunkPlan used{};
   static_assert(sizeof(WsLayout) <= sizeof(ctx->vocab_layout), "saved layout");
-  const int layout_flags = (f.need_teacher ? 1 : 0) | (f.teacher_rows ? 2 : 0) | (f.teacher_grad ? 4 : 0) |
+  const int layout_flags = (f.fast ? 64 : 0) | (f.need_teacher ? 1 : 0) | (f.teacher_rows ? 2 : 0) |
+                           (f.teacher_grad ? 4 : 0) |
                            (f.quant ? 8 : 0) | (f.kd > 0.0f ? 16 : 0) | (f.teacher_ce ? 32 : 0);
   bool have = false;
   if (vphase == 2) {
@@ -484,8 +491,10 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
   if (plan_out) *plan_out = used;
 
   uint8_t* ws = static_cast<uint8_t*>(ctx->ws);
-  float* logits = reinterpret_cast<float*>(ws + L.logits);
-  float* logits_t = logits + L.fwd_rows * L.ldv;
+  void* logits = ws + L.logits;
+  void* logits_t = ws + L.logits + L.fwd_rows * L.ldv * (f.fast ? 2 : 4);
+  float* x_label = f.fast ? reinterpret_cast<float*>(ws + L.x_label) : nullptr;
+  float* t_label = f.fast && f.teacher_rows && f.teacher_ce ? reinterpret_cast<float*>(ws + L.t_label) : nullptr;
   float* rec_own = reinterpret_cast<float*>(ws + L.rec_own);
   float* rec_own_t = reinterpret_cast<float*>(ws + L.rec_own_t);
   uint16_t* dlog_s = reinterpret_cast<uint16_t*>(ws + L.dlog_s);
@@ -533,6 +542,7 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
                                                                    s * in.ld_t_logits * t_esz);
       const long long t_ld = live_teacher ? static_cast<long long>(L.ldv) : in.ld_t_logits;
       const int t_bf16 = live_teacher ? 0 : static_cast<int>(in.t_logits_bf16);
+      const int t_dtype = live_teacher ? (f.fast ? kLogitF16 : kLogitF32) : (in.t_logits_bf16 ? kLogitBF16 : kLogitF32);
       if (vphase != 2) {
         Phase ph_fwd(ctx, 0, st);
         // ---- teacher logits + statistics (Tied / Separate)
@@ -550,6 +560,7 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
           gd.epi = Epi::Logits;
           gd.status = status;
           gd.args.logits = logits_t;
+          gd.args.logits_f16 = f.fast;
           gd.args.ldl = static_cast<long long>(L.ldv);
           gd.args.rec_own = rec_own_t;
           gd.args.n_parts = static_cast<int>(L.parts);
@@ -573,6 +584,7 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
         gd.epi = Epi::Logits;
         gd.status = status;
         gd.args.logits = logits;
+        gd.args.logits_f16 = f.fast;
         gd.args.ldl = static_cast<long long>(L.ldv);
         gd.args.rec_own = rec_own;
         gd.args.n_parts = static_cast<int>(L.parts);
@@ -593,7 +605,22 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
         if (vphase != 2 && f.need_teacher && !live_teacher) {
           ph_rows.launched();
           launch_teacher_stats(t_rows, t_ld, t_bf16, static_cast<int>(n), static_cast<int>(v), inv_t, rec_own_t, st,
-                               f.teacher_ce);
+                               f.teacher_ce, f.fast);
+        }
+        if (f.fast && vphase != 2) {
+          // exact fp32 label logits (the 16-bit logits buffer is rounded)
+          const long long lv0 = vphase ? vc->v0 : 0;
+          ph_rows.launched();
+          launch_label_logits(static_cast<const uint16_t*>(in.hs.ptr) + s * in.hs.ld, in.hs.ld, in.w.ptr, in.w.ld,
+                              static_cast<long long>(h), in.labels + s, static_cast<long long>(n), lv0,
+                              static_cast<long long>(v), o.ignore_index, x_label, st);
+          if (t_label) {
+            const MatRef& tw = in.mode == ORDA_TEACHER_TIED ? in.w : in.wt;
+            ph_rows.launched();
+            launch_label_logits(static_cast<const uint16_t*>(in.ht.ptr) + s * in.ht.ld, in.ht.ld, tw.ptr, tw.ld,
+                                static_cast<long long>(in.mode == ORDA_TEACHER_TIED ? h : ht), in.labels + s,
+                                static_cast<long long>(n), lv0, static_cast<long long>(v), o.ignore_index, t_label, st);
+          }
         }
         ph_rows.launched(vphase == 1 ? 1 : kRowLaunches);
         RowArgs r{};
@@ -602,10 +629,14 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
         r.n_parts = static_cast<int>(L.parts);
         r.n_parts_t = static_cast<int>(L.parts_t);
         r.logits_s = logits;
+        r.logits_f16 = f.fast;
+        r.x_label = x_label;
+        r.t_label = t_label;
+        r.fast = f.fast;
         r.ldl = static_cast<long long>(L.ldv);
         r.teacher = t_rows;
         r.ld_teacher = t_ld;
-        r.teacher_is_bf16 = t_bf16;
+        r.teacher_dtype = t_dtype;
         r.rec_own = rec_own;
         r.rec_own_t = rec_own_t;
         r.labels = in.labels + s;

@@ -34,6 +34,7 @@
 // the CTA pair's loads each land in their own CTA.
 #include <cuda.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
@@ -45,6 +46,7 @@
 #include <cstring>
 #include <mutex>
 
+#include "fastmath.cuh"
 #include "kernels.h"
 #include "ptx.cuh"
 
@@ -170,8 +172,9 @@ __device__ __forceinline__ float max32(const float (&v)[32]) {
 }
 
 // Online-softmax statistics of one 32-column chunk of one row. FULL: all 32
-// columns valid (no per-element masking).
-template <bool FULL, bool OWN_DT>
+// columns valid (no per-element masking). POLY (Fast profile): the tempered
+// sum's exp2 on the FMA pipe (exp2_fma), the other on the SFU.
+template <bool FULL, bool OWN_DT, bool POLY>
 __device__ __forceinline__ void logits_chunk(const EpiArgs& e, long long grow, bool row_ok, int col0, int nvalid,
                                              const uint32_t (&r)[32], OwnStats& os) {
   float v[32];
@@ -192,7 +195,7 @@ __device__ __forceinline__ void logits_chunk(const EpiArgs& e, long long grow, b
     if (FULL || j < nvalid) {
       const float u = v[j] - m_new;
       a1[j & 3] += fast_exp2(u * LOG2E);
-      if (OWN_DT) aT[j & 3] += fast_exp2(u * lt);
+      if (OWN_DT) aT[j & 3] += POLY ? exp2_fma(u * lt) : fast_exp2(u * lt);
       ax[j & 3] += v[j];
     }
   }
@@ -201,12 +204,22 @@ __device__ __forceinline__ void logits_chunk(const EpiArgs& e, long long grow, b
   os.sx += (ax[0] + ax[1]) + (ax[2] + ax[3]);
 }
 
-template <bool OWN_DT>
+template <bool OWN_DT, bool POLY>
 __device__ __forceinline__ void logits_chunk_any(const EpiArgs& e, long long grow, bool row_ok, int col0, int N,
                                                  const uint32_t (&r)[32], OwnStats& os) {
   const int nvalid = N - col0;
-  if (nvalid >= 32) logits_chunk<true, OWN_DT>(e, grow, row_ok, col0, 32, r, os);
-  else if (nvalid > 0) logits_chunk<false, OWN_DT>(e, grow, row_ok, col0, nvalid, r, os);
+  if (nvalid >= 32) logits_chunk<true, OWN_DT, POLY>(e, grow, row_ok, col0, 32, r, os);
+  else if (nvalid > 0) logits_chunk<false, OWN_DT, POLY>(e, grow, row_ok, col0, nvalid, r, os);
+}
+
+// Two fp32 accumulator values as an fp16 pair (round to nearest, saturated to
+// the largest finite fp16, so no logit becomes infinite); the first value in
+// the low half (the lower address).
+__device__ __forceinline__ uint32_t pack_f16x2_sat(uint32_t a, uint32_t b) {
+  const float fa = fminf(fmaxf(__uint_as_float(a), -65504.0f), 65504.0f);
+  const float fb = fminf(fmaxf(__uint_as_float(b), -65504.0f), 65504.0f);
+  const __half2 h = __floats2half2_rn(fa, fb);
+  return *reinterpret_cast<const uint32_t*>(&h);
 }
 
 // Writes the warp's 32 x 32 fp32 chunk (row `lane` = this thread's values,
@@ -508,16 +521,44 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         store(3, rb);
       } else {
         constexpr bool OWN_DT = (EPI & 1) != 0;
+        constexpr bool F16 = (EPI & 2) != 0;  // Fast profile: fp16 logits, exp2 split over SFU and FMA
         OwnStats os{-INFINITY, 0.f, 0.f, 0.f};
         const EpiArgs& e = p.e;
         auto chunk = [&](int c, const uint32_t(&r)[32]) {
           const int col0 = colh + c * 32;
+          if constexpr (F16) {
+            if (col0 < p.N) logits_chunk_any<OWN_DT, true>(e, grow, row_ok, col0, p.N, r, os);
+            // this row's 32 values as fp16 into the staging row of a 64-column
+            // pair (128 bytes, 128-byte swizzle: 16-byte piece (c & 1) * 4 + k);
+            // the pair goes out in one TMA store, clipped at the tensor bounds
+            if ((c & 1) == 0) {
+              if (lane == 0) bulk_wait_read_all();
+              __syncwarp();
+            }
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const uint4 q = make_uint4(pack_f16x2_sat(r[8 * k], r[8 * k + 1]), pack_f16x2_sat(r[8 * k + 2], r[8 * k + 3]),
+                                         pack_f16x2_sat(r[8 * k + 4], r[8 * k + 5]),
+                                         pack_f16x2_sat(r[8 * k + 6], r[8 * k + 7]));
+              *reinterpret_cast<uint4*>(buf + lane * 128 + ((((c & 1) * 4 + k) ^ (lane & 7)) << 4)) = q;
+            }
+            if (c & 1) {
+              fence_proxy_async_smem();
+              __syncwarp();
+              const int x = colh + (c - 1) * 32;
+              if (lane == 0 && row0 < p.M && x < p.N) {
+                tma_store_2d_hint(&mapC, buf, x, row0, pol_c);
+                bulk_commit();
+              }
+            }
+            return;
+          }
           if (col0 >= p.N) return;
-          logits_chunk_any<OWN_DT>(e, grow, row_ok, col0, p.N, r, os);
+          logits_chunk_any<OWN_DT, false>(e, grow, row_ok, col0, p.N, r, os);
           if (p.tma_store) {
             if (row0 < p.M) stage_and_store(buf, lane, r, 1.0f, &mapC, col0, row0, false, pol_c);
           } else if (row_ok) {
-            float* dst = e.logits + grow * e.ldl + col0;
+            float* dst = static_cast<float*>(e.logits) + grow * e.ldl + col0;
             const int nv = min(32, p.N - col0);
 #pragma unroll
             for (int j = 0; j < 32; ++j)
@@ -634,8 +675,22 @@ bool encode_out_map(CUtensorMap* map, float* ptr, long long rows, long long cols
   return r == CUDA_SUCCESS;
 }
 
-bool out_map_ok(const float* ptr, long long ld) {
-  return ptr && (reinterpret_cast<uintptr_t>(ptr) & 15) == 0 && (ld * 4) % 16 == 0;
+bool out_map_ok(const void* ptr, long long ld, int esz = 4) {
+  return ptr && (reinterpret_cast<uintptr_t>(ptr) & 15) == 0 && (ld * esz) % 16 == 0;
+}
+
+// fp16 logits map: rows x cols with leading dimension ld (elements), a box of
+// 64 columns (128 bytes) x 32 rows, 128-byte swizzle (the staging layout of
+// the Fast logits epilogue).
+bool encode_out_map_f16(CUtensorMap* map, void* ptr, long long rows, long long cols, long long ld) {
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2};
+  cuuint32_t box[2] = {64, 32};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, ptr, dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
 }
 
 // Per-device, per-instantiation launch state: the shared-memory opt-in
@@ -711,7 +766,11 @@ cudaError_t dispatch(const GemmDesc& d, const CUtensorMap* maps, const KParams& 
       if (why) *why = "logits epilogue requires K-major operands";
       return cudaErrorInvalidValue;
     }
-    // EPI code: 16 | own dT
+    // EPI code: 16 | own dT | 2 * fp16 logits
+    if (d.args.logits_f16) {
+      if (d.args.own_dT) return launch_t<CG, false, false, 19>(maps, kp, num_sms, stream);
+      return launch_t<CG, false, false, 18>(maps, kp, num_sms, stream);
+    }
     if (d.args.own_dT) return launch_t<CG, false, false, 17>(maps, kp, num_sms, stream);
     return launch_t<CG, false, false, 16>(maps, kp, num_sms, stream);
   }
@@ -800,8 +859,18 @@ cudaError_t gemm_launch(const GemmDesc& d, int num_sms, cudaStream_t stream, con
       return cudaErrorInvalidValue;
     }
   } else if (d.epi == Epi::Logits) {
-    if (out_map_ok(d.args.logits, d.args.ldl) && encode_out_map(&maps[4], d.args.logits, d.M, d.N, d.args.ldl))
+    if (d.args.logits_f16) {
+      // the fp16 epilogue stores through TMA only
+      if (!out_map_ok(d.args.logits, d.args.ldl, 2) ||
+          !encode_out_map_f16(&maps[4], d.args.logits, d.M, d.N, d.args.ldl)) {
+        if (why) *why = "fp16 logits need a 16-byte aligned buffer with ld a multiple of 8";
+        return cudaErrorInvalidValue;
+      }
       kp.tma_store = 1;
+    } else if (out_map_ok(d.args.logits, d.args.ldl) &&
+               encode_out_map(&maps[4], static_cast<float*>(d.args.logits), d.M, d.N, d.args.ldl)) {
+      kp.tma_store = 1;
+    }
   } else if (d.args.split_row >= d.M && (d.args.beta == 0.0f || d.args.beta == 1.0f) &&
              out_map_ok(d.args.out0, d.args.ld0) && encode_out_map(&maps[4], d.args.out0, d.M, d.N, d.args.ld0)) {
     kp.tma_store = 1;

@@ -36,12 +36,13 @@ struct EpiArgs {
   const float* alpha_ptr = nullptr;  // device scalar overriding alpha
   float beta = 0.0f;
   // Logits
-  float* logits = nullptr;
+  void* logits = nullptr;  // fp32, or fp16 with logits_f16
   long long ldl = 0;
   float* rec_own = nullptr;   // float4 per (row, part)
   int n_parts = 0;
   float inv_t = 1.0f;
   int own_dT = 0;
+  int logits_f16 = 0;  // Fast profile: logits stored as fp16 (the statistics still come from fp32)
   // Store, scattered to the owners of grad_W rows (row-sharded runs): global
   // row g belongs to rank o = g / slot_slice and lands in rank o's slot
   // buffer, at partial slot_rank, row g - o * slot_slice (fp32, ld slot_ld).
@@ -77,16 +78,27 @@ struct GemmDesc {
 cudaError_t gemm_launch(const GemmDesc& d, int num_sms, cudaStream_t stream, const char** why);
 
 // ------------------------------------------------------------ row kernels
+// Element type of a logits buffer the row kernels read.
+enum LogitType : int { kLogitF32 = 0, kLogitBF16 = 1, kLogitF16 = 2 };
+
 struct RowArgs {
   int n;                  // rows in this chunk
   int v;                  // vocabulary
   int n_parts;            // student record parts per row
   int n_parts_t;          // teacher record parts per row (1 after the teacher pre-pass)
-  const float* logits_s;  // [n, ldl] fp32 student logits
-  const void* teacher;    // teacher logits rows for this chunk (fp32 or bf16)
+  const void* logits_s;   // [n, ldl] student logits (fp32, or fp16 with logits_f16)
+  int logits_f16;         // Fast profile: 16-bit student logits
+  const void* teacher;    // teacher logits rows for this chunk
   long long ld_teacher;
-  int teacher_is_bf16;
+  int teacher_dtype;      // LogitType of the teacher logits
   long long ldl;
+  // Optional exact label logits (fp32) of this chunk's rows: the student's
+  // (and teacher's) logit at the label column, 0 for ignored rows or labels
+  // outside this rank's slice. With 16-bit logits the losses take the label
+  // logit from here instead of the rounded buffer.
+  const float* x_label;
+  const float* t_label;
+  int fast;               // Fast profile: part of the exp2 work on the FMA pipe
   const float* rec_own;   // [n] student records
   const float* rec_own_t; // [n] teacher records (from the teacher GEMM or the pre-pass)
   const int64_t* labels;  // chunk labels
@@ -133,8 +145,16 @@ void launch_vocab_rows(const RowArgs& a, cudaStream_t stream);
 // Teacher statistics pre-pass over given teacher logits (Precomputed mode):
 // one (max, sum e^(t-m), sum e^((t-m)/T), sum t) record per row. need_d1 =
 // false (no teacher CE term) skips sum e^(t-m) and records 1 in its place.
+// fast: half of the exp2 work on the FMA pipe (Fast profile).
 void launch_teacher_stats(const void* teacher, long long ld, int is_bf16, int n, int v, float inv_t, float* rec,
-                          cudaStream_t stream, bool need_d1 = true);
+                          cudaStream_t stream, bool need_d1 = true, bool fast = false);
+
+// Exact label logits: out[i] = sum_k h[i, k] * w[labels[i] - v0, k] (fp32
+// products of the bf16 inputs) for labels in [v0, v0 + v_rows), else 0
+// (ignored rows and labels of other slices). One warp per row.
+void launch_label_logits(const void* h, long long ldh, const void* w, long long ldw, long long k,
+                         const int64_t* labels, long long n, long long v0, long long v_rows, int64_t ignore_index,
+                         float* out, cudaStream_t stream);
 
 // Label pass: counts non-ignored labels, checks the range [0, v), marks
 // target rows (for the quantiser) and writes the mean scale.

@@ -21,11 +21,13 @@
 //                     without another pass; finalize adds the segments in a
 //                     fixed order (deterministic).
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <cmath>
 #include <cstdint>
 
+#include "fastmath.cuh"
 #include "kernels.h"
 #include "ptx.cuh"
 
@@ -62,6 +64,20 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
 
 __device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+__device__ __forceinline__ float f16_lo(uint32_t w) {
+  return __half2float(__ushort_as_half(static_cast<unsigned short>(w & 0xFFFFu)));
+}
+__device__ __forceinline__ float f16_hi(uint32_t w) {
+  return __half2float(__ushort_as_half(static_cast<unsigned short>(w >> 16)));
+}
+
+// One logit of a buffer of LogitType `dtype`.
+__device__ __forceinline__ float logit_at(const void* base, int dtype, long long idx) {
+  if (dtype == kLogitBF16)
+    return __uint_as_float(static_cast<uint32_t>(static_cast<const uint16_t*>(base)[idx]) << 16);
+  if (dtype == kLogitF16) return __half2float(static_cast<const __half*>(base)[idx]);
+  return static_cast<const float*>(base)[idx];
+}
 
 // ------------------------------------------------------ block reductions
 // Results are returned to every thread; the order of additions is fixed, so
@@ -151,11 +167,7 @@ __device__ __forceinline__ bool row_label(const RowArgs& a, int i, long long& y)
 }
 
 __device__ __forceinline__ double teacher_value(const RowArgs& a, long long i, long long col) {
-  if (a.teacher_is_bf16) {
-    const uint16_t b = static_cast<const uint16_t*>(a.teacher)[i * a.ld_teacher + col];
-    return static_cast<double>(__uint_as_float(static_cast<uint32_t>(b) << 16));
-  }
-  return static_cast<double>(static_cast<const float*>(a.teacher)[i * a.ld_teacher + col]);
+  return static_cast<double>(logit_at(a.teacher, a.teacher_dtype, i * a.ld_teacher + col));
 }
 
 // Per-row losses and constants of row i from its merged statistics (own:
@@ -216,8 +228,10 @@ __global__ void __launch_bounds__(ROW_THREADS) row_stats_kernel(const RowArgs a)
   const bool ignored = row_label(a, i, y);
   double x_y = 0.0, t_y = 0.0;
   if (!ignored) {
-    x_y = static_cast<double>(a.logits_s[static_cast<long long>(i) * a.ldl + y]);
-    if (a.teacher_ce) t_y = teacher_value(a, i, y);
+    x_y = a.x_label ? static_cast<double>(a.x_label[i])
+                    : static_cast<double>(logit_at(a.logits_s, a.logits_f16 ? kLogitF16 : kLogitF32,
+                                                   static_cast<long long>(i) * a.ldl + y));
+    if (a.teacher_ce) t_y = a.t_label ? static_cast<double>(a.t_label[i]) : teacher_value(a, i, y);
   }
   finish_row(a, i, own, ts, ignored, x_y, t_y, static_cast<int>(y));
 }
@@ -237,8 +251,9 @@ __global__ void __launch_bounds__(ROW_THREADS) vocab_partials_kernel(const RowAr
   const long long yl = y - a.v0;
   float x_y = 0.0f, t_y = 0.0f, has_y = 0.0f;
   if (!ignored && yl >= 0 && yl < a.v) {
-    x_y = a.logits_s[static_cast<long long>(i) * a.ldl + yl];
-    if (a.teacher_ce) t_y = static_cast<float>(teacher_value(a, i, yl));
+    x_y = a.x_label ? a.x_label[i]
+                    : logit_at(a.logits_s, a.logits_f16 ? kLogitF16 : kLogitF32, static_cast<long long>(i) * a.ldl + yl);
+    if (a.teacher_ce) t_y = a.t_label ? a.t_label[i] : static_cast<float>(teacher_value(a, i, yl));
     has_y = 1.0f;
   }
   float4* out = reinterpret_cast<float4*>(a.partials_out + static_cast<long long>(i) * kVocabTuple);
@@ -295,13 +310,16 @@ struct GradScalars {
 
 // One element: the student (and teacher) logit gradient and the KL cross
 // term p_t^T (t - x) / T.
-template <bool KL, bool TGRAD>
+// FAST: the student's tempered probability on the FMA pipe (exp2_fma), the
+// other exp2 on the SFU.
+template <bool KL, bool TGRAD, bool FAST>
 __device__ __forceinline__ void grad_elem(const GradScalars& g, const RowConst& c, int j, float x, float t, float& gs,
                                           float& gt, float& cross) {
   float s = g.ws * (fast_exp2(fmaf(x, g.l1, -c.c_s1)) - g.eps);
   if (KL) {
     const float pt = fast_exp2(fmaf(t, g.lT, -c.c_tT));
-    s += g.kdT * (fast_exp2(fmaf(x, g.lT, -c.c_sT)) - pt);
+    const float ps = FAST ? exp2_fma(fmaf(x, g.lT, -c.c_sT)) : fast_exp2(fmaf(x, g.lT, -c.c_sT));
+    s += g.kdT * (ps - pt);
     cross = fmaf(pt, (t - x) * g.inv_t, cross);
   }
   if (j == c.y) s -= g.ws_tgt;
@@ -314,8 +332,10 @@ __device__ __forceinline__ void grad_elem(const GradScalars& g, const RowConst& 
   gt = u;
 }
 
-__device__ __forceinline__ void load_teacher8(const void* teacher, bool is_bf16, long long off, float (&t)[8]) {
-  if (is_bf16) {
+// Eight consecutive logits of a buffer of LogitType `dtype` (16-byte aligned
+// for the 16-bit types, 32-byte for fp32).
+__device__ __forceinline__ void load_teacher8(const void* teacher, int dtype, long long off, float (&t)[8]) {
+  if (dtype == kLogitBF16) {
     const uint4 q = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(teacher) + off));
     t[0] = bf16_lo(q.x);
     t[1] = bf16_hi(q.x);
@@ -325,6 +345,16 @@ __device__ __forceinline__ void load_teacher8(const void* teacher, bool is_bf16,
     t[5] = bf16_hi(q.z);
     t[6] = bf16_lo(q.w);
     t[7] = bf16_hi(q.w);
+  } else if (dtype == kLogitF16) {
+    const uint4 q = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(teacher) + off));
+    t[0] = f16_lo(q.x);
+    t[1] = f16_hi(q.x);
+    t[2] = f16_lo(q.y);
+    t[3] = f16_hi(q.y);
+    t[4] = f16_lo(q.z);
+    t[5] = f16_hi(q.z);
+    t[6] = f16_lo(q.w);
+    t[7] = f16_hi(q.w);
   } else {
     const float* tp = static_cast<const float*>(teacher) + off;
     const float4 t0 = __ldg(reinterpret_cast<const float4*>(tp));
@@ -349,13 +379,16 @@ __device__ __forceinline__ float block_sum_f(float v, float* sh) {
 // ---- grid (row, segment): gradients of one 8192-column segment of one row
 // (rows on grid x, which has no 65535 limit).
 // VEC: V % 8 == 0 and 16-byte aligned rows (8 columns per thread step).
-template <bool VEC, bool KL, bool TGRAD>
+// FAST (Fast profile): fp16 student logits, part of the exp2 work on the FMA
+// pipe.
+template <bool VEC, bool KL, bool TGRAD, bool FAST>
 __global__ void __launch_bounds__(GRAD_THREADS) row_grad_kernel(const RowArgs a, const GradScalars g) {
   __shared__ float sh[GRAD_THREADS / 32];
   const int seg = blockIdx.y;
   const long long row = blockIdx.x;
   const RowConst c = reinterpret_cast<const RowConst*>(a.row_const)[row];
-  const float* xs = a.logits_s + row * a.ldl;
+  const float* xs = FAST ? nullptr : static_cast<const float*>(a.logits_s) + row * a.ldl;
+  const __half* xh = FAST ? static_cast<const __half*>(a.logits_s) + row * a.ldl : nullptr;
   uint16_t* gs_row = a.dlog_s + row * a.ldd;
   uint16_t* gt_row = TGRAD ? a.dlog_t + row * a.ldd : nullptr;
   const bool need_t = KL || TGRAD;
@@ -381,14 +414,22 @@ __global__ void __launch_bounds__(GRAD_THREADS) row_grad_kernel(const RowArgs a,
     for (int step = 0; step < GRAD_STEPS; ++step) {
       const int j0 = c0 + (step * GRAD_THREADS + threadIdx.x) * 8;
       if (j0 < c1) {
-        const float4 x0 = __ldg(reinterpret_cast<const float4*>(xs + j0));
-        const float4 x1 = __ldg(reinterpret_cast<const float4*>(xs + j0 + 4));
-        const float x[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+        float x[8];
+        if (FAST) {
+          const uint4 q = __ldg(reinterpret_cast<const uint4*>(xh + j0));
+          x[0] = f16_lo(q.x); x[1] = f16_hi(q.x); x[2] = f16_lo(q.y); x[3] = f16_hi(q.y);
+          x[4] = f16_lo(q.z); x[5] = f16_hi(q.z); x[6] = f16_lo(q.w); x[7] = f16_hi(q.w);
+        } else {
+          const float4 x0 = __ldg(reinterpret_cast<const float4*>(xs + j0));
+          const float4 x1 = __ldg(reinterpret_cast<const float4*>(xs + j0 + 4));
+          x[0] = x0.x; x[1] = x0.y; x[2] = x0.z; x[3] = x0.w;
+          x[4] = x1.x; x[5] = x1.y; x[6] = x1.z; x[7] = x1.w;
+        }
         float t[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        if (need_t) load_teacher8(a.teacher, a.teacher_is_bf16, row * a.ld_teacher + j0, t);
+        if (need_t) load_teacher8(a.teacher, a.teacher_dtype, row * a.ld_teacher + j0, t);
         float gsv[8], gtv[8];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) grad_elem<KL, TGRAD>(g, c, j0 + k, x[k], t[k], gsv[k], gtv[k], cross);
+        for (int k = 0; k < 8; ++k) grad_elem<KL, TGRAD, FAST>(g, c, j0 + k, x[k], t[k], gsv[k], gtv[k], cross);
         *reinterpret_cast<uint4*>(gs_row + j0) = make_uint4(pack_bf16x2(gsv[0], gsv[1]), pack_bf16x2(gsv[2], gsv[3]),
                                                             pack_bf16x2(gsv[4], gsv[5]), pack_bf16x2(gsv[6], gsv[7]));
         if (TGRAD)
@@ -400,16 +441,10 @@ __global__ void __launch_bounds__(GRAD_THREADS) row_grad_kernel(const RowArgs a,
   } else {
     for (int j = c0 + threadIdx.x; j < c1; j += GRAD_THREADS) {
       float t = 0.0f;
-      if (need_t) {
-        if (a.teacher_is_bf16) {
-          const uint16_t b = static_cast<const uint16_t*>(a.teacher)[row * a.ld_teacher + j];
-          t = __uint_as_float(static_cast<uint32_t>(b) << 16);
-        } else {
-          t = static_cast<const float*>(a.teacher)[row * a.ld_teacher + j];
-        }
-      }
+      if (need_t) t = logit_at(a.teacher, a.teacher_dtype, row * a.ld_teacher + j);
+      const float x = FAST ? __half2float(xh[j]) : xs[j];
       float gs, gt;
-      grad_elem<KL, TGRAD>(g, c, j, xs[j], t, gs, gt, cross);
+      grad_elem<KL, TGRAD, FAST>(g, c, j, x, t, gs, gt, cross);
       gs_row[j] = __bfloat16_as_ushort(__float2bfloat16_rn(gs));
       if (TGRAD) gt_row[j] = __bfloat16_as_ushort(__float2bfloat16_rn(gt));
     }
@@ -430,7 +465,9 @@ __device__ __forceinline__ float teacher_at(const void* teacher, int is_bf16, lo
 // sums cost one exp2 each per element on the SFU, which bounds this kernel
 // before HBM does: NEED_D1 = false (no teacher CE term) skips sum e^(t-m)
 // and records d1 = 1.
-template <bool NEED_D1>
+// FAST: the tempered sum of every other vector of 8 on the FMA pipe
+// (exp2_fma), the rest on the SFU.
+template <bool NEED_D1, bool FAST>
 __global__ void __launch_bounds__(ROW_THREADS) teacher_stats_kernel(const void* teacher, long long ld, int is_bf16,
                                                                     int v, float inv_t, float* rec) {
   __shared__ double sh[3 * 32];
@@ -447,7 +484,7 @@ __global__ void __launch_bounds__(ROW_THREADS) teacher_stats_kernel(const void* 
       for (int u = 0; u < U; ++u) {
         const int j0 = base + u * ROW_THREADS * 8;
         if (j0 < v) {
-          load_teacher8(teacher, is_bf16, row * ld + j0, t[u]);
+          load_teacher8(teacher, is_bf16 ? kLogitBF16 : kLogitF32, row * ld + j0, t[u]);
         } else {
 #pragma unroll
           for (int k = 0; k < 8; ++k) t[u][k] = -INFINITY;
@@ -471,7 +508,7 @@ __global__ void __launch_bounds__(ROW_THREADS) teacher_stats_kernel(const void* 
           if (t[u][k] != -INFINITY) {
             const float x = t[u][k] - m;
             if (NEED_D1) d1 += fast_exp2(x * LOG2E_F);
-            dT += fast_exp2(x * lt);
+            dT += (FAST && (u & 1)) ? exp2_fma(x * lt) : fast_exp2(x * lt);
             sx += t[u][k];
           }
         }
@@ -603,14 +640,54 @@ __global__ void f32_to_bf16_kernel(const float* src, long long rows, long long c
   }
 }
 
-template <bool VEC>
+template <bool VEC, bool FAST>
 void launch_grad(const RowArgs& a, const GradScalars& g, cudaStream_t stream) {
   const dim3 grid(static_cast<unsigned>(a.n), static_cast<unsigned>((a.v + kGradSegCols - 1) / kGradSegCols));
   const bool kl = a.need_kl != 0, tg = a.teacher_grad != 0;
-  if (kl && tg) row_grad_kernel<VEC, true, true><<<grid, GRAD_THREADS, 0, stream>>>(a, g);
-  else if (kl) row_grad_kernel<VEC, true, false><<<grid, GRAD_THREADS, 0, stream>>>(a, g);
-  else if (tg) row_grad_kernel<VEC, false, true><<<grid, GRAD_THREADS, 0, stream>>>(a, g);
-  else row_grad_kernel<VEC, false, false><<<grid, GRAD_THREADS, 0, stream>>>(a, g);
+  if (kl && tg) row_grad_kernel<VEC, true, true, FAST><<<grid, GRAD_THREADS, 0, stream>>>(a, g);
+  else if (kl) row_grad_kernel<VEC, true, false, FAST><<<grid, GRAD_THREADS, 0, stream>>>(a, g);
+  else if (tg) row_grad_kernel<VEC, false, true, FAST><<<grid, GRAD_THREADS, 0, stream>>>(a, g);
+  else row_grad_kernel<VEC, false, false, FAST><<<grid, GRAD_THREADS, 0, stream>>>(a, g);
+}
+
+// ---- exact label logits: one warp per row, fp32 dot product of the bf16
+// hidden row and the label's weight row (16-byte loads when aligned)
+__global__ void __launch_bounds__(256) label_logit_kernel(const uint16_t* h, long long ldh, const uint16_t* w,
+                                                          long long ldw, long long k, const int64_t* labels,
+                                                          long long n, long long v0, long long v_rows,
+                                                          int64_t ignore_index, float* out) {
+  const long long i = blockIdx.x * 8ll + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (i >= n) return;
+  const int64_t y = labels[i];
+  const long long yl = static_cast<long long>(y) - v0;
+  if (y == ignore_index || yl < 0 || yl >= v_rows) {
+    if (lane == 0) out[i] = 0.0f;
+    return;
+  }
+  const uint16_t* hr = h + i * ldh;
+  const uint16_t* wr = w + yl * ldw;
+  float acc = 0.0f;
+  const bool vec = ((reinterpret_cast<uintptr_t>(hr) | reinterpret_cast<uintptr_t>(wr)) & 15) == 0;
+  // 16-byte loads over the whole groups of 8 columns, then the tail
+  const long long kv = vec ? (k / 8) * 8 : 0;
+  for (long long c = lane * 8; c < kv; c += 256) {
+    const uint4 p = __ldg(reinterpret_cast<const uint4*>(hr + c));
+    const uint4 q = __ldg(reinterpret_cast<const uint4*>(wr + c));
+    acc = fmaf(bf16_lo(p.x), bf16_lo(q.x), acc);
+    acc = fmaf(bf16_hi(p.x), bf16_hi(q.x), acc);
+    acc = fmaf(bf16_lo(p.y), bf16_lo(q.y), acc);
+    acc = fmaf(bf16_hi(p.y), bf16_hi(q.y), acc);
+    acc = fmaf(bf16_lo(p.z), bf16_lo(q.z), acc);
+    acc = fmaf(bf16_hi(p.z), bf16_hi(q.z), acc);
+    acc = fmaf(bf16_lo(p.w), bf16_lo(q.w), acc);
+    acc = fmaf(bf16_hi(p.w), bf16_hi(q.w), acc);
+  }
+  for (long long j = kv + lane; j < k; j += 32)
+    acc = fmaf(__uint_as_float(static_cast<uint32_t>(hr[j]) << 16), __uint_as_float(static_cast<uint32_t>(wr[j]) << 16),
+               acc);
+  for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if (lane == 0) out[i] = acc;
 }
 
 void launch_row_grad(const RowArgs& a, cudaStream_t stream);
@@ -649,22 +726,39 @@ void launch_row_grad(const RowArgs& a, cudaStream_t stream) {
   g.l1 = LOG2E_F;
   g.lT = LOG2E_F * a.inv_t;
   g.inv_t = a.inv_t;
-  const long long tsz = a.teacher_is_bf16 ? 2 : 4;
+  const long long tsz = a.teacher_dtype == kLogitF32 ? 4 : 2;
   const bool teacher_ok = !(a.need_kl || a.teacher_grad) ||
                           (((a.ld_teacher * tsz) % 16 == 0) && ((reinterpret_cast<uintptr_t>(a.teacher) & 15) == 0));
-  const bool vec = (a.v % 8 == 0) && (a.ldl % 4 == 0) && (a.ldd % 8 == 0) && teacher_ok &&
+  const long long lsz = a.logits_f16 ? 2 : 4;
+  const bool vec = (a.v % 8 == 0) && ((a.ldl * lsz) % 16 == 0) && (a.ldd % 8 == 0) && teacher_ok &&
                    ((reinterpret_cast<uintptr_t>(a.logits_s) & 15) == 0);
-  if (vec) launch_grad<true>(a, g, stream);
-  else launch_grad<false>(a, g, stream);
+  if (a.logits_f16) {
+    if (vec) launch_grad<true, true>(a, g, stream);
+    else launch_grad<false, true>(a, g, stream);
+  } else {
+    if (vec) launch_grad<true, false>(a, g, stream);
+    else launch_grad<false, false>(a, g, stream);
+  }
 }
 
 }  // namespace
 
 void launch_teacher_stats(const void* teacher, long long ld, int is_bf16, int n, int v, float inv_t, float* rec,
-                          cudaStream_t stream, bool need_d1) {
+                          cudaStream_t stream, bool need_d1, bool fast) {
   if (n <= 0) return;
-  if (need_d1) teacher_stats_kernel<true><<<n, ROW_THREADS, 0, stream>>>(teacher, ld, is_bf16, v, inv_t, rec);
-  else teacher_stats_kernel<false><<<n, ROW_THREADS, 0, stream>>>(teacher, ld, is_bf16, v, inv_t, rec);
+  if (need_d1 && fast) teacher_stats_kernel<true, true><<<n, ROW_THREADS, 0, stream>>>(teacher, ld, is_bf16, v, inv_t, rec);
+  else if (need_d1) teacher_stats_kernel<true, false><<<n, ROW_THREADS, 0, stream>>>(teacher, ld, is_bf16, v, inv_t, rec);
+  else if (fast) teacher_stats_kernel<false, true><<<n, ROW_THREADS, 0, stream>>>(teacher, ld, is_bf16, v, inv_t, rec);
+  else teacher_stats_kernel<false, false><<<n, ROW_THREADS, 0, stream>>>(teacher, ld, is_bf16, v, inv_t, rec);
+}
+
+void launch_label_logits(const void* h, long long ldh, const void* w, long long ldw, long long k,
+                         const int64_t* labels, long long n, long long v0, long long v_rows, int64_t ignore_index,
+                         float* out, cudaStream_t stream) {
+  if (n <= 0) return;
+  label_logit_kernel<<<static_cast<unsigned>((n + 7) / 8), 256, 0, stream>>>(
+      static_cast<const uint16_t*>(h), ldh, static_cast<const uint16_t*>(w), ldw, k, labels, n, v0, v_rows,
+      ignore_index, out);
 }
 
 void launch_label_prep(const int64_t* labels, long long bt, long long v, int64_t ignore_index, int reduction_sum,

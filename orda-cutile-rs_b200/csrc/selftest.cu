@@ -1,4 +1,5 @@
-// selftest.cu -- exercises the bounded-wait machinery on the device.
+// selftest.cu -- device self-tests: the bounded-wait machinery, and the two
+// exp2 implementations the kernels use (for accuracy tests against float64).
 //
 // One warp initialises an mbarrier that nothing ever arrives on and waits on
 // it with the same bounded wait the GEMM roles use, but with a short limit.
@@ -7,7 +8,10 @@
 // the context stays usable. No fault, trap or unbounded spin is involved.
 #include <cuda_runtime.h>
 
+#include <algorithm>
+
 #include "../../include/orda.h"
+#include "fastmath.cuh"
 #include "host_logic.h"
 #include "ptx.cuh"
 
@@ -25,6 +29,18 @@ __global__ void bounded_wait_selftest_kernel(int* status, uint64_t limit_ns) {
   mbar_wait(&bar, 0, status, DEV_TIMEOUT_SELFTEST, limit_ns);
 }
 
+// y_fma[i] = exp2_fma(x[i]) (FMA pipe), y_sfu[i] = ex2.approx.ftz (SFU).
+__global__ void exp2_selftest_kernel(const float* x, float* y_fma, float* y_sfu, long long n) {
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const float v = x[i];
+    float s;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(s) : "f"(v));
+    y_fma[i] = exp2_fma(v);
+    y_sfu[i] = s;
+  }
+}
+
 }  // namespace
 
 cudaError_t launch_bounded_wait_selftest(int* status, uint64_t limit_ns, cudaStream_t stream) {
@@ -33,3 +49,21 @@ cudaError_t launch_bounded_wait_selftest(int* status, uint64_t limit_ns, cudaStr
 }
 
 }  // namespace orda
+
+extern "C" int orda_selftest_exp2(const float* x, float* y_fma, float* y_sfu, size_t n, void* stream, char* err,
+                                  size_t err_len) {
+  if (!x || !y_fma || !y_sfu) {
+    orda::set_error(err, err_len, "null argument");
+    return ORDA_ERR_INVALID;
+  }
+  if (n == 0) return ORDA_OK;
+  const long long blocks = std::min<long long>((static_cast<long long>(n) + 255) / 256, 148 * 8);
+  orda::exp2_selftest_kernel<<<static_cast<unsigned>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      x, y_fma, y_sfu, static_cast<long long>(n));
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    orda::set_error(err, err_len, "CUDA error in the exp2 self-test: %s", cudaGetErrorString(e));
+    return ORDA_ERR_CUDA;
+  }
+  return ORDA_OK;
+}

@@ -484,3 +484,84 @@ def test_host_entry_slab_pipeline_matches_oracle(ob, oracle, quantize):
     else:
         assert rel_l2(piped.grad_weight.a, whole.grad_weight.a) < 1e-5
     assert_parity(piped, oracle.distillation_loss(s, w, labs, t, opts, nthreads=NT), "pipelined")
+
+
+# ------------------------------------------------------------ Profile::Fast
+
+# Stated tolerances of Profile::Fast (include/orda.h, OrdaProfile): the CE
+# terms come from the fp32 statistics and exact label logits (as Balanced);
+# the KL cross term and the logit gradients read fp16 logits.
+FAST_CE_RTOL = 1e-4
+FAST_KL_RTOL = 1e-3
+FAST_GRAD_REL_L2 = 2e-2
+
+
+def assert_parity_fast(gpu, ref, what=""):
+    for name, tol in (("student_ce", FAST_CE_RTOL), ("teacher_ce", FAST_CE_RTOL), ("kl", FAST_KL_RTOL),
+                      ("loss", FAST_KL_RTOL)):
+        a, b = getattr(gpu, name), getattr(ref, name)
+        assert abs(a - b) <= tol * abs(b) + LOSS_ATOL, f"{what} {name}: gpu {a!r} ref {b!r}"
+    for name in ("grad_student_hidden", "grad_weight", "grad_teacher_hidden", "grad_teacher_weight"):
+        a, b = getattr(gpu, name), getattr(ref, name)
+        assert (a is None) == (b is None), f"{what} {name} presence differs"
+        if a is not None:
+            e = rel_l2(a.a, b.a)
+            assert e <= FAST_GRAD_REL_L2, f"{what} {name}: rel L2 {e:.3e}"
+    assert gpu.chunk_plan == ref.chunk_plan
+
+
+@pytest.mark.parametrize("case", ["tied", "separate", "precomputed", "large_logits", "odd_vocab"])
+def test_fast_profile_matches_oracle_and_differs_from_balanced(ob, oracle, case):
+    """Profile::Fast (config.rs:35-42, 81-93): fp16 logits storage, exact label
+    logits, exp2 split between SFU and FMA pipe; within its stated
+    tolerances of the oracle, and not byte-identical to Balanced."""
+    gen = torch.Generator().manual_seed(sum(map(ord, case)) + 1)
+    bt, h, ht_, v = 96, 256, 192, 4096
+    w_std, h_std = 0.05, 1.0
+    if case == "large_logits":
+        w_std, h_std = 0.25, 2.0
+    if case == "odd_vocab":
+        v = 1001
+    s = randn_mat(ob, bt, h, gen, h_std)
+    w = randn_mat(ob, v, h, gen, w_std)
+    labs = torch.randint(0, v, (bt,), generator=gen).tolist()
+    labs[7] = -100
+    kw = dict(kd_weight=0.4, temperature=1.5, label_smoothing=0.05)
+    if case == "separate":
+        t = ob.Teacher.Separate(randn_mat(ob, bt, ht_, gen), randn_mat(ob, v, ht_, gen, 0.05))
+        kw["teacher_ce_weight"] = 0.5
+    elif case == "precomputed":
+        t = ob.Teacher.Precomputed(ob.Mat.from_array((np.sqrt(2.0) * torch.randn(bt, v, generator=gen)).numpy()))
+        kw["teacher_ce_weight"] = 0.3
+    else:
+        t = ob.Teacher.Tied(randn_mat(ob, bt, h, gen, h_std))
+    fast = ob.LossOptions(config=ob.KernelConfig.from_profile(ob.Profile.Fast), **kw)
+    bal = ob.LossOptions(**kw)
+    assert fast.config.fast_math and not bal.config.fast_math
+    g = ob.distillation_loss(s, w, labs, t, fast)
+    r = oracle.distillation_loss(s, w, labs, t, fast, nthreads=NT)
+    assert_parity_fast(g, r, case)
+    b = ob.distillation_loss(s, w, labs, t, bal)
+    assert not np.array_equal(g.grad_weight.a, b.grad_weight.a)
+    # the CE terms share Balanced's fp32 statistics and exact label logits
+    assert abs(g.student_ce - b.student_ce) <= 1e-6 * abs(b.student_ce) + 1e-7
+
+
+def test_exp2_fma_accuracy_on_device(ob):
+    """The Fast profile's FMA-pipe exp2 against float64 2^x over its range
+    [-125, 126]: within 2 ulp (the SFU's ex2.approx is reported beside it)."""
+    from orda_b200 import _abi
+
+    lib = ob.load_library()
+    x = torch.cat([torch.linspace(-125.0, 126.0, 1 << 20), torch.rand(1 << 20) * -40.0,
+                   torch.arange(-125, 126, dtype=torch.float32) + 0.5]).cuda()
+    yf, ys = torch.empty_like(x), torch.empty_like(x)
+    buf = _abi.err_buf()
+    rc = lib.orda_selftest_exp2(x.data_ptr(), yf.data_ptr(), ys.data_ptr(), x.numel(),
+                                torch.cuda.current_stream().cuda_stream, buf, len(buf))
+    assert rc == 0, buf.value
+    torch.cuda.synchronize()
+    ref = torch.exp2(x.double())
+    ef = ((yf.double() / ref) - 1.0).abs().max().item()
+    es = ((ys.double() / ref) - 1.0).abs().max().item()
+    assert ef < 2 * 2.0 ** -23, (ef, es)
