@@ -715,8 +715,8 @@ def run_ours(args):
 
 
 def run_c4_fast(torch, ob, D, ctx, hs, w, tl, labels, ref_out, stream, args, raw_gw):
-    """Profile::Fast (fp16 logits storage, exact label logits, exp2 split
-    between SFU and FMA pipe) on the c4 workload: timing and roofline as the
+    """Profile::Fast (fp16 logits storage, exact label logits, a quarter of
+    the logits epilogue's tempered exp2 on the FMA pipe) on the c4 workload: timing and roofline as the
     headline, and its agreement with the Balanced call of the timed steps
     (scalars, grad_hidden; grad_W before the INT8 round trip). The Fast
     tolerances against the reference are stated in include/orda.h."""

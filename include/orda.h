@@ -85,8 +85,9 @@ typedef enum OrdaBackend { ORDA_BACKEND_AUTO = 0, ORDA_BACKEND_CPU = 1, ORDA_BAC
 /* `Profile` (src/config.rs:35-42). Fast (KernelConfig.fast_math = 1) stores
  * the logits of the forward group as fp16 (saturated to the largest finite
  * value) instead of fp32, takes the label logits of the losses from an exact
- * fp32 dot product, and computes part of the exp2 work on the FMA pipe
- * (exp2 by range reduction and a degree-6 polynomial). The softmax statistics
+ * fp32 dot product, and computes a quarter of the logits epilogue's
+ * tempered-sum exp2 on the FMA pipe (range reduction and a degree-6
+ * polynomial). The softmax statistics
  * still come from the fp32 GEMM accumulators, so the CE terms are as precise
  * as with Balanced; the KL cross term and the logit gradients read the fp16
  * logits. Stated tolerances against the reference: student and teacher CE

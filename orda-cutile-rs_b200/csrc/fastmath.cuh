@@ -1,10 +1,13 @@
 // fastmath.cuh -- 2^x on the FMA pipe, for the Fast profile.
 //
-// The SFU (MUFU ex2) issues 16 results per SM cycle; the row kernels and the
-// logits epilogue need one to three exp2 per logit, which makes the SFU a
-// co-bound with HBM once logits are stored in 16 bits. exp2_fma computes 2^x
-// with FMA-pipe instructions only, so a kernel can split its exp2 work
-// between the two pipes.
+// The SFU (MUFU ex2) delivers 16 results per SM cycle for one issue slot
+// each; exp2_fma computes 2^x with about ten FMA-pipe instructions, i.e. ten
+// issue slots (128 thread-instructions per SM cycle). Moving exp2 work to it
+// pays only where the SFU bounds a loop and issue slots are spare: in the
+// logits GEMM epilogue (two exp2 and about eight other instructions per
+// element) a quarter of one sum goes to it under the Fast profile; the row
+// kernels, already balanced between SFU and issue, measured 23 % slower with
+// half their exp2 moved, and keep the SFU.
 //
 // Method (Cody and Waite's argument reduction, "Software Manual for the
 // Elementary Functions", 1980): x = n + f with n = rint(x), f = x - n in

@@ -172,8 +172,11 @@ __device__ __forceinline__ float max32(const float (&v)[32]) {
 }
 
 // Online-softmax statistics of one 32-column chunk of one row. FULL: all 32
-// columns valid (no per-element masking). POLY (Fast profile): the tempered
-// sum's exp2 on the FMA pipe (exp2_fma), the other on the SFU.
+// columns valid (no per-element masking). POLY (Fast profile): one column in
+// four of the tempered sum takes its exp2 from the FMA pipe (exp2_fma). With
+// two exp2 and about eight other instructions per element the SFU (16 per
+// SM-cycle) bounds this code; the ten-instruction polynomial on a quarter of
+// one of the sums balances the SFU against the issue slots.
 template <bool FULL, bool OWN_DT, bool POLY>
 __device__ __forceinline__ void logits_chunk(const EpiArgs& e, long long grow, bool row_ok, int col0, int nvalid,
                                              const uint32_t (&r)[32], OwnStats& os) {
@@ -195,7 +198,7 @@ __device__ __forceinline__ void logits_chunk(const EpiArgs& e, long long grow, b
     if (FULL || j < nvalid) {
       const float u = v[j] - m_new;
       a1[j & 3] += fast_exp2(u * LOG2E);
-      if (OWN_DT) aT[j & 3] += POLY ? exp2_fma(u * lt) : fast_exp2(u * lt);
+      if (OWN_DT) aT[j & 3] += (POLY && (j & 3) == 3) ? exp2_fma(u * lt) : fast_exp2(u * lt);
       ax[j & 3] += v[j];
     }
   }

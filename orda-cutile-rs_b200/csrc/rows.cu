@@ -27,7 +27,6 @@
 #include <cmath>
 #include <cstdint>
 
-#include "fastmath.cuh"
 #include "kernels.h"
 #include "ptx.cuh"
 
@@ -310,16 +309,16 @@ struct GradScalars {
 
 // One element: the student (and teacher) logit gradient and the KL cross
 // term p_t^T (t - x) / T.
-// FAST: the student's tempered probability on the FMA pipe (exp2_fma), the
-// other exp2 on the SFU.
-template <bool KL, bool TGRAD, bool FAST>
+// All exp2 on the SFU: with about 20 other instructions per element this
+// kernel keeps the SFU and the issue slots about equally busy, and the FMA
+// polynomial (about 10 issue slots per exp2) would make it issue-bound.
+template <bool KL, bool TGRAD>
 __device__ __forceinline__ void grad_elem(const GradScalars& g, const RowConst& c, int j, float x, float t, float& gs,
                                           float& gt, float& cross) {
   float s = g.ws * (fast_exp2(fmaf(x, g.l1, -c.c_s1)) - g.eps);
   if (KL) {
     const float pt = fast_exp2(fmaf(t, g.lT, -c.c_tT));
-    const float ps = FAST ? exp2_fma(fmaf(x, g.lT, -c.c_sT)) : fast_exp2(fmaf(x, g.lT, -c.c_sT));
-    s += g.kdT * (ps - pt);
+    s += g.kdT * (fast_exp2(fmaf(x, g.lT, -c.c_sT)) - pt);
     cross = fmaf(pt, (t - x) * g.inv_t, cross);
   }
   if (j == c.y) s -= g.ws_tgt;
@@ -379,8 +378,7 @@ __device__ __forceinline__ float block_sum_f(float v, float* sh) {
 // ---- grid (row, segment): gradients of one 8192-column segment of one row
 // (rows on grid x, which has no 65535 limit).
 // VEC: V % 8 == 0 and 16-byte aligned rows (8 columns per thread step).
-// FAST (Fast profile): fp16 student logits, part of the exp2 work on the FMA
-// pipe.
+// FAST (Fast profile): fp16 student logits (half the bytes of the pass).
 template <bool VEC, bool KL, bool TGRAD, bool FAST>
 __global__ void __launch_bounds__(GRAD_THREADS) row_grad_kernel(const RowArgs a, const GradScalars g) {
   __shared__ float sh[GRAD_THREADS / 32];
@@ -429,7 +427,7 @@ __global__ void __launch_bounds__(GRAD_THREADS) row_grad_kernel(const RowArgs a,
         if (need_t) load_teacher8(a.teacher, a.teacher_dtype, row * a.ld_teacher + j0, t);
         float gsv[8], gtv[8];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) grad_elem<KL, TGRAD, FAST>(g, c, j0 + k, x[k], t[k], gsv[k], gtv[k], cross);
+        for (int k = 0; k < 8; ++k) grad_elem<KL, TGRAD>(g, c, j0 + k, x[k], t[k], gsv[k], gtv[k], cross);
         *reinterpret_cast<uint4*>(gs_row + j0) = make_uint4(pack_bf16x2(gsv[0], gsv[1]), pack_bf16x2(gsv[2], gsv[3]),
                                                             pack_bf16x2(gsv[4], gsv[5]), pack_bf16x2(gsv[6], gsv[7]));
         if (TGRAD)
@@ -444,7 +442,7 @@ __global__ void __launch_bounds__(GRAD_THREADS) row_grad_kernel(const RowArgs a,
       if (need_t) t = logit_at(a.teacher, a.teacher_dtype, row * a.ld_teacher + j);
       const float x = FAST ? __half2float(xh[j]) : xs[j];
       float gs, gt;
-      grad_elem<KL, TGRAD, FAST>(g, c, j, x, t, gs, gt, cross);
+      grad_elem<KL, TGRAD>(g, c, j, x, t, gs, gt, cross);
       gs_row[j] = __bfloat16_as_ushort(__float2bfloat16_rn(gs));
       if (TGRAD) gt_row[j] = __bfloat16_as_ushort(__float2bfloat16_rn(gt));
     }
@@ -465,8 +463,9 @@ __device__ __forceinline__ float teacher_at(const void* teacher, int is_bf16, lo
 // sums cost one exp2 each per element on the SFU, which bounds this kernel
 // before HBM does: NEED_D1 = false (no teacher CE term) skips sum e^(t-m)
 // and records d1 = 1.
-// FAST: the tempered sum of every other vector of 8 on the FMA pipe
-// (exp2_fma), the rest on the SFU.
+// FAST selects the same arithmetic (the exp2 work stays on the SFU: with
+// one exp2 and about six other instructions per element, moving any of it to
+// the ten-instruction FMA polynomial costs more issue slots than it frees).
 template <bool NEED_D1, bool FAST>
 __global__ void __launch_bounds__(ROW_THREADS) teacher_stats_kernel(const void* teacher, long long ld, int is_bf16,
                                                                     int v, float inv_t, float* rec) {
@@ -508,7 +507,7 @@ __global__ void __launch_bounds__(ROW_THREADS) teacher_stats_kernel(const void* 
           if (t[u][k] != -INFINITY) {
             const float x = t[u][k] - m;
             if (NEED_D1) d1 += fast_exp2(x * LOG2E_F);
-            dT += (FAST && (u & 1)) ? exp2_fma(x * lt) : fast_exp2(x * lt);
+            dT += fast_exp2(x * lt);
             sx += t[u][k];
           }
         }

@@ -513,7 +513,7 @@ def assert_parity_fast(gpu, ref, what=""):
 @pytest.mark.parametrize("case", ["tied", "separate", "precomputed", "large_logits", "odd_vocab"])
 def test_fast_profile_matches_oracle_and_differs_from_balanced(ob, oracle, case):
     """Profile::Fast (config.rs:35-42, 81-93): fp16 logits storage, exact label
-    logits, exp2 split between SFU and FMA pipe; within its stated
+    logits, part of the epilogue's exp2 on the FMA pipe; within its stated
     tolerances of the oracle, and not byte-identical to Balanced."""
     gen = torch.Generator().manual_seed(sum(map(ord, case)) + 1)
     bt, h, ht_, v = 96, 256, 192, 4096
