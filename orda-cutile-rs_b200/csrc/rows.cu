@@ -463,12 +463,13 @@ __device__ __forceinline__ float teacher_at(const void* teacher, int is_bf16, lo
 // sums cost one exp2 each per element on the SFU, which bounds this kernel
 // before HBM does: NEED_D1 = false (no teacher CE term) skips sum e^(t-m)
 // and records d1 = 1.
-// FAST selects the same arithmetic (the exp2 work stays on the SFU: with
-// one exp2 and about six other instructions per element, moving any of it to
-// the ten-instruction FMA polynomial costs more issue slots than it frees).
-template <bool NEED_D1, bool FAST>
-__global__ void __launch_bounds__(ROW_THREADS) teacher_stats_kernel(const void* teacher, long long ld, int is_bf16,
-                                                                    int v, float inv_t, float* rec) {
+// The exp2 work stays on the SFU in every profile (FAST is unused): with one
+// exp2 and about six other instructions per element, moving any of it to the
+// ten-instruction FMA polynomial costs more issue slots than it frees. BF16:
+// the teacher logits are bf16 (else fp32).
+template <bool NEED_D1, bool FAST, bool BF16>
+__global__ void __launch_bounds__(ROW_THREADS, 3) teacher_stats_kernel(const void* teacher, long long ld, int is_bf16,
+                                                                       int v, float inv_t, float* rec) {
   __shared__ double sh[3 * 32];
   const long long row = blockIdx.x;
   const bool vec = (v % 8 == 0) && ((ld * (is_bf16 ? 2 : 4)) % 16 == 0) &&
@@ -476,14 +477,44 @@ __global__ void __launch_bounds__(ROW_THREADS) teacher_stats_kernel(const void* 
   const float lt = LOG2E_F * inv_t;
   float m = -INFINITY, d1 = 0.f, dT = 0.f, sx = 0.f;
   if (vec) {
-    constexpr int U = 4;  // vectors of 8 per thread per iteration
-    for (int base = threadIdx.x * 8; base < v; base += ROW_THREADS * 8 * U) {
-      float t[U][8];
+    // U vectors of 8 per thread per iteration; the next iteration's raw
+    // 16-byte words are loaded before the current ones are reduced, so the
+    // loads of two iterations are in flight (the reduction would otherwise
+    // leave the memory pipe idle between iterations)
+    constexpr int U = 4;
+    constexpr int STEP = ROW_THREADS * 8 * U;
+    constexpr int NW = BF16 ? 1 : 2;  // 16-byte words per vector of 8
+    const uint4* src = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(teacher) +
+                                                      row * ld * (BF16 ? 2 : 4));
+    auto fetch = [&](int base, uint4 (&r)[U][NW]) {
 #pragma unroll
       for (int u = 0; u < U; ++u) {
         const int j0 = base + u * ROW_THREADS * 8;
         if (j0 < v) {
-          load_teacher8(teacher, is_bf16 ? kLogitBF16 : kLogitF32, row * ld + j0, t[u]);
+#pragma unroll
+          for (int q = 0; q < NW; ++q) r[u][q] = __ldg(src + static_cast<long long>(j0) * NW / 8 + q);
+        }
+      }
+    };
+    uint4 cur[U][NW], nxt[U][NW];
+    fetch(threadIdx.x * 8, cur);
+    for (int base = threadIdx.x * 8; base < v; base += STEP) {
+      if (base + STEP < v) fetch(base + STEP, nxt);
+      float t[U][8];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        if (base + u * ROW_THREADS * 8 < v) {
+          const uint4 a = cur[u][0];
+          if constexpr (BF16) {
+            t[u][0] = bf16_lo(a.x); t[u][1] = bf16_hi(a.x); t[u][2] = bf16_lo(a.y); t[u][3] = bf16_hi(a.y);
+            t[u][4] = bf16_lo(a.z); t[u][5] = bf16_hi(a.z); t[u][6] = bf16_lo(a.w); t[u][7] = bf16_hi(a.w);
+          } else {
+            const uint4 b = cur[u][NW - 1];
+            t[u][0] = __uint_as_float(a.x); t[u][1] = __uint_as_float(a.y);
+            t[u][2] = __uint_as_float(a.z); t[u][3] = __uint_as_float(a.w);
+            t[u][4] = __uint_as_float(b.x); t[u][5] = __uint_as_float(b.y);
+            t[u][6] = __uint_as_float(b.z); t[u][7] = __uint_as_float(b.w);
+          }
         } else {
 #pragma unroll
           for (int k = 0; k < 8; ++k) t[u][k] = -INFINITY;
@@ -511,6 +542,10 @@ __global__ void __launch_bounds__(ROW_THREADS) teacher_stats_kernel(const void* 
             sx += t[u][k];
           }
         }
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+#pragma unroll
+        for (int q = 0; q < NW; ++q) cur[u][q] = nxt[u][q];
     }
   } else {
     for (int j = threadIdx.x; j < v; j += ROW_THREADS) m = fmaxf(m, teacher_at(teacher, is_bf16, row * ld + j));
@@ -745,10 +780,12 @@ void launch_row_grad(const RowArgs& a, cudaStream_t stream) {
 void launch_teacher_stats(const void* teacher, long long ld, int is_bf16, int n, int v, float inv_t, float* rec,
                           cudaStream_t stream, bool need_d1, bool fast) {
   if (n <= 0) return;
-  if (need_d1 && fast) teacher_stats_kernel<true, true><<<n, ROW_THREADS, 0, stream>>>(teacher, ld, is_bf16, v, inv_t, rec);
-  else if (need_d1) teacher_stats_kernel<true, false><<<n, ROW_THREADS, 0, stream>>>(teacher, ld, is_bf16, v, inv_t, rec);
-  else if (fast) teacher_stats_kernel<false, true><<<n, ROW_THREADS, 0, stream>>>(teacher, ld, is_bf16, v, inv_t, rec);
-  else teacher_stats_kernel<false, false><<<n, ROW_THREADS, 0, stream>>>(teacher, ld, is_bf16, v, inv_t, rec);
+  (void)fast;  // the Fast profile keeps this kernel's arithmetic (see teacher_stats_kernel)
+  auto go = [&](auto kern) { kern<<<n, ROW_THREADS, 0, stream>>>(teacher, ld, is_bf16, v, inv_t, rec); };
+  if (need_d1 && is_bf16) go(teacher_stats_kernel<true, false, true>);
+  else if (need_d1) go(teacher_stats_kernel<true, false, false>);
+  else if (is_bf16) go(teacher_stats_kernel<false, false, true>);
+  else go(teacher_stats_kernel<false, false, false>);
 }
 
 void launch_label_logits(const void* h, long long ldh, const void* w, long long ldw, long long k,
