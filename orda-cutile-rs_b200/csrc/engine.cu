@@ -57,6 +57,13 @@ struct OrdaContext {
   cudaStream_t own_stream = nullptr;  // host-Mat entry: compute stream
   cudaStream_t copy_in = nullptr;     // host-Mat entry: host->device copies
   cudaStream_t copy_out = nullptr;    // host-Mat entry: device->host copies
+  // Concurrency of bandwidth-bound kernels with the tensor-bound GEMMs: the
+  // persistent GEMM grid leaves `spare_sms` SMs free and the teacher
+  // statistics (during the logits GEMM) and the INT8 quantiser (during
+  // dgrad) run on the low-priority auxiliary stream. 0 = serial.
+  int spare_sms = 4;
+  cudaStream_t aux_stream = nullptr;
+  cudaEvent_t aux_ev[3] = {nullptr, nullptr, nullptr};
   std::mutex mu;
   // phase timing (see orda_context_enable_timing)
   bool timing = false;
@@ -325,6 +332,23 @@ WireSlots wire_slots(const OrdaContext* ctx) {
   return w;
 }
 
+// The auxiliary stream (lowest priority, so the GEMM's CTAs are placed
+// first) and its dependency events; created on first use.
+cudaError_t aux_init(OrdaContext* ctx) {
+  if (ctx->aux_stream) return cudaSuccess;
+  int least = 0, greatest = 0;
+  cudaError_t e = cudaDeviceGetStreamPriorityRange(&least, &greatest);
+  if (e == cudaSuccess) e = cudaStreamCreateWithPriority(&ctx->aux_stream, cudaStreamNonBlocking, least);
+  for (int i = 0; i < 3 && e == cudaSuccess; ++i) e = cudaEventCreateWithFlags(&ctx->aux_ev[i], cudaEventDisableTiming);
+  return e;
+}
+
+// `to` waits for the work queued on `from` so far (through event ev).
+cudaError_t stream_after(cudaStream_t to, cudaStream_t from, cudaEvent_t ev) {
+  cudaError_t e = cudaEventRecord(ev, from);
+  return e == cudaSuccess ? cudaStreamWaitEvent(to, ev, 0) : e;
+}
+
 // Rows of this rank's slice (the last owner may hold fewer than slot_slice).
 long long slot_rows_mine(const OrdaContext* ctx) {
   const long long r0 = static_cast<long long>(ctx->slot_rank) * ctx->slot_slice;
@@ -533,6 +557,7 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
   const size_t fwd_rows = L.fwd_rows;
   const size_t group_rows = L.group_rows;
   const size_t t_esz = in.t_logits_bf16 ? 2 : 4;
+  bool quant_async = false;  // the INT8 round trip was queued on the auxiliary stream
   for (size_t g0 = 0; g0 < bt; g0 += group_rows) {
     const size_t g1 = std::min(g0 + group_rows, bt);
     for (size_t s = g0; s < g1; s += fwd_rows) {
@@ -543,6 +568,20 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
       const long long t_ld = live_teacher ? static_cast<long long>(L.ldv) : in.ld_t_logits;
       const int t_bf16 = live_teacher ? 0 : static_cast<int>(in.t_logits_bf16);
       const int t_dtype = live_teacher ? (f.fast ? kLogitF16 : kLogitF32) : (in.t_logits_bf16 ? kLogitBF16 : kLogitF32);
+      // given teacher logits: their statistics run on the auxiliary stream
+      // while the logits GEMM runs on all SMs but spare_sms
+      const bool conc_t = ctx->spare_sms > 0 && vphase != 2 && f.need_teacher && !live_teacher && !hp;
+      if (conc_t) {
+        if ((e = aux_init(ctx)) != cudaSuccess) return cuda_fail(e, "auxiliary stream", err, len);
+        if ((e = stream_after(ctx->aux_stream, st, ctx->aux_ev[0])) != cudaSuccess)
+          return cuda_fail(e, "event", err, len);
+        Phase ph_t(ctx, 1, ctx->aux_stream);
+        ph_t.launched();
+        launch_teacher_stats(t_rows, t_ld, t_bf16, static_cast<int>(n), static_cast<int>(v), inv_t, rec_own_t,
+                             ctx->aux_stream, f.teacher_ce, f.fast);
+        if ((e = cudaEventRecord(ctx->aux_ev[1], ctx->aux_stream)) != cudaSuccess)
+          return cuda_fail(e, "event", err, len);
+      }
       if (vphase != 2) {
         Phase ph_fwd(ctx, 0, st);
         // ---- teacher logits + statistics (Tied / Separate)
@@ -585,6 +624,7 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
         gd.status = status;
         gd.args.logits = logits;
         gd.args.logits_f16 = f.fast;
+        gd.spare_sms = conc_t ? ctx->spare_sms : 0;
         gd.args.ldl = static_cast<long long>(L.ldv);
         gd.args.rec_own = rec_own;
         gd.args.n_parts = static_cast<int>(L.parts);
@@ -602,7 +642,9 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
       }
       {
         Phase ph_rows(ctx, 1, st);
-        if (vphase != 2 && f.need_teacher && !live_teacher) {
+        if (conc_t) {
+          if ((e = cudaStreamWaitEvent(st, ctx->aux_ev[1], 0)) != cudaSuccess) return cuda_fail(e, "event", err, len);
+        } else if (vphase != 2 && f.need_teacher && !live_teacher) {
           ph_rows.launched();
           launch_teacher_stats(t_rows, t_ld, t_bf16, static_cast<int>(n), static_cast<int>(v), inv_t, rec_own_t, st,
                                f.teacher_ce, f.fast);
@@ -676,6 +718,85 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
     if (vphase == 1) continue;  // the backward phase follows the exchange of the partials
     const long long rows_g = static_cast<long long>(g1 - g0);
     const long long vv = static_cast<long long>(v);
+    // Last backward group with the INT8 round trip: wgrad first, then the
+    // quantiser on the auxiliary stream while dgrad runs on all SMs but
+    // spare_sms (dgrad does not touch grad_W; the order of the two GEMMs does
+    // not change any result).
+    const bool conc_q = ctx->spare_sms > 0 && f.quant && g1 == bt && !hp;
+    auto do_wgrad = [&]() -> int {
+      // ---- wgrad: grad_W (+)= mean_scale * dlogits^T @ hidden
+      {
+        Phase ph(ctx, 3, st);
+        int nl = 0;  // the GEMM and, with an L2 carve-out, the demotion kernel
+        GemmDesc gd;
+        gd.a_mn_major = true;
+        gd.b_mn_major = true;
+        gd.a[0] = MatRef{dlog_s, rows_g, vv, static_cast<long long>(L.ldd)};
+        gd.b[0] = MatRef{static_cast<const uint16_t*>(in.hs.ptr) + g0 * in.hs.ld, rows_g, static_cast<long long>(h),
+                         in.hs.ld};
+        gd.k_seg[0] = rows_g;
+        if (f.teacher_grad && in.mode == ORDA_TEACHER_TIED) {
+          gd.nseg = 2;
+          gd.a[1] = MatRef{dlog_t, rows_g, vv, static_cast<long long>(L.ldd)};
+          gd.b[1] = MatRef{static_cast<const uint16_t*>(in.ht.ptr) + g0 * in.ht.ld, rows_g, static_cast<long long>(h),
+                           in.ht.ld};
+          gd.k_seg[1] = rows_g;
+        }
+        gd.M = vv;
+        gd.N = static_cast<long long>(h);
+        gd.raster_n_fastest = true;
+        gd.status = status;
+        if (wire) {
+          // INT8 wire: the local fp32 partial first (quantised into the owners'
+          // slots once complete)
+          gd.args.out0 = ctx->wire_local;
+          gd.args.ld0 = static_cast<long long>(h);
+        } else if (scatter) {
+          // each owner's rows go straight to its slot buffer: the reduce-scatter
+          // transfer overlaps this GEMM
+          gd.args.scatter = 1;
+          gd.args.slot_rank = ctx->slot_rank;
+          gd.args.slot_slice = ctx->slot_slice;
+          gd.args.slot_ld = ctx->slot_h;
+          for (int r = 0; r < kMaxSlotRanks; ++r) gd.args.slot[r] = ctx->slot_peer[r];
+        } else {
+          gd.args.out0 = out.grad_weight;
+          gd.args.ld0 = static_cast<long long>(out.ld_grad_weight);
+        }
+        gd.args.alpha_ptr = ctx->d_mean_scale;
+        gd.args.beta = g0 > 0 ? 1.0f : 0.0f;
+        gd.demote_kept = ctx->l2_set;
+        gd.launches = &nl;
+        if ((e = gemm_launch(gd, ctx->num_sms, st, &why)) != cudaSuccess)
+          return cuda_fail(e, why ? why : "wgrad GEMM", err, len);
+        ph.launched(nl);
+      }
+      if (f.teacher_grad && in.mode == ORDA_TEACHER_SEPARATE) {
+        Phase ph(ctx, 3, st);
+        int nl = 0;  // the GEMM and, with an L2 carve-out, the demotion kernel
+        GemmDesc gd;
+        gd.a_mn_major = true;
+        gd.b_mn_major = true;
+        gd.a[0] = MatRef{dlog_t, rows_g, vv, static_cast<long long>(L.ldd)};
+        gd.b[0] = MatRef{static_cast<const uint16_t*>(in.ht.ptr) + g0 * in.ht.ld, rows_g, static_cast<long long>(ht),
+                         in.ht.ld};
+        gd.k_seg[0] = rows_g;
+        gd.M = vv;
+        gd.N = static_cast<long long>(ht);
+        gd.raster_n_fastest = true;
+        gd.status = status;
+        gd.args.out0 = out.grad_teacher_weight;
+        gd.args.ld0 = static_cast<long long>(out.ld_grad_teacher_weight);
+        gd.args.alpha_ptr = ctx->d_mean_scale;
+        gd.args.beta = g0 > 0 ? 1.0f : 0.0f;
+        gd.demote_kept = ctx->l2_set;
+        gd.launches = &nl;
+        if ((e = gemm_launch(gd, ctx->num_sms, st, &why)) != cudaSuccess)
+          return cuda_fail(e, why ? why : "teacher wgrad GEMM", err, len);
+        ph.launched(nl);
+      }
+      return ORDA_OK;
+    };
     // ---- dgrad: grad_h rows = mean_scale * dlogits @ W
     auto dgrad = [&](const uint16_t* dl, const MatRef& wmat, long long ncols, float* outp, size_t ldo,
                      int copy) -> int {
@@ -690,6 +811,7 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
       gd.N = ncols;
       gd.raster_n_fastest = true;
       gd.status = status;
+      gd.spare_sms = conc_q ? ctx->spare_sms : 0;
       if (scatter_hidden) {
         // vocabulary-sharded: this rank's partial of every owner's rows goes
         // straight to the owner's slot set `copy` (a reduce-scatter over rows)
@@ -707,6 +829,21 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
       if (ee != cudaSuccess) return cuda_fail(ee, why ? why : "dgrad GEMM", err, len);
       return ORDA_OK;
     };
+    if (conc_q) {
+      if (int rc = do_wgrad()) return rc;
+      if ((e = aux_init(ctx)) != cudaSuccess) return cuda_fail(e, "auxiliary stream", err, len);
+      if ((e = stream_after(ctx->aux_stream, st, ctx->aux_ev[0])) != cudaSuccess)
+        return cuda_fail(e, "event", err, len);
+      Phase ph(ctx, 4, ctx->aux_stream);
+      ph.launched();
+      const uint64_t seed = o.config.has_stochastic_seed ? o.config.stochastic_seed : 0;
+      launch_quant(out.grad_weight, static_cast<long long>(v), static_cast<long long>(h),
+                   static_cast<long long>(out.ld_grad_weight), tflags, o.config.stochastic_rounding, seed,
+                   out.grad_weight_q, out.grad_weight_scale, ctx->aux_stream, vphase == 2 ? vc->v0 : 0);
+      if ((e = cudaEventRecord(ctx->aux_ev[2], ctx->aux_stream)) != cudaSuccess)
+        return cuda_fail(e, "event", err, len);
+      quant_async = true;
+    }
     if (int rc = dgrad(dlog_s, in.w, static_cast<long long>(h), out.grad_student_hidden, out.ld_grad_student_hidden,
                        0))
       return rc;
@@ -718,76 +855,8 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
     if (hp && hp->after_dgrad) {
       if (int rc = hp->after_dgrad(g0, g1)) return rc;
     }
-    // ---- wgrad: grad_W (+)= mean_scale * dlogits^T @ hidden
-    {
-      Phase ph(ctx, 3, st);
-      int nl = 0;  // the GEMM and, with an L2 carve-out, the demotion kernel
-      GemmDesc gd;
-      gd.a_mn_major = true;
-      gd.b_mn_major = true;
-      gd.a[0] = MatRef{dlog_s, rows_g, vv, static_cast<long long>(L.ldd)};
-      gd.b[0] = MatRef{static_cast<const uint16_t*>(in.hs.ptr) + g0 * in.hs.ld, rows_g, static_cast<long long>(h),
-                       in.hs.ld};
-      gd.k_seg[0] = rows_g;
-      if (f.teacher_grad && in.mode == ORDA_TEACHER_TIED) {
-        gd.nseg = 2;
-        gd.a[1] = MatRef{dlog_t, rows_g, vv, static_cast<long long>(L.ldd)};
-        gd.b[1] = MatRef{static_cast<const uint16_t*>(in.ht.ptr) + g0 * in.ht.ld, rows_g, static_cast<long long>(h),
-                         in.ht.ld};
-        gd.k_seg[1] = rows_g;
-      }
-      gd.M = vv;
-      gd.N = static_cast<long long>(h);
-      gd.raster_n_fastest = true;
-      gd.status = status;
-      if (wire) {
-        // INT8 wire: the local fp32 partial first (quantised into the owners'
-        // slots once complete)
-        gd.args.out0 = ctx->wire_local;
-        gd.args.ld0 = static_cast<long long>(h);
-      } else if (scatter) {
-        // each owner's rows go straight to its slot buffer: the reduce-scatter
-        // transfer overlaps this GEMM
-        gd.args.scatter = 1;
-        gd.args.slot_rank = ctx->slot_rank;
-        gd.args.slot_slice = ctx->slot_slice;
-        gd.args.slot_ld = ctx->slot_h;
-        for (int r = 0; r < kMaxSlotRanks; ++r) gd.args.slot[r] = ctx->slot_peer[r];
-      } else {
-        gd.args.out0 = out.grad_weight;
-        gd.args.ld0 = static_cast<long long>(out.ld_grad_weight);
-      }
-      gd.args.alpha_ptr = ctx->d_mean_scale;
-      gd.args.beta = g0 > 0 ? 1.0f : 0.0f;
-      gd.demote_kept = ctx->l2_set;
-      gd.launches = &nl;
-      if ((e = gemm_launch(gd, ctx->num_sms, st, &why)) != cudaSuccess)
-        return cuda_fail(e, why ? why : "wgrad GEMM", err, len);
-      ph.launched(nl);
-    }
-    if (f.teacher_grad && in.mode == ORDA_TEACHER_SEPARATE) {
-      Phase ph(ctx, 3, st);
-      int nl = 0;  // the GEMM and, with an L2 carve-out, the demotion kernel
-      GemmDesc gd;
-      gd.a_mn_major = true;
-      gd.b_mn_major = true;
-      gd.a[0] = MatRef{dlog_t, rows_g, vv, static_cast<long long>(L.ldd)};
-      gd.b[0] = MatRef{static_cast<const uint16_t*>(in.ht.ptr) + g0 * in.ht.ld, rows_g, static_cast<long long>(ht),
-                       in.ht.ld};
-      gd.k_seg[0] = rows_g;
-      gd.M = vv;
-      gd.N = static_cast<long long>(ht);
-      gd.raster_n_fastest = true;
-      gd.status = status;
-      gd.args.out0 = out.grad_teacher_weight;
-      gd.args.ld0 = static_cast<long long>(out.ld_grad_teacher_weight);
-      gd.args.alpha_ptr = ctx->d_mean_scale;
-      gd.args.beta = g0 > 0 ? 1.0f : 0.0f;
-      gd.demote_kept = ctx->l2_set;
-      gd.launches = &nl;
-      if ((e = gemm_launch(gd, ctx->num_sms, st, &why)) != cudaSuccess)
-        return cuda_fail(e, why ? why : "teacher wgrad GEMM", err, len);
-      ph.launched(nl);
+    if (!conc_q) {
+      if (int rc = do_wgrad()) return rc;
     }
   }
   if (wire) {
@@ -817,7 +886,10 @@ int run_device(OrdaContext* ctx, const DevInputs& in, const OrdaLossOptions& o, 
     launch_finalize(nll_s, nll_t, kl_base, s_part, static_cast<int>(L.nseg), t_sq, static_cast<long long>(bt),
                     ctx->d_mean_scale, f.w_s, f.w_t, f.kd, out.scalars, st, vphase == 2 ? vc->include_rows : 1);
   }
-  if (f.quant) {
+  if (quant_async) {
+    // the call ends on `st` after the auxiliary stream's quantiser
+    if ((e = cudaStreamWaitEvent(st, ctx->aux_ev[2], 0)) != cudaSuccess) return cuda_fail(e, "event", err, len);
+  } else if (f.quant) {
     Phase ph(ctx, 4, st);
     ph.launched();
     const uint64_t seed = o.config.has_stochastic_seed ? o.config.stochastic_seed : 0;
@@ -1161,8 +1233,10 @@ void orda_context_destroy(OrdaContext* ctx) {
   cudaFree(ctx->wire_local);
   cudaFree(ctx->d_words);
   cudaFree(ctx->d_mean_scale);
-  for (cudaStream_t sp : {ctx->own_stream, ctx->copy_in, ctx->copy_out})
+  for (cudaStream_t sp : {ctx->own_stream, ctx->copy_in, ctx->copy_out, ctx->aux_stream})
     if (sp) cudaStreamDestroy(sp);
+  for (cudaEvent_t ev : ctx->aux_ev)
+    if (ev) cudaEventDestroy(ev);
   for (auto& pe : ctx->pending) {
     cudaEventDestroy(pe.begin);
     cudaEventDestroy(pe.end);
@@ -1377,6 +1451,10 @@ int orda_gemm_bf16_device(OrdaContext* ctx, const void* a, size_t lda, int a_kin
   if (e != cudaSuccess) return cuda_fail(e, why ? why : "GEMM", err, err_len);
   ctx->last_stream = st;
   return ORDA_OK;
+}
+
+void orda_context_set_concurrency(OrdaContext* ctx, int spare_sms) {
+  if (ctx) ctx->spare_sms = std::max(0, std::min(spare_sms, 32));
 }
 
 void orda_context_enable_timing(OrdaContext* ctx, int enable) {

@@ -89,6 +89,7 @@ struct KParams {
   int tma_store;   // output written through the staging buffers + TMA
   int tma_reduce;  // TMA reduce-add into the output (beta == 1)
   int pol_a, pol_b, pol_c;  // L2 policy kinds (0 normal, 1 evict-first, 2 evict-last)
+  int spare_sms;            // host side: SMs the persistent grid leaves free
   EpiArgs e;
 };
 
@@ -741,6 +742,8 @@ cudaError_t launch_t(const CUtensorMap* maps, const KParams& kp, int num_sms, cu
     }
     if (CG > 1) units = cache.max_clusters[dev];
   }
+  // leave kp.spare_sms SMs to kernels that run concurrently on another stream
+  if (kp.spare_sms > 0) units = std::max(1, units - (kp.spare_sms + CG - 1) / CG);
   if (kp.num_tiles < units) units = kp.num_tiles;
   if (CG == 1) {
     kern<<<units, NUM_THREADS, T::SMEM, stream>>>(maps[0], maps[1], maps[2], maps[3], maps[4], kp);
@@ -811,6 +814,7 @@ cudaError_t gemm_launch(const GemmDesc& d, int num_sms, cudaStream_t stream, con
   kp.raster_n_fastest = d.raster_n_fastest ? 1 : 0;
   kp.nseg = d.nseg;
   kp.status = d.status;
+  kp.spare_sms = d.spare_sms;
   kp.e = d.args;
   long long k_total = 0;
   CUtensorMap maps[5];

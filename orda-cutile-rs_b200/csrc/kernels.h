@@ -71,6 +71,9 @@ struct GemmDesc {
   // they stay pinned and shrink L2 for the kernels that follow).
   bool demote_kept = false;
   int* launches = nullptr;  // if set, incremented by the number of kernels launched
+  // SMs the persistent grid leaves free for a bandwidth-bound kernel that
+  // runs concurrently on another stream (0: the grid covers every SM)
+  int spare_sms = 0;
 };
 
 // Encodes the tensor maps and launches the persistent tcgen05 GEMM.

@@ -56,6 +56,12 @@ class DeviceContext:
         _lib().orda_context_phase_times(self.handle, ms, n)
         return {name: (float(ms[i]), int(n[i])) for i, name in enumerate(_abi.PHASE_NAMES)}
 
+    def set_concurrency(self, spare_sms: int) -> None:
+        """`orda_context_set_concurrency`: SMs the persistent GEMMs leave to the
+        teacher statistics and the INT8 quantiser running beside them on an
+        auxiliary stream (0 = every kernel serial on the caller's stream)."""
+        _lib().orda_context_set_concurrency(self.handle, int(spare_sms))
+
     def launch_count(self) -> int:
         return int(_lib().orda_context_launch_count(self.handle))
 

@@ -247,6 +247,7 @@ extern "C" {
     pub fn orda_context_enable_timing(ctx: *mut OrdaContext, enable: c_int);
     pub fn orda_context_phase_times(ctx: *mut OrdaContext, ms_out: *mut f64, launches_out: *mut u64) -> c_int;
     pub fn orda_context_reset_timing(ctx: *mut OrdaContext);
+    pub fn orda_context_set_concurrency(ctx: *mut OrdaContext, spare_sms: c_int);
     pub fn orda_context_launch_count(ctx: *const OrdaContext) -> u64;
     pub fn orda_context_set_l2_persisting(ctx: *mut OrdaContext, bytes: usize, granted: *mut usize,
                                           err: *mut c_char, err_len: usize) -> c_int;

@@ -565,3 +565,30 @@ def test_exp2_fma_accuracy_on_device(ob):
     ef = ((yf.double() / ref) - 1.0).abs().max().item()
     es = ((ys.double() / ref) - 1.0).abs().max().item()
     assert ef < 2 * 2.0 ** -23, (ef, es)
+
+
+def test_concurrent_schedule_is_bit_identical_to_serial(ob):
+    """orda_context_set_concurrency: teacher statistics beside the logits GEMM
+    and the INT8 round trip beside dgrad (on an auxiliary stream, the GEMMs on
+    all SMs but the spare ones) give the same bits as the serial schedule."""
+    from orda_b200.device import DeviceContext, distillation_loss_device
+
+    gen = torch.Generator(device="cuda").manual_seed(77)
+    bt, h, v = 512, 512, 8192
+    hs = torch.randn(bt, h, generator=gen, device="cuda").bfloat16()
+    w = (0.02 * torch.randn(v, h, generator=gen, device="cuda")).bfloat16()
+    tl = (2.0 ** 0.5 * torch.randn(bt, v, generator=gen, device="cuda")).bfloat16()
+    labels = torch.randint(0, v, (bt,), generator=gen, device="cuda")
+    opts = ob.LossOptions(kd_weight=0.4, temperature=1.5, config=ob.KernelConfig(quantize_grad_weight=True))
+    res = []
+    with DeviceContext(0) as ctx:
+        for spare in (0, 4, 8, 0):
+            ctx.set_concurrency(spare)
+            r = distillation_loss_device(ctx, hs, w, labels, ob.TeacherMode.Precomputed, teacher_logits=tl,
+                                         opts=opts, want_int8=True)
+            torch.cuda.synchronize()
+            ctx.check()
+            res.append(r)
+    for r in res[1:]:
+        for name in ("scalars", "grad_student_hidden", "grad_weight", "grad_weight_q", "grad_weight_scale"):
+            assert torch.equal(getattr(r, name), getattr(res[0], name)), name
