@@ -116,6 +116,49 @@ def balanced_rows(total: int, speeds: list, quantum: int, lo: int, hi: int) -> l
     return [g * quantum for g in got]
 
 
+class RowBalancer:
+    """Feedback load balancing of the global batch (per_rank x world rows)
+    across ranks whose GPUs run at different speeds: power-capped B200s of one
+    node settle at different SM clocks, and with equal row blocks every step
+    waits for the slowest. After each step a rank records the device time of
+    its device entry (CUDA events); `lag` steps later (so reading the events
+    waits for nothing the host still needs to enqueue) the ranks exchange
+    rows / ms over a CPU (gloo) group, smooth it, and give the next step
+    rows in proportion, in whole `quantum`s (the GEMM's M tile, so no rank
+    computes a partly empty tile) within [lo, hi]. Every rank computes the
+    same allocation from the same gathered numbers. The global row count is
+    unchanged; n_global comes from prefix counts exchanged once."""
+
+    def __init__(self, dist, group, world, rank, per_rank, quantum, lo, hi, smoothing=0.5, lag=2):
+        self.dist, self.group, self.world, self.rank = dist, group, world, rank
+        self.total = per_rank * world
+        self.quantum, self.lo, self.hi = quantum, lo, hi
+        self.smoothing, self.lag = smoothing, lag
+        self.rows = [per_rank] * world
+        self.speed = None
+        self.pending = []
+        self.history = []
+
+    def mine(self):
+        return self.rows[self.rank]
+
+    def record(self, ev_start, ev_end, rows):
+        self.pending.append((ev_start, ev_end, rows))
+        if len(self.pending) > self.lag:
+            a, b, n = self.pending.pop(0)
+            b.synchronize()
+            mine = n / max(a.elapsed_time(b), 1e-3)
+            speeds = [None] * self.world
+            self.dist.all_gather_object(speeds, mine, group=self.group)
+            if self.speed is None:
+                self.speed = speeds
+            else:
+                k = self.smoothing
+                self.speed = [k * x + (1 - k) * y for x, y in zip(speeds, self.speed)]
+            self.rows = balanced_rows(self.total, self.speed, self.quantum, self.lo, self.hi)
+            self.history.append(list(self.rows))
+
+
 def load_peaks():
     p = REPO / "MEASURED_PEAKS.json"
     if p.exists():
@@ -520,8 +563,8 @@ def run_ours(args):
         print(f"warning: --gpus {args.gpus} but WORLD_SIZE {world}", file=sys.stderr)
     bt, h, v = args.rows, CFG["h"], CFG["v"]
     # N > 1 with balancing: room for up to 25 % more rows on a faster GPU
-    balance = world > 1 and args.balance
-    cap = bt + (bt // 4 if balance else 0)
+    balance = args.balance if world > 1 else "off"
+    cap = bt + (bt // 4 if balance != "off" else 0)
     hs_all, tl_all, labels_all = c4_rows(torch, cap, dev, 1000 + rank)
     w = c4_weight(torch, dev)
     gsh_all = torch.empty(cap, h, device=dev)
@@ -553,7 +596,23 @@ def run_ours(args):
         del out["grad_weight"]  # the local full grad_W is never materialised
     marks = []  # (after compute, end of step) events of the timed steps
 
+    balancer = None
+    if balance == "dynamic":
+        quantum = 256
+        gl = D.dist.new_group(backend="gloo")
+        balancer = RowBalancer(D.dist, gl, world, rank, bt, quantum, bt - bt // 4, cap)
+        # non-ignored labels among this rank's first k * quantum rows, for every k
+        valid = (labels_all != -100).to(torch.int64).cumsum(0)
+        mine = [0] + [int(x) for x in valid[quantum - 1::quantum].tolist()]
+        prefix = [None] * world
+        D.dist.all_gather_object(prefix, mine, group=gl)
+
     def step():
+        nonlocal n_global
+        if balancer is not None:
+            rows_now = balancer.rows
+            use_rows(rows_now[rank])
+            n_global = sum(prefix[r][rows_now[r] // quantum] for r in range(world))
         if world == 1:
             out["grad_weight_q"], out["grad_weight_scale"] = q, qs
             return distillation_loss_device(ctx, hs, w, labels, ob.TeacherMode.Precomputed, teacher_logits=tl,
@@ -586,13 +645,15 @@ def run_ours(args):
             res = shard.row_sharded_step(compute, labels, -100, n_global, quantize=quant, label_capacity=cap)
         ev[1].record(stream)
         marks.append(ev)
+        if balancer is not None:
+            balancer.record(ev[4], ev[0], hs.shape[0])
         return res
 
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
     ctx.check()
-    if balance:
+    if balance == "once":
         # Power-capped GPUs of one node settle at different clocks, so equal
         # row blocks finish at different times and every step waits for the
         # slowest rank. Redistribute the global batch (8192 x N rows, as
@@ -651,7 +712,10 @@ def run_ours(args):
                    "global_batch": tokens, "seq_len": None, "rows_per_gpu": bt,
                    "rows_per_rank": rows_per_rank,
                    "balance": ("rows redistributed in proportion to each GPU's measured speed (warm-up); "
-                               "the global batch is unchanged") if rows_per_rank else None,
+                               "the global batch is unchanged") if rows_per_rank else
+                              ("rows redistributed every step in proportion to each GPU's smoothed speed "
+                               "(256-row quanta, 0.75x-1.25x); the global batch is unchanged; allocations of the "
+                               "timed steps in `rows_per_step`") if balancer is not None else None,
                    "parallelism": (f"rows sharded, grad_W reduce-scatter "
                                    f"({'fused into the wgrad GEMM' if args.reduce == 'fused' else 'NCCL'})"
                                    if world > 1 else "single GPU"),
@@ -664,6 +728,8 @@ def run_ours(args):
                          "ranks": rank_split} if rank_split else None),
         "roofline": roofline, "gpu_launches": int(launches), "clocks": clocks,
     }
+    if balancer is not None:
+        line["config"]["rows_per_step"] = balancer.history[-args.steps:]
 
     # ---------------- parity of the timed path (outside the timed region)
     parity = {}
@@ -1281,9 +1347,9 @@ def main():
     ap.add_argument("--config", choices=["c4", "c5"], default="c4",
                     help="c4: the metric configuration with c5 sub-objects (default); c5: only c5")
     ap.add_argument("--shard", choices=["rows", "vocab"], default="rows", help="--config c5: partitioning")
-    ap.add_argument("--balance", action="store_true",
-                    help="N > 1: redistribute rows to each GPU's speed measured in warm-up (off by default: "
-                         "warm-up clocks do not predict the power-capped steady state)")
+    ap.add_argument("--balance", choices=["off", "once", "dynamic"], default="off",
+                    help="N > 1: redistribute the global batch to the GPUs' measured speeds: once after warm-up, "
+                         "or every step by feedback (RowBalancer)")
     ap.add_argument("--reduce", choices=["fused", "nccl"], default="fused",
                     help="N > 1: grad_W reduce-scatter fused into the wgrad GEMM, or an NCCL reduce-scatter")
     ap.add_argument("--int8-wire", action="store_true",
