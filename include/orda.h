@@ -269,14 +269,16 @@ ORDA_API void orda_context_enable_timing(OrdaContext* ctx, int enable);
 ORDA_API int orda_context_phase_times(OrdaContext* ctx, double* ms_out, uint64_t* launches_out);
 ORDA_API void orda_context_reset_timing(OrdaContext* ctx);
 /* Concurrency of the bandwidth-bound kernels with the tensor-bound GEMMs.
- * With spare_sms > 0 (default 4) the device entry runs the statistics of
+ * With spare_sms > 0 (default 0: serial) the device entry runs the statistics of
  * given (Precomputed) teacher logits on a low-priority auxiliary stream while
  * the logits GEMM runs on all SMs but spare_sms, and for the last backward
  * group runs wgrad before dgrad and the INT8 round trip on that stream while
  * dgrad runs; the call still ends on the caller's stream after all of it.
  * Results do not depend on the setting. 0 makes every kernel serial on the
- * caller's stream; values are clamped to [0, 32]. No counterpart in the
- * reference (a single-threaded CPU path). */
+ * caller's stream; values are clamped to [0, 32]. Measured at c4 with 2 to 8
+ * spare SMs the step got no faster: the side kernels compete with the GEMMs
+ * for HBM, L2 and power. No counterpart in the reference (a single-threaded
+ * CPU path). */
 ORDA_API void orda_context_set_concurrency(OrdaContext* ctx, int spare_sms);
 /* Total kernels this context has launched (all calls, timing on or off). */
 ORDA_API uint64_t orda_context_launch_count(const OrdaContext* ctx);

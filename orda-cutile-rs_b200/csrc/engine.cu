@@ -60,8 +60,11 @@ struct OrdaContext {
   // Concurrency of bandwidth-bound kernels with the tensor-bound GEMMs: the
   // persistent GEMM grid leaves `spare_sms` SMs free and the teacher
   // statistics (during the logits GEMM) and the INT8 quantiser (during
-  // dgrad) run on the low-priority auxiliary stream. 0 = serial.
-  int spare_sms = 4;
+  // dgrad) run on the low-priority auxiliary stream. 0 = serial, the
+  // default: at c4 the side kernels cost the GEMMs more than they saved
+  // (they compete for HBM, L2 and power: GEMM DRAM traffic per step rose from
+  // 33.9 to 49.4 GB and the step did not get faster with 2 to 8 spare SMs).
+  int spare_sms = 0;
   cudaStream_t aux_stream = nullptr;
   cudaEvent_t aux_ev[3] = {nullptr, nullptr, nullptr};
   std::mutex mu;

@@ -59,7 +59,8 @@ class DeviceContext:
     def set_concurrency(self, spare_sms: int) -> None:
         """`orda_context_set_concurrency`: SMs the persistent GEMMs leave to the
         teacher statistics and the INT8 quantiser running beside them on an
-        auxiliary stream (0 = every kernel serial on the caller's stream)."""
+        auxiliary stream (0, the default = every kernel serial on the caller's
+        stream)."""
         _lib().orda_context_set_concurrency(self.handle, int(spare_sms))
 
     def launch_count(self) -> int:
