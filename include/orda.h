@@ -384,7 +384,9 @@ ORDA_API int orda_distillation_loss_device(OrdaContext* ctx, const OrdaDeviceMat
  *   1. orda_vocab_forward_device: the slice's logits GEMMs; writes one tuple
  *      of ORDA_VOCAB_TUPLE floats per row (the slice's max / sum-exp
  *      statistics of student and teacher and the label's logits when the
- *      slice holds the label column) to row_partials [bt][ORDA_VOCAB_TUPLE];
+ *      slice holds the label column, as 12 doubles: the merge then matches
+ *      the single-device one to f64 precision) to row_partials
+ *      [bt][ORDA_VOCAB_TUPLE], 8-byte aligned;
  *   2. the caller all-gathers the tuples of every rank, by rank, into
  *      [world][bt][ORDA_VOCAB_TUPLE] (e.g. an NCCL all-gather);
  *   3. orda_vocab_backward_device on the same context and inputs: merges the
@@ -398,7 +400,7 @@ ORDA_API int orda_distillation_loss_device(OrdaContext* ctx, const OrdaDeviceMat
  *      configured, runs on the slice (target rows = labels in the slice).
  * The slice logits of the whole batch stay in the context's workspace
  * between the two calls; nothing else may run on the context in between. */
-#define ORDA_VOCAB_TUPLE 12
+#define ORDA_VOCAB_TUPLE 24
 typedef struct OrdaVocabShard {
   int64_t v_total;      /* full vocabulary */
   int64_t v0;           /* first vocabulary row of this rank's slice */

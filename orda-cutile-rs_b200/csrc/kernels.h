@@ -128,10 +128,11 @@ struct RowArgs {
   const float* partials_in;  // phase 2: [world][n][kVocabTuple] every rank's partials, by rank
   int world;
 };
-// Partial row statistics of one vocabulary slice: student (m, sum e^(x-m),
-// sum e^((x-m)/T), sum x), teacher (same), the label's student and teacher
-// logits and 1 when the label column lies in the slice (else 0), one pad.
-constexpr int kVocabTuple = 12;
+// Partial row statistics of one vocabulary slice, 12 doubles stored in 24
+// floats: student (m, sum e^(x-m), sum e^((x-m)/T), sum x), teacher (same),
+// the label's student and teacher logits and 1 when the label column lies in
+// the slice (else 0), one pad.
+constexpr int kVocabTuple = 24;
 // Two launches: the per-row statistics kernel and the gradient kernel.
 constexpr int kRowLaunches = 2;
 constexpr size_t kRowConstBytes = 32;

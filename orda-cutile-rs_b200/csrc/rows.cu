@@ -248,19 +248,23 @@ __global__ void __launch_bounds__(ROW_THREADS) vocab_partials_kernel(const RowAr
   long long y;
   const bool ignored = row_label(a, i, y);
   const long long yl = y - a.v0;
-  float x_y = 0.0f, t_y = 0.0f, has_y = 0.0f;
+  double x_y = 0.0, t_y = 0.0, has_y = 0.0;
   if (!ignored && yl >= 0 && yl < a.v) {
     x_y = a.x_label ? a.x_label[i]
                     : logit_at(a.logits_s, a.logits_f16 ? kLogitF16 : kLogitF32, static_cast<long long>(i) * a.ldl + yl);
-    if (a.teacher_ce) t_y = a.t_label ? a.t_label[i] : static_cast<float>(teacher_value(a, i, yl));
-    has_y = 1.0f;
+    if (a.teacher_ce) t_y = a.t_label ? static_cast<double>(a.t_label[i]) : teacher_value(a, i, yl);
+    has_y = 1.0;
   }
-  float4* out = reinterpret_cast<float4*>(a.partials_out + static_cast<long long>(i) * kVocabTuple);
-  out[0] = make_float4(static_cast<float>(own.m), static_cast<float>(own.d1), static_cast<float>(own.dT),
-                       static_cast<float>(own.sx));
-  out[1] = make_float4(static_cast<float>(ts.m), static_cast<float>(ts.d1), static_cast<float>(ts.dT),
-                       static_cast<float>(ts.sx));
-  out[2] = make_float4(x_y, t_y, has_y, 0.0f);
+  // f64, so that the merge of the slices matches the single-device merge of
+  // the same records to f64 precision (an f32 tuple moves the row's lse by
+  // an f32 rounding, which flips the bf16 rounding of some logit gradients)
+  double2* out = reinterpret_cast<double2*>(a.partials_out + static_cast<long long>(i) * kVocabTuple);
+  out[0] = make_double2(own.m, own.d1);
+  out[1] = make_double2(own.dT, own.sx);
+  out[2] = make_double2(ts.m, ts.d1);
+  out[3] = make_double2(ts.dT, ts.sx);
+  out[4] = make_double2(x_y, t_y);
+  out[5] = make_double2(has_y, 0.0);
 }
 
 // ---- vocabulary-sharded phase 2, one thread per row: merges the ranks'
@@ -270,27 +274,28 @@ __global__ void __launch_bounds__(128) vocab_merge_kernel(const RowArgs a) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= a.n) return;
   const double inv_t = static_cast<double>(a.inv_t);
-  const long long stride = static_cast<long long>(a.n) * kVocabTuple;
-  const float* base = a.partials_in + static_cast<long long>(i) * kVocabTuple;
+  // tuples of kVocabTuple floats per row, read as 12 doubles
+  const long long stride = static_cast<long long>(a.n) * kVocabTuple / 2;
+  const double* base = reinterpret_cast<const double*>(a.partials_in) + static_cast<long long>(i) * kVocabTuple / 2;
   double ms = -INFINITY, mt = -INFINITY;
   for (int r = 0; r < a.world; ++r) {
-    ms = fmax(ms, static_cast<double>(base[r * stride + 0]));
-    mt = fmax(mt, static_cast<double>(base[r * stride + 4]));
+    ms = fmax(ms, base[r * stride + 0]);
+    mt = fmax(mt, base[r * stride + 4]);
   }
   Acc own{ms, 0.0, 0.0, 0.0}, ts{mt, 0.0, 0.0, 0.0};
   double x_y = 0.0, t_y = 0.0;
   for (int r = 0; r < a.world; ++r) {
-    const float* q = base + r * stride;
+    const double* q = base + r * stride;
     const double m_r = q[0], mt_r = q[4];
-    own.d1 += static_cast<double>(q[1]) * exp(m_r - ms);
-    own.dT += static_cast<double>(q[2]) * exp((m_r - ms) * inv_t);
-    own.sx += static_cast<double>(q[3]);
+    own.d1 += q[1] * exp(m_r - ms);
+    own.dT += q[2] * exp((m_r - ms) * inv_t);
+    own.sx += q[3];
     if (a.need_kl || a.teacher_ce) {
-      ts.d1 += static_cast<double>(q[5]) * exp(mt_r - mt);
-      ts.dT += static_cast<double>(q[6]) * exp((mt_r - mt) * inv_t);
-      ts.sx += static_cast<double>(q[7]);
+      ts.d1 += q[5] * exp(mt_r - mt);
+      ts.dT += q[6] * exp((mt_r - mt) * inv_t);
+      ts.sx += q[7];
     }
-    if (q[10] != 0.0f) {
+    if (q[10] != 0.0) {
       x_y = q[8];
       t_y = q[9];
     }

@@ -134,7 +134,7 @@ class OrdaShardOptions(C.Structure):
                 ("scatter_grad_weight", C.c_int32), ("int8_wire", C.c_int32), ("reserved", C.c_int32)]
 
 
-VOCAB_TUPLE = 12  # ORDA_VOCAB_TUPLE
+VOCAB_TUPLE = 24  # ORDA_VOCAB_TUPLE
 
 
 class OrdaVocabShard(C.Structure):

@@ -44,7 +44,7 @@ pub const ORDA_DTYPE_BF16: c_int = 0;
 pub const ORDA_DTYPE_F32: c_int = 1;
 
 pub const ORDA_NUM_PHASES: usize = 6;
-pub const ORDA_VOCAB_TUPLE: usize = 12;
+pub const ORDA_VOCAB_TUPLE: usize = 24;
 pub const ORDA_NOALLOC_MAX_V: usize = 262144;
 
 #[repr(C)]
