@@ -543,11 +543,11 @@ def gemm_roofline(phases, steps, flops, kernel):
 
 # ----------------------------------------------------------------- c4 arm
 
-# DRAM bytes per c4 step of the three GEMM launches, from the committed
-# single-kernel ncu captures (profiles/gemm_traffic_c4.md): per layout, one
-# launch of a reduced case with the same V and H, scaled to 8192 rows by the
-# rows processed.
-GEMM_TRAFFIC_C4 = None
+# DRAM bytes (read + write) per c4 step of the three GEMM launches, from a
+# one-pass ncu capture of exactly those launches at full size
+# (profiles/gemm_traffic_c4.md, which gives the command and the spread
+# between boxes).
+GEMM_TRAFFIC_C4 = 50799347200
 
 
 def run_ours(args):
@@ -699,9 +699,9 @@ def run_ours(args):
     peak = load_peaks()[0]
     roofline = gemm_roofline(phases, args.steps, flops, "gemm_kernel (tcgen05 cta_group::2, 3 layouts)")
     roofline["traffic"] = GEMM_TRAFFIC_C4 if bt == CFG["bt"] else None
-    roofline["traffic_scope"] = ("DRAM bytes (read + write) per step of the 3 GEMM launches: per layout one "
-                                 "single-kernel ncu capture of a reduced case, scaled to the timed rows "
-                                 "(profiles/gemm_traffic_c4.md)")
+    roofline["traffic_scope"] = ("DRAM bytes (read + write) per step of the 3 GEMM launches, one-pass ncu "
+                                 "capture of those launches at full size (profiles/gemm_traffic_c4.md; "
+                                 "algorithmic 13.2 GB)")
     step_tflops = flops / (ms_step / 1e3) / 1e12
 
     line = {
