@@ -74,14 +74,18 @@ TOL = dict(
 )
 
 
-def grad_w_tol(k_terms):
-    """Tolerance (rel-L2) between two fp32 evaluations of grad_W whose K sums
-    (k_terms products per element: rows, x2 for a Tied teacher's second K
-    segment) are associated differently. Each element is a sum of terms of
-    random sign, so the rounding difference grows like sqrt(K) * 2^-24
-    relative to the result (7.6e-6 at K=16384); six times that, and never
-    below the 1e-5 of the other quantities."""
-    return max(TOL["shard_rel"], 6.0 * (k_terms ** 0.5) * 2.0 ** -24)
+def ksum_tol(k_terms):
+    """Tolerance (rel-L2) between two fp32 evaluations of a GEMM output whose
+    K sums (k_terms products per element) are associated differently: grad_W
+    summed over row blocks or ranks (K = rows, x2 for a Tied teacher's second
+    K segment), grad_hidden summed over vocabulary shards (K = V). With
+    rounding of random sign the difference grows like sqrt(K) * 2^-24 relative
+    to the result (six times that is allowed); the tensor-core accumulator
+    rounds once per 16-product MMA step, and where that rounding leans one way
+    the difference grows like (K / 16) * 2^-24 instead. The tolerance is the
+    larger of the two, and never below the 1e-5 of the other quantities:
+    6.1e-5 at K = 16384, 5.7e-4 at K = 152064."""
+    return max(TOL["shard_rel"], 6.0 * (k_terms ** 0.5) * 2.0 ** -24, k_terms / 16.0 * 2.0 ** -24)
 
 
 def algorithmic_flops(bt, h, v):
@@ -307,7 +311,7 @@ def check_row_blocks(torch, call, bt, n_global, blocks=8, k_segments=1):
     as device tensors. The per-row terms, grad_hidden rows and the grad_W
     partials of the blocks must add up to the full call (src/api.rs:188-422
     is a sum over rows with one global mean); the partials are summed in f64
-    so that only the GEMMs' own fp32 order differs (grad_w_tol of the
+    so that only the GEMMs' own fp32 order differs (ksum_tol of the
     bt * k_segments summed products)."""
     sc_f, gh_f, gw_f, gth_f = [None if t is None else t.clone() for t in call(0, bt, n_global)]
     sc_sum = np.zeros(4)
@@ -324,7 +328,7 @@ def check_row_blocks(torch, call, bt, n_global, blocks=8, k_segments=1):
         if gth_b is not None:
             gth_b[r0:r1] = gth
     torch.cuda.synchronize()
-    tol_w = grad_w_tol(bt * k_segments)
+    tol_w = ksum_tol(bt * k_segments)
     res = {"blocks": blocks, "scalars_rel": scalars_rel(sc_sum, sc_f.double().cpu().numpy()),
            "grad_weight_rel_l2": rel_l2_dev(torch, gw_sum, gw_f),
            "grad_hidden_rel_l2": rel_l2_dev(torch, gh_b, gh_f), "tol": TOL["blocks_rel"], "tol_grad_weight": tol_w}
@@ -969,7 +973,7 @@ def verify_c4_sharded(torch, ob, shard, D, ctx, fused, w, q, qs, args, rows=256)
     worst = D.max(torch, float(dq.max()))
     sc_err = scalars_rel(res.scalars.cpu().numpy(), sc_ref.cpu().numpy())
     sc_err = D.max(torch, sc_err)
-    tol_w = grad_w_tol(rows * world)
+    tol_w = ksum_tol(rows * world)
     out = {"rows_per_rank": rows, "path": "fused wgrad scatter + slot reduce" if fused else "NCCL reduce-scatter",
            "scalars_rel": sc_err, "grad_weight_slice_rel_l2": (stats[0] ** 0.5) / (stats[1] ** 0.5),
            "grad_hidden_rel_l2": (stats[2] ** 0.5) / (stats[3] ** 0.5), "int8_max_code_diff": worst,
@@ -1297,13 +1301,16 @@ def verify_c5_sharded(torch, ob, shard, D, ctx, part, args, rows=256, int8_wire=
         float(((my_gth.double() - gth_ref[r0:r1].double()) ** 2).sum()), float((gth_ref[r0:r1].double() ** 2).sum()),
     ])
     sc_err = D.max(torch, scalars_rel(res.scalars.cpu().numpy(), sc_ref.cpu().numpy()))
-    tol_w = 2e-2 if int8_wire else grad_w_tol(2 * rows * world)  # Tied: student and teacher rows
+    tol_w = 2e-2 if int8_wire else ksum_tol(2 * rows * world)  # Tied: student and teacher rows
+    # vocabulary sharding sums grad_hidden over the ranks' V slices: its K
+    # (= V) is associated differently from the one-GPU GEMM's
+    tol_h = ksum_tol(v) if part == "vocab" else TOL["shard_rel"]
     out = {"rows": rows * world, "scalars_rel": sc_err, "grad_weight_rel_l2": (stats[0] / stats[1]) ** 0.5,
            "grad_hidden_rel_l2": (stats[2] / stats[3]) ** 0.5,
            "grad_teacher_hidden_rel_l2": (stats[4] / stats[5]) ** 0.5, "tol": TOL["shard_rel"],
-           "tol_grad_weight": tol_w}
-    out["pass"] = out["grad_weight_rel_l2"] <= tol_w and all(
-        x <= TOL["shard_rel"] for k, x in out.items() if k.endswith(("_rel", "_rel_l2")) and k != "grad_weight_rel_l2")
+           "tol_grad_weight": tol_w, "tol_grad_hidden": tol_h}
+    out["pass"] = (out["scalars_rel"] <= TOL["shard_rel"] and out["grad_weight_rel_l2"] <= tol_w
+                   and out["grad_hidden_rel_l2"] <= tol_h and out["grad_teacher_hidden_rel_l2"] <= tol_h)
     del gw_ref, gh_ref, gth_ref
     torch.cuda.empty_cache()
     return out

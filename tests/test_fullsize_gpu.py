@@ -13,8 +13,8 @@ lie past element 2^31 of the logits buffer from row 5931 on) and checks:
         (rel-L2 <= 1e-2, the bf16 logit-gradient tolerance);
   (ii)  the full call against the sum of 8 row-block calls given the global
         mean denominator: scalars and grad_hidden within 1e-5, grad_W within
-        bench.grad_w_tol of its K (fp32 sums of the same products in another
-        order: about sqrt(K) * 2^-24 relative, 2.2e-5 at K=8192);
+        bench.ksum_tol of its K (fp32 sums of the same products in another
+        order: 3.2e-5 at K=8192);
   (iii) c4: the GPU's fp32 grad_W (skip_quantize), quantised by the oracle's
         restatement of src/quant.rs:157-202, bit-identical to the GPU's INT8
         codes, scales and dequantised grad_W of the timed call.
