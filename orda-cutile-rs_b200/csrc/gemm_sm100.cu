@@ -65,14 +65,27 @@ constexpr int OUT_STAGE_BYTES = 32 * 32 * 4;
 constexpr int OUT_BYTES = NUM_EPI_WARPS * OUT_STAGE_BYTES;  // 32 KB
 constexpr float LOG2E = 1.4426950408889634f;
 
-template <int CG>
+// WIDE (CTA pairs only): a 256 x 512 tile per pair, two N = 256 MMAs per K
+// slice sharing the A stage, one accumulator filling all 512 TMEM columns.
+// A CTA then stages 48 KB per K slice for 1024 MMA cycles instead of 32 KB
+// for 512: a quarter fewer L2->SM bytes per FLOP and 3 slices (3072 cycles)
+// of loads in flight instead of 5 x 512 = 2560 cycles. The single
+// accumulator leaves the epilogue exposed once per tile, so it suits GEMMs
+// with a long K loop per tile.
+template <int CG, bool WIDE = false>
 struct TileCfg {
+  static_assert(!WIDE || CG == 2, "wide tiles are CTA-pair tiles");
+  static constexpr int NW = WIDE ? 2 : 1;     // N = 256 MMAs per K slice
   static constexpr int TILE_M = 128 * CG;     // rows of C per tile
-  static constexpr int B_ROWS = BN / CG;      // B rows staged by one CTA
+  static constexpr int TILE_N = BN * NW;      // columns of C per tile
+  static constexpr int NACC = WIDE ? 1 : 2;   // TMEM accumulators
+  static constexpr int B_PART = BN / CG;      // B rows one CTA stages per MMA
+  static constexpr int B_ROWS = B_PART * NW;  // B rows staged by one CTA
+  static constexpr int B_PART_BYTES = B_PART * BK * 2;
   static constexpr int A_STAGE = 128 * BK * 2;
   static constexpr int B_STAGE = B_ROWS * BK * 2;
   static constexpr int STAGE = A_STAGE + B_STAGE;
-  static constexpr int STAGES = CG == 2 ? 6 : 4;
+  static constexpr int STAGES = CG == 2 ? (WIDE ? 4 : 6) : 4;
   static constexpr int SMEM = STAGES * STAGE + OUT_BYTES + 1024 /*align*/ + 256 /*barriers*/;
   static_assert(SMEM <= 232448, "shared memory over the sm_100 opt-in limit");
   static_assert((2 * STAGES + 5) * 8 + 4 <= 256, "barrier area");
@@ -90,8 +103,31 @@ struct KParams {
   int tma_reduce;  // TMA reduce-add into the output (beta == 1)
   int pol_a, pol_b, pol_c;  // L2 policy kinds (0 normal, 1 evict-first, 2 evict-last)
   int spare_sms;            // host side: SMs the persistent grid leaves free
+  // Work items: tiles [0, full_tiles) over the whole K; then the rem_tiles
+  // tiles of the last partial wave, each split into nsplit (1 or 2) K
+  // halves whose partial sums are reduce-added into a zeroed output. An
+  // unsplit tile sums K in one order whatever the tile shape; a split tile
+  // sums each half in that order and adds the two.
+  int full_tiles, rem_tiles, nsplit, num_items;
+  int allow_split;  // host side: the output may take split tiles (plain TMA store, one K segment)
   EpiArgs e;
 };
+
+// Work item -> tile and its K-block range [kb0, kb1) (single K segment when
+// split; otherwise kb0 = 0, kb1 = -1 meaning every segment in full).
+__device__ __forceinline__ int work_item(const KParams& p, int w, int& kb0, int& kb1) {
+  if (w < p.full_tiles) {
+    kb0 = 0;
+    kb1 = -1;
+    return w;
+  }
+  const int j = w - p.full_tiles;
+  const int part = j / p.rem_tiles;
+  const int kb = p.seg_kblocks[0];
+  kb0 = static_cast<int>(static_cast<long long>(kb) * part / p.nsplit);
+  kb1 = static_cast<int>(static_cast<long long>(kb) * (part + 1) / p.nsplit);
+  return p.full_tiles + j % p.rem_tiles;
+}
 
 // Tile index -> (M block, N block). N-fastest: the N blocks of one M block
 // are consecutive. Otherwise M-fastest inside groups of group_m M blocks, so
@@ -294,12 +330,13 @@ __device__ __forceinline__ void stage_and_scatter(uint8_t* buf, int lane, const 
 
 // ------------------------------------------------------------------ kernel
 
-template <int CG, bool A_MN, bool B_MN, int EPI>
+template <int CG, bool A_MN, bool B_MN, int EPI, bool WIDE>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap mapA0, const __grid_constant__ CUtensorMap mapA1,
                 const __grid_constant__ CUtensorMap mapB0, const __grid_constant__ CUtensorMap mapB1,
                 const __grid_constant__ CUtensorMap mapC, const __grid_constant__ KParams p) {
-  using T = TileCfg<CG>;
+  using T = TileCfg<CG, WIDE>;
+  static_assert(!WIDE || EPI == static_cast<int>(Epi::Store), "wide tiles take the store epilogue");
   constexpr bool PAIR = CG == 2;
   extern __shared__ uint8_t smem_raw[];
   // Same static layout in both CTAs of a pair: the MMA reads the peer's
@@ -360,15 +397,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     int stage = 0;
     uint32_t phase = 0;
     bool ok = true;
-    for (int tile = unit; tile < p.num_tiles && ok; tile += nunits) {
-      int mb, nb;
+    for (int w = unit; w < p.num_items && ok; w += nunits) {
+      int mb, nb, kb0, kb1;
+      const int tile = work_item(p, w, kb0, kb1);
       tile_coords(p, tile, mb, nb);
       const int a_row = mb * T::TILE_M + static_cast<int>(rank) * 128;
-      const int b_row = nb * BN + static_cast<int>(rank) * T::B_ROWS;
+      // this CTA's B rows of MMA q start at b_row + q * BN
+      const int b_row = nb * T::TILE_N + static_cast<int>(rank) * T::B_PART;
       for (int seg = 0; seg < p.nseg && ok; ++seg) {
         const CUtensorMap* ma = seg == 0 ? &mapA0 : &mapA1;
         const CUtensorMap* mbm = seg == 0 ? &mapB0 : &mapB1;
-        for (int kb = 0; kb < p.seg_kblocks[seg]; ++kb) {
+        const int k_end = kb1 < 0 ? p.seg_kblocks[seg] : kb1;
+        for (int kb = kb1 < 0 ? 0 : kb0; kb < k_end; ++kb) {
           if (!mbar_wait<PAIR>(&empty[stage], phase ^ 1, p.status, DEV_TIMEOUT_PRODUCER)) {
             ok = false;
             break;
@@ -385,12 +425,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
               for (int i = 0; i < 128 / 64; ++i)
                 tma_load_2d_hint<CG>(a_dst + i * (BK * 128), ma, bar, a_row + i * 64, kb * BK, pol_a);
             }
-            if (!B_MN) {
-              tma_load_2d_hint<CG>(b_dst, mbm, bar, kb * BK, b_row, pol_b);
-            } else {
 #pragma unroll
-              for (int i = 0; i < T::B_ROWS / 64; ++i)
-                tma_load_2d_hint<CG>(b_dst + i * (BK * 128), mbm, bar, b_row + i * 64, kb * BK, pol_b);
+            for (int q = 0; q < T::NW; ++q) {
+              if (!B_MN) {
+                tma_load_2d_hint<CG>(b_dst + q * T::B_PART_BYTES, mbm, bar, kb * BK, b_row + q * BN, pol_b);
+              } else {
+#pragma unroll
+                for (int i = 0; i < T::B_PART / 64; ++i)
+                  tma_load_2d_hint<CG>(b_dst + q * T::B_PART_BYTES + i * (BK * 128), mbm, bar,
+                                       b_row + q * BN + i * 64, kb * BK, pol_b);
+              }
             }
           }
           __syncwarp();
@@ -409,7 +453,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     bool ok = true;
-    for (int tile = unit; tile < p.num_tiles && ok; tile += nunits) {
+    for (int w = unit; w < p.num_items && ok; w += nunits) {
+      int kb0, kb1;
+      work_item(p, w, kb0, kb1);
       if (!mbar_wait<PAIR>(&tempty[acc], acc_phase ^ 1, p.status, DEV_TIMEOUT_MMA)) {
         ok = false;
         break;
@@ -418,7 +464,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
       bool first = true;
       for (int seg = 0; seg < p.nseg && ok; ++seg) {
-        for (int kb = 0; kb < p.seg_kblocks[seg]; ++kb) {
+        const int k_end = kb1 < 0 ? p.seg_kblocks[seg] : kb1;
+        for (int kb = kb1 < 0 ? 0 : kb0; kb < k_end; ++kb) {
           if (!mbar_wait<PAIR>(&full[stage], phase, p.status, DEV_TIMEOUT_MMA)) {
             ok = false;
             break;
@@ -429,12 +476,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             const uint32_t b_base = smem_u32(sB + stage * T::B_STAGE);
 #pragma unroll
             for (int k = 0; k < BK / 16; ++k) {
-              uint64_t ad, bd;
+              uint64_t ad;
               if (!A_MN) ad = make_smem_desc_sw128(a_base + k * 32, 16, 1024);
               else ad = make_smem_desc_sw128(a_base + k * 2048, BK * 128, 1024);
-              if (!B_MN) bd = make_smem_desc_sw128(b_base + k * 32, 16, 1024);
-              else bd = make_smem_desc_sw128(b_base + k * 2048, BK * 128, 1024);
-              umma_bf16_cg<CG>(d_tmem, ad, bd, idesc, (first && k == 0) ? 0u : 1u);
+#pragma unroll
+              for (int q = 0; q < T::NW; ++q) {
+                const uint32_t bq = b_base + q * T::B_PART_BYTES;
+                uint64_t bd;
+                if (!B_MN) bd = make_smem_desc_sw128(bq + k * 32, 16, 1024);
+                else bd = make_smem_desc_sw128(bq + k * 2048, BK * 128, 1024);
+                umma_bf16_cg<CG>(d_tmem + q * BN, ad, bd, idesc, (first && k == 0) ? 0u : 1u);
+              }
             }
             // frees this stage in both CTAs once the MMAs have read it
             if constexpr (PAIR) umma_commit_pair(&empty[stage], 0x3);
@@ -454,7 +506,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         else umma_commit(&tfull[acc]);
       }
       __syncwarp();
-      if (++acc == 2) {
+      if (++acc == T::NACC) {
         acc = 0;
         acc_phase ^= 1;
       }
@@ -473,16 +525,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const uint32_t tempty_leader0 = PAIR ? mapa_shared(smem_u32(&tempty[0]), 0) : 0u;
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int tile = unit; tile < p.num_tiles; tile += nunits) {
-      int mb, nb;
+    for (int w = unit; w < p.num_items; w += nunits) {
+      int mb, nb, kb0, kb1;
+      const int tile = work_item(p, w, kb0, kb1);
+      // a K half of a split tile adds its partial sum into the zeroed output
+      const bool split = w >= p.full_tiles && p.nsplit > 1;
       tile_coords(p, tile, mb, nb);
       if (!mbar_wait<PAIR>(&tfull[acc], acc_phase, p.status, DEV_TIMEOUT_EPILOGUE)) break;
       tc_fence_after();
       const long long grow = static_cast<long long>(mb) * T::TILE_M + row_in_tile;
       const bool row_ok = grow < p.M;
+      // this warp's half of the tile's columns: TMEM column j holds tile column j
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
-                             static_cast<uint32_t>(acc * BN + half * 128);
-      const int colh = nb * BN + half * 128;
+                             static_cast<uint32_t>(acc * BN + half * (T::TILE_N / 2));
+      const int colh = nb * T::TILE_N + half * (T::TILE_N / 2);
       const int row0 = mb * T::TILE_M + static_cast<int>(rank) * 128 + quad * 32;
       uint8_t* buf = sOut + ew * OUT_STAGE_BYTES;
       // Releases the accumulator to the (leader's) MMA warp as soon as its
@@ -501,7 +557,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const int col0 = colh + c * 32;
           if (col0 >= p.N) return;
           if (p.tma_store) {
-            if (row0 < p.M) stage_and_store(buf, lane, r, alpha, &mapC, col0, row0, p.tma_reduce != 0, pol_c);
+            if (row0 < p.M) stage_and_store(buf, lane, r, alpha, &mapC, col0, row0, p.tma_reduce != 0 || split, pol_c);
           } else if (p.e.scatter) {
             if (row0 < p.M) stage_and_scatter(buf, lane, r, alpha, p, col0, row0);
           } else if (row_ok) {
@@ -509,20 +565,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
         };
         // the TMEM load of chunk c+1 is in flight while chunk c is stored
+        constexpr int NCH = T::TILE_N / 2 / 32;
         uint32_t ra[32], rb[32];
         tmem_ld_32x32b_x32(t_row, ra);
         tmem_ld_wait();
-        tmem_ld_32x32b_x32(t_row + 32, rb);
-        store(0, ra);
-        tmem_ld_wait();
-        tmem_ld_32x32b_x32(t_row + 64, ra);
-        store(1, rb);
-        tmem_ld_wait();
-        tmem_ld_32x32b_x32(t_row + 96, rb);
-        store(2, ra);
-        tmem_ld_wait();
-        release_tmem();
-        store(3, rb);
+#pragma unroll
+        for (int c = 0; c < NCH; c += 2) {
+          tmem_ld_32x32b_x32(t_row + (c + 1) * 32, rb);
+          store(c, ra);
+          tmem_ld_wait();
+          if (c + 2 < NCH) tmem_ld_32x32b_x32(t_row + (c + 2) * 32, ra);
+          else release_tmem();
+          store(c + 1, rb);
+          if (c + 2 < NCH) tmem_ld_wait();
+        }
       } else {
         constexpr bool OWN_DT = (EPI & 1) != 0;
         constexpr bool F16 = (EPI & 2) != 0;  // Fast profile: fp16 logits, exp2 split over SFU and FMA
@@ -589,7 +645,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           reinterpret_cast<float4*>(e.rec_own)[ri] = make_float4(os.m, os.d1, os.dT, os.sx);
         }
       }
-      if (++acc == 2) {
+      if (++acc == T::NACC) {
         acc = 0;
         acc_phase ^= 1;
       }
@@ -706,10 +762,30 @@ struct LaunchCache {
   int max_clusters[64] = {0};
 };
 
-template <int CG, bool A_MN, bool B_MN, int EPI>
-cudaError_t launch_t(const CUtensorMap* maps, const KParams& kp, int num_sms, cudaStream_t stream) {
-  using T = TileCfg<CG>;
-  auto kern = gemm_kernel<CG, A_MN, B_MN, EPI>;
+// Host copy of tile_coords: the first M block among tiles [t0, num_tiles).
+int first_m_block(const KParams& p, int t0) {
+  int lo = p.m_blocks;
+  for (int t = t0; t < p.num_tiles; ++t) {
+    int mb;
+    if (p.raster_n_fastest) {
+      mb = t / p.n_blocks;
+    } else {
+      const int per_group = p.group_m * p.n_blocks;
+      const int g = t / per_group;
+      const int first_m = g * p.group_m;
+      const int gm = std::min(p.group_m, p.m_blocks - first_m);
+      mb = first_m + (t - g * per_group) % gm;
+    }
+    lo = std::min(lo, mb);
+  }
+  return lo;
+}
+
+template <int CG, bool A_MN, bool B_MN, int EPI, bool WIDE = false>
+cudaError_t launch_t(const CUtensorMap* maps, const KParams& kp_in, int num_sms, cudaStream_t stream) {
+  using T = TileCfg<CG, WIDE>;
+  auto kern = gemm_kernel<CG, A_MN, B_MN, EPI, WIDE>;
+  KParams kp = kp_in;
   static LaunchCache cache;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -744,7 +820,30 @@ cudaError_t launch_t(const CUtensorMap* maps, const KParams& kp, int num_sms, cu
   }
   // leave kp.spare_sms SMs to kernels that run concurrently on another stream
   if (kp.spare_sms > 0) units = std::max(1, units - (kp.spare_sms + CG - 1) / CG);
-  if (kp.num_tiles < units) units = kp.num_tiles;
+  // Work items. When the last wave would leave at least half of the units
+  // idle, its tiles are split into two K halves, reduce-added into the
+  // output zeroed here: 0 + a + b is the same sum in either order, so the
+  // result does not depend on which half lands first.
+  kp.full_tiles = kp.num_tiles;
+  kp.rem_tiles = 0;
+  kp.nsplit = 1;
+  kp.num_items = kp.num_tiles;
+  {
+    const int rem = kp.num_tiles % units;
+    if (kp.allow_split && rem > 0 && units / rem >= 2 && kp.seg_kblocks[0] >= 2) {
+      kp.full_tiles = kp.num_tiles - rem;
+      kp.rem_tiles = rem;
+      kp.nsplit = 2;
+      kp.num_items = kp.full_tiles + 2 * rem;
+      const long long r0 = static_cast<long long>(first_m_block(kp, kp.full_tiles)) * T::TILE_M;
+      if (r0 < kp.M) {
+        cudaError_t e = cudaMemset2DAsync(kp.e.out0 + r0 * kp.e.ld0, static_cast<size_t>(kp.e.ld0) * 4, 0,
+                                          static_cast<size_t>(kp.N) * 4, static_cast<size_t>(kp.M - r0), stream);
+        if (e != cudaSuccess) return e;
+      }
+    }
+  }
+  if (kp.num_items < units) units = kp.num_items;
   if (CG == 1) {
     kern<<<units, NUM_THREADS, T::SMEM, stream>>>(maps[0], maps[1], maps[2], maps[3], maps[4], kp);
     return cudaGetLastError();
@@ -764,9 +863,17 @@ cudaError_t launch_t(const CUtensorMap* maps, const KParams& kp, int num_sms, cu
   return cudaLaunchKernelEx(&cfg, kern, maps[0], maps[1], maps[2], maps[3], maps[4], kp);
 }
 
+template <int CG, bool A_MN, bool B_MN>
+cudaError_t store_launch(bool wide, const CUtensorMap* maps, const KParams& kp, int num_sms, cudaStream_t stream) {
+  if constexpr (CG == 2) {
+    if (wide) return launch_t<CG, A_MN, B_MN, 0, true>(maps, kp, num_sms, stream);
+  }
+  return launch_t<CG, A_MN, B_MN, 0, false>(maps, kp, num_sms, stream);
+}
+
 template <int CG>
 cudaError_t dispatch(const GemmDesc& d, const CUtensorMap* maps, const KParams& kp, int num_sms,
-                     cudaStream_t stream, const char** why) {
+                     cudaStream_t stream, const char** why, bool wide) {
   if (d.epi == Epi::Logits) {
     if (d.a_mn_major || d.b_mn_major) {
       if (why) *why = "logits epilogue requires K-major operands";
@@ -780,10 +887,10 @@ cudaError_t dispatch(const GemmDesc& d, const CUtensorMap* maps, const KParams& 
     if (d.args.own_dT) return launch_t<CG, false, false, 17>(maps, kp, num_sms, stream);
     return launch_t<CG, false, false, 16>(maps, kp, num_sms, stream);
   }
-  if (!d.a_mn_major && !d.b_mn_major) return launch_t<CG, false, false, 0>(maps, kp, num_sms, stream);
-  if (!d.a_mn_major && d.b_mn_major) return launch_t<CG, false, true, 0>(maps, kp, num_sms, stream);
-  if (d.a_mn_major && !d.b_mn_major) return launch_t<CG, true, false, 0>(maps, kp, num_sms, stream);
-  return launch_t<CG, true, true, 0>(maps, kp, num_sms, stream);
+  if (!d.a_mn_major && !d.b_mn_major) return store_launch<CG, false, false>(wide, maps, kp, num_sms, stream);
+  if (!d.a_mn_major && d.b_mn_major) return store_launch<CG, false, true>(wide, maps, kp, num_sms, stream);
+  if (d.a_mn_major && !d.b_mn_major) return store_launch<CG, true, false>(wide, maps, kp, num_sms, stream);
+  return store_launch<CG, true, true>(wide, maps, kp, num_sms, stream);
 }
 
 // CTA pairs by default; ORDA_GEMM_CTA_PAIR=0 selects single-CTA tiles (a
@@ -792,6 +899,24 @@ cudaError_t dispatch(const GemmDesc& d, const CUtensorMap* maps, const KParams& 
 bool use_cta_pair() {
   const char* v = std::getenv("ORDA_GEMM_CTA_PAIR");
   return !(v && v[0] == '0');
+}
+
+// Wide (256 x 512) pair tiles for large store-epilogue GEMMs: at least two
+// waves of wide tiles over the SMs and at least 128 K blocks per tile, so
+// that the per-tile epilogue, which the next tile's MMAs do not overlap,
+// stays a few percent of the tile (measured at c4: dgrad, K = 2048 blocks,
+// 4.8 % fewer SM cycles; wgrad, K = 128 blocks, 1.5 % fewer). A scattered
+// epilogue (peer stores) is exposed in full, so it needs 1024 K blocks.
+// ORDA_GEMM_WIDE=0 never uses them and ORDA_GEMM_WIDE=2 uses them for every
+// store-epilogue GEMM with N > 256 (diagnostic switches; every choice
+// computes the same sums, associated per tile as described at KParams).
+bool use_wide(const GemmDesc& d, long long k_blocks, long long m_blocks, int num_sms) {
+  const char* v = std::getenv("ORDA_GEMM_WIDE");
+  const int mode = v ? (v[0] - '0') : 1;
+  if (mode == 0 || d.epi != Epi::Store || d.N <= BN) return false;
+  if (mode == 2) return true;
+  const long long tiles = m_blocks * ((d.N + 2 * BN - 1) / (2 * BN));
+  return tiles >= num_sms && k_blocks >= (d.args.scatter ? 1024 : 128);
 }
 
 }  // namespace
@@ -805,11 +930,15 @@ cudaError_t gemm_launch(const GemmDesc& d, int num_sms, cudaStream_t stream, con
   const int cg = use_cta_pair() ? 2 : 1;
   const int tile_m = 128 * cg;
   const int b_rows = BN / cg;
+  long long k_blocks = 0;
+  for (int s = 0; s < d.nseg; ++s) k_blocks += (d.k_seg[s] + BK - 1) / BK;
+  const bool wide = cg == 2 && use_wide(d, k_blocks, (d.M + tile_m - 1) / tile_m, num_sms);
+  const int tile_n = wide ? 2 * BN : BN;
   KParams kp{};
   kp.M = static_cast<int>(d.M);
   kp.N = static_cast<int>(d.N);
   kp.m_blocks = static_cast<int>((d.M + tile_m - 1) / tile_m);
-  kp.n_blocks = static_cast<int>((d.N + BN - 1) / BN);
+  kp.n_blocks = static_cast<int>((d.N + tile_n - 1) / tile_n);
   kp.num_tiles = kp.m_blocks * kp.n_blocks;
   kp.raster_n_fastest = d.raster_n_fastest ? 1 : 0;
   kp.nseg = d.nseg;
@@ -883,9 +1012,13 @@ cudaError_t gemm_launch(const GemmDesc& d, int num_sms, cudaStream_t stream, con
     kp.tma_store = 1;
     kp.tma_reduce = d.args.beta == 1.0f ? 1 : 0;
   }
+  // Split tail tiles only for wide tiles: a split tile sums its K range as
+  // two halves plus one add, so its rows are associated differently from
+  // those of an unsplit tile of another call.
+  kp.allow_split = wide && kp.tma_store && !kp.tma_reduce && d.nseg == 1 && !d.args.scatter;
   if (kp.num_tiles == 0) return cudaSuccess;
-  cudaError_t e = cg == 2 ? dispatch<2>(d, maps, kp, num_sms, stream, why)
-                          : dispatch<1>(d, maps, kp, num_sms, stream, why);
+  cudaError_t e = cg == 2 ? dispatch<2>(d, maps, kp, num_sms, stream, why, wide)
+                          : dispatch<1>(d, maps, kp, num_sms, stream, why, false);
   if (e != cudaSuccess) return e;
   int n = 1;
   if (d.demote_kept && (kp.pol_a == 2 || kp.pol_b == 2)) {
