@@ -557,7 +557,7 @@ def gemm_roofline(phases, steps, flops, kernel):
 # one-pass ncu capture of exactly those launches at full size
 # (profiles/gemm_traffic_c4.md, which gives the command and the spread
 # between boxes).
-GEMM_TRAFFIC_C4 = 50799347200
+GEMM_TRAFFIC_C4 = 32474239488
 
 
 def run_ours(args):

@@ -63,6 +63,10 @@ def _worker(rank, world, port, outdir, mode="nccl"):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     os.environ["NCCL_NVLS_ENABLE"] = "0"
+    if mode == "fused_wide":
+        # the scattering wgrad GEMM on wide (256 x 512) pair tiles, which the
+        # default rule keeps for larger shapes
+        os.environ["ORDA_GEMM_WIDE"] = "2"
     import datetime
 
     import torch.distributed as dist
@@ -143,7 +147,7 @@ def _worker(rank, world, port, outdir, mode="nccl"):
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("mode", ["nccl", "fused", "fused_side", "fused_wire"])
+@pytest.mark.parametrize("mode", ["nccl", "fused", "fused_side", "fused_wire", "fused_wide"])
 def test_row_sharded_two_gpus_match_single_gpu(ob, tmp_path, mode):
     import torch.multiprocessing as mp
 

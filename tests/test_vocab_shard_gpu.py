@@ -166,6 +166,10 @@ def _worker(rank, world, port, outdir, scatter=False):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     os.environ["NCCL_NVLS_ENABLE"] = "0"
+    if scatter == "wide":
+        # the scattering dgrad GEMMs on wide (256 x 512) pair tiles, which the
+        # default rule takes for long vocabulary slices (1024 K blocks)
+        os.environ["ORDA_GEMM_WIDE"] = "2"
     import datetime
 
     import torch.distributed as dist
@@ -200,7 +204,7 @@ def _worker(rank, world, port, outdir, scatter=False):
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("scatter", [False, True])
+@pytest.mark.parametrize("scatter", [False, True, "wide"])
 def test_vocab_sharded_two_gpus_match_single_gpu(ob, tmp_path, scatter):
     """grad_hidden all-reduced (full on every rank), or reduce-scattered by
     the dgrad GEMMs into the owners' slot buffers (each rank its rows)."""
