@@ -39,6 +39,7 @@
 #include <vector>
 
 #include "../../include/orda.h"
+#include "host_io.h"
 #include "host_logic.h"
 #include "kernels.h"
 #include "ptx.cuh"
@@ -933,6 +934,21 @@ int check_status(OrdaContext* ctx, char* err, size_t len) {
 // Teacher-logit slab of the host entry's copy pipeline (bytes).
 std::atomic<size_t> g_host_slab_bytes{size_t{512} << 20};
 
+// The host-Mat entry's compressed grad_W download (on unless
+// ORDA_HOST_DEQUANT=0, a diagnostic switch read on every call).
+bool host_dequant_enabled() {
+  const char* v = std::getenv("ORDA_HOST_DEQUANT");
+  return !(v && v[0] == '0');
+}
+
+// The host-Mat entry's bf16 uploads: GEMM operands rounded on the host and
+// teacher-logit chunks that hold bf16 values sent as bf16 (on unless
+// ORDA_HOST_CONVERT=0, a diagnostic switch read on every call).
+bool host_convert_enabled() {
+  const char* v = std::getenv("ORDA_HOST_CONVERT");
+  return !(v && v[0] == '0');
+}
+
 std::mutex g_default_mu;
 OrdaContext* g_default_ctx[64] = {nullptr};
 
@@ -1590,6 +1606,29 @@ int orda_distillation_loss(const OrdaMatF32* student_hidden, const OrdaMatF32* w
   }
   const size_t n_groups = group_rows ? ceil_div(bt, group_rows) : 1;
 
+  // With the INT8 round trip, grad_W comes back compressed: its INT8 codes,
+  // row scales and exact target rows (0.66 GB instead of 2.15 GB at c4), and
+  // the host forms q * s (host_dequant.cc: the device's own float multiply,
+  // so the values are bit-identical). ORDA_HOST_DEQUANT=0 copies the fp32
+  // grad_W instead (a diagnostic switch). Target rows: non-ignored labels,
+  // the rule of target_flags_kernel.
+  const bool host_deq = opts->config.quantize_grad_weight != 0 && host_dequant_enabled();
+  std::vector<int32_t> exact_pos, exact_idx;
+  if (host_deq) {
+    std::vector<uint8_t> is_target(v, 0);
+    for (size_t i = 0; i < bt; ++i) {
+      const int64_t t = labels[i];
+      if (t != opts->ignore_index && t >= 0 && static_cast<size_t>(t) < v) is_target[static_cast<size_t>(t)] = 1;
+    }
+    exact_pos.assign(v, -1);
+    for (size_t r = 0; r < v; ++r) {
+      if (!is_target[r]) continue;
+      exact_pos[r] = static_cast<int32_t>(exact_idx.size());
+      exact_idx.push_back(static_cast<int32_t>(r));
+    }
+  }
+  const size_t n_exact = exact_idx.size();
+
   // device staging layout
   size_t off = 0;
   auto take = [&](size_t bytes) {
@@ -1606,6 +1645,15 @@ int orda_distillation_loss(const OrdaMatF32* student_hidden, const OrdaMatF32* w
   const size_t o_sc = take(4 * sizeof(float));
   const size_t ring_bytes = std::max(kRingBytes, std::max(h, ht) * 4);
   const size_t o_ring = take(ring_bytes);
+  const size_t o_q = take(host_deq ? v * h : 0), o_qs = take(host_deq ? v * 4 : 0);
+  const size_t o_xidx = take(n_exact * 4), o_xrows = take(n_exact * h * 4);
+  // Host conversion: a ring of kRing page-locked bf16 chunks of kChunk
+  // elements feeds the copies; bf16 teacher-logit chunks land in a device
+  // scratch chunk and are widened into the fp32 teacher rows.
+  const bool host_conv = host_convert_enabled();
+  constexpr size_t kChunk = size_t{32} << 20;  // elements (64 MiB of bf16)
+  constexpr int kRing = 3;
+  const size_t o_tscr = take(host_conv && pre ? std::max(kChunk, v) * 2 : 0);
   if (ctx->stage_bytes < off) {
     cudaFree(ctx->stage);
     ctx->stage = nullptr;
@@ -1631,7 +1679,35 @@ int orda_distillation_loss(const OrdaMatF32* student_hidden, const OrdaMatF32* w
   bool ok_alloc = sc_host && host_mat(bt, h, out->grad_student_hidden) && host_mat(v, h, out->grad_weight);
   if (ok_alloc && tgrad) ok_alloc = host_mat(bt, ht, out->grad_teacher_hidden);
   if (ok_alloc && tgrad && mode == ORDA_TEACHER_SEPARATE) ok_alloc = host_mat(v, ht, out->grad_teacher_weight);
+  // page-locked landing buffers of the compressed grad_W
+  int8_t* q_host = nullptr;
+  float *qs_host = nullptr, *xrows_host = nullptr;
+  if (ok_alloc && host_deq) {
+    q_host = reinterpret_cast<int8_t*>(pinned_alloc(v * h));
+    qs_host = pinned_alloc(v * 4);
+    xrows_host = pinned_alloc(n_exact * h * 4);
+    ok_alloc = q_host && qs_host && xrows_host;
+  }
+  uint16_t* ring_host[kRing] = {nullptr, nullptr, nullptr};
+  if (ok_alloc && host_conv) {
+    for (int b = 0; b < kRing && ok_alloc; ++b) {
+      ring_host[b] = reinterpret_cast<uint16_t*>(pinned_alloc(std::max(kChunk, std::max(std::max(h, ht), v)) * 2));
+      ok_alloc = ring_host[b] != nullptr;
+    }
+  }
+  auto release_landing = [&]() {
+    pinned_release(q_host);
+    pinned_release(qs_host);
+    pinned_release(xrows_host);
+    for (int b = 0; b < kRing; ++b) pinned_release(ring_host[b]);
+  };
+  // host workers of the conversions and the dequantisation (one per core,
+  // at most 16: about 90 GB/s of fp32 converted on a 16-core host)
+  std::unique_ptr<HostPool> pool;
+  if (ok_alloc && (host_conv || host_deq))
+    pool = std::make_unique<HostPool>(std::max(1u, std::min(16u, std::thread::hardware_concurrency())));
   if (!ok_alloc) {
+    release_landing();
     pinned_release(sc_host);
     orda_output_free(out);
     set_error(err, err_len, "page-locked host allocation for the outputs failed");
@@ -1669,9 +1745,41 @@ int orda_distillation_loss(const OrdaMatF32* student_hidden, const OrdaMatF32* w
     feed.cv.notify_all();
   };
   float* ring = reinterpret_cast<float*>(S + o_ring);
+  cudaEvent_t ev_ring[kRing] = {nullptr, nullptr, nullptr};
+  if (host_conv)
+    for (int b = 0; b < kRing; ++b) ev_ring[b] = mk_event();
   std::thread copier([&]() {
     cudaSetDevice(ctx->device);
     cudaError_t e = cudaMemcpyAsync(S + o_lab, labels, bt * 8, cudaMemcpyHostToDevice, cin);
+    // next page-locked ring chunk, once the copy that last read it is done
+    int slot = 0;
+    bool used[kRing] = {false, false, false};
+    auto next_chunk = [&](int* b) -> uint16_t* {
+      *b = slot;
+      slot = (slot + 1) % kRing;
+      if (used[*b] && e == cudaSuccess) e = cudaEventSynchronize(ev_ring[*b]);
+      used[*b] = true;
+      return ring_host[*b];
+    };
+    // f32 host rows -> bf16 on the host -> device rows
+    auto put_bf16_host = [&](const OrdaMatF32& m, size_t ld, size_t o) {
+      const size_t per = std::max<size_t>(1, kChunk / std::max<size_t>(m.cols, 1));
+      for (size_t r0 = 0; r0 < m.rows && e == cudaSuccess; r0 += per) {
+        const size_t n = std::min(per, m.rows - r0), cnt = n * m.cols;
+        int b;
+        uint16_t* buf = next_chunk(&b);
+        if (e != cudaSuccess) break;
+        const float* src = m.data + r0 * m.cols;
+        pool->run([&](unsigned w, unsigned nw) {
+          size_t a, z;
+          split_range(cnt, nw, w, &a, &z);
+          f32_to_bf16_host(src + a, z - a, buf + a);
+        });
+        e = cudaMemcpy2DAsync(S + o + r0 * ld * 2, ld * 2, buf, m.cols * 2, m.cols * 2, n, cudaMemcpyHostToDevice,
+                              cin);
+        if (e == cudaSuccess) e = cudaEventRecord(ev_ring[b], cin);
+      }
+    };
     // f32 host rows -> ring -> bf16 device rows (one stream: each slab's copy
     // follows the conversion of the previous one, so one ring buffer serves)
     auto put_bf16 = [&](const OrdaMatF32& m, size_t ld, size_t o) {
@@ -1685,21 +1793,64 @@ int orda_distillation_loss(const OrdaMatF32* student_hidden, const OrdaMatF32* w
         e = cudaGetLastError();
       }
     };
-    if (e == cudaSuccess) put_bf16(*student_hidden, ldh, o_hs);
-    if (e == cudaSuccess) put_bf16(*weight, ldh, o_w);
-    if (e == cudaSuccess && live) put_bf16(teacher->hidden, ldht, o_ht);
-    if (e == cudaSuccess && mode == ORDA_TEACHER_SEPARATE) put_bf16(teacher->weight, ldht, o_wt);
+    auto put = [&](const OrdaMatF32& m, size_t ld, size_t o) {
+      if (host_conv) put_bf16_host(m, ld, o);
+      else put_bf16(m, ld, o);
+    };
+    if (e == cudaSuccess) put(*student_hidden, ldh, o_hs);
+    if (e == cudaSuccess) put(*weight, ldh, o_w);
+    if (e == cudaSuccess && live) put(teacher->hidden, ldht, o_ht);
+    if (e == cudaSuccess && mode == ORDA_TEACHER_SEPARATE) put(teacher->weight, ldht, o_wt);
     if (e == cudaSuccess) e = cudaEventRecord(ev_inputs, cin);
     if (e != cudaSuccess) {
       announce(SIZE_MAX, e);
       return;
     }
     announce(1, cudaSuccess);
+    // Teacher logits: a chunk whose values are all bf16 values crosses as
+    // bf16 and is widened on the device (exact); otherwise as fp32, and
+    // after the first such chunk the rest of the call copies fp32 directly.
+    bool try_bf16 = host_conv;
+    auto put_teacher_rows = [&](size_t r0, size_t n) {
+      if (try_bf16) {
+        const size_t per = std::max<size_t>(1, kChunk / v);
+        for (size_t c0 = r0; c0 < r0 + n && e == cudaSuccess && try_bf16; c0 += per) {
+          const size_t m = std::min(per, r0 + n - c0), cnt = m * v;
+          int b;
+          uint16_t* buf = next_chunk(&b);
+          if (e != cudaSuccess) return;
+          const float* src = teacher->logits.data + c0 * v;
+          unsigned char exact[64];
+          pool->run([&](unsigned w, unsigned nw) {
+            size_t a, z;
+            split_range(cnt, nw, w, &a, &z);
+            exact[w] = f32_to_bf16_if_exact(src + a, z - a, buf + a) ? 1 : 0;
+          });
+          for (unsigned w = 0; w < pool->size(); ++w) try_bf16 = try_bf16 && exact[w];
+          if (!try_bf16) {
+            // this chunk and the rest of the rows as fp32
+            e = cudaMemcpy2DAsync(S + o_tl + c0 * ldtl * 4, ldtl * 4, teacher->logits.data + c0 * v, v * 4, v * 4,
+                                  r0 + n - c0, cudaMemcpyHostToDevice, cin);
+            return;
+          }
+          e = cudaMemcpyAsync(S + o_tscr, buf, cnt * 2, cudaMemcpyHostToDevice, cin);
+          if (e == cudaSuccess) e = cudaEventRecord(ev_ring[b], cin);
+          if (e == cudaSuccess) {
+            launch_bf16_rows_to_f32(reinterpret_cast<const uint16_t*>(S + o_tscr), static_cast<long long>(m),
+                                    static_cast<long long>(v), reinterpret_cast<float*>(S + o_tl + c0 * ldtl * 4),
+                                    static_cast<long long>(ldtl), cin);
+            e = cudaGetLastError();
+          }
+        }
+        return;
+      }
+      e = cudaMemcpy2DAsync(S + o_tl + r0 * ldtl * 4, ldtl * 4, teacher->logits.data + r0 * v, v * 4, v * 4, n,
+                            cudaMemcpyHostToDevice, cin);
+    };
     for (size_t k = 0; k < ev_teacher.size(); ++k) {
       const size_t r0 = k * (group_rows ? group_rows : bt);
       const size_t n = std::min(group_rows ? group_rows : bt, bt - r0);
-      e = cudaMemcpy2DAsync(S + o_tl + r0 * ldtl * 4, ldtl * 4, teacher->logits.data + r0 * v, v * 4, v * 4, n,
-                            cudaMemcpyHostToDevice, cin);
+      put_teacher_rows(r0, n);
       if (e == cudaSuccess) e = cudaEventRecord(ev_teacher[k], cin);
       if (e != cudaSuccess) {
         announce(SIZE_MAX, e);
@@ -1739,6 +1890,7 @@ int orda_distillation_loss(const OrdaMatF32* student_hidden, const OrdaMatF32* w
       orda_output_free(out);
     }
     pinned_release(sc_host);
+    release_landing();
     return rc;
   };
 
@@ -1756,6 +1908,10 @@ int orda_distillation_loss(const OrdaMatF32* student_hidden, const OrdaMatF32* w
     dout.ld_grad_teacher_weight = ht;
   }
   dout.scalars = reinterpret_cast<float*>(S + o_sc);
+  if (host_deq) {
+    dout.grad_weight_q = reinterpret_cast<int8_t*>(S + o_q);
+    dout.grad_weight_scale = reinterpret_cast<float*>(S + o_qs);
+  }
 
   DevInputs in;
   in.bt = bt;
@@ -1777,6 +1933,10 @@ int orda_distillation_loss(const OrdaMatF32* student_hidden, const OrdaMatF32* w
 
   if (int rc = wait_stage(1)) return finish(rc);
   if (cudaError_t e = cudaStreamWaitEvent(st, ev_inputs, 0); e != cudaSuccess) return finish(cuda_fail(e, "event wait", err, err_len));
+  if (n_exact > 0) {
+    cudaError_t e = cudaMemcpyAsync(S + o_xidx, exact_idx.data(), n_exact * 4, cudaMemcpyHostToDevice, st);
+    if (e != cudaSuccess) return finish(cuda_fail(e, "host->device copy", err, err_len));
+  }
   HostPipe hp;
   hp.group_rows = group_rows;
   if (pre) {
@@ -1805,16 +1965,61 @@ int orda_distillation_loss(const OrdaMatF32* student_hidden, const OrdaMatF32* w
   if (int rc = run_device(ctx, in, *opts, dout, nullptr, st, &plan, err, err_len, nullptr, &hp)) return finish(rc);
 
   // grad_W (after the INT8 round trip, if any) and the scalars
+  float* xrows_dev = reinterpret_cast<float*>(S + o_xrows);
+  if (n_exact > 0) {
+    launch_gather_rows(dout.grad_weight, static_cast<long long>(h), reinterpret_cast<const int32_t*>(S + o_xidx),
+                       static_cast<long long>(n_exact), static_cast<long long>(h), xrows_dev, st);
+    if (cudaError_t e = cudaGetLastError(); e != cudaSuccess) return finish(cuda_fail(e, "gather rows", err, err_len));
+  }
   cudaEvent_t ev_done = mk_event();
   cudaError_t e = cudaEventRecord(ev_done, st);
   if (e == cudaSuccess) e = cudaStreamWaitEvent(cout, ev_done, 0);
-  if (e == cudaSuccess)
+  // compressed grad_W: scales and exact rows first, then the codes in row
+  // slabs, each announced by an event so the host dequantises slab k while
+  // slab k + 1 is in flight
+  std::vector<std::pair<size_t, cudaEvent_t>> slabs;  // (end row, event)
+  cudaEvent_t ev_meta = nullptr;
+  if (host_deq) {
+    if (e == cudaSuccess) e = cudaMemcpyAsync(qs_host, dout.grad_weight_scale, v * 4, cudaMemcpyDeviceToHost, cout);
+    if (e == cudaSuccess && n_exact > 0)
+      e = cudaMemcpyAsync(xrows_host, xrows_dev, n_exact * h * 4, cudaMemcpyDeviceToHost, cout);
+    if (e == cudaSuccess) e = cudaEventRecord(ev_meta = mk_event(), cout);
+    const size_t slab_rows = std::max<size_t>(1, (size_t{32} << 20) / std::max<size_t>(h, 1));
+    for (size_t r0 = 0; r0 < v && e == cudaSuccess; r0 += slab_rows) {
+      const size_t r1 = std::min(v, r0 + slab_rows);
+      e = cudaMemcpyAsync(q_host + r0 * h, dout.grad_weight_q + r0 * h, (r1 - r0) * h, cudaMemcpyDeviceToHost, cout);
+      cudaEvent_t ev = mk_event();
+      if (e == cudaSuccess) e = cudaEventRecord(ev, cout);
+      slabs.emplace_back(r1, ev);
+    }
+  } else if (e == cudaSuccess) {
     e = cudaMemcpyAsync(out->grad_weight.data, dout.grad_weight, v * h * 4, cudaMemcpyDeviceToHost, cout);
+  }
   if (e == cudaSuccess && tgrad && mode == ORDA_TEACHER_SEPARATE)
     e = cudaMemcpyAsync(out->grad_teacher_weight.data, dout.grad_teacher_weight, v * ht * 4, cudaMemcpyDeviceToHost,
                         cout);
   if (e == cudaSuccess) e = cudaMemcpyAsync(sc_host, dout.scalars, 4 * sizeof(float), cudaMemcpyDeviceToHost, cout);
   if (e != cudaSuccess) return finish(cuda_fail(e, "device->host copy", err, err_len));
+  if (host_deq) {
+    // the workers split each slab's rows once the slab has landed (the
+    // copier, the pool's other user, has finished)
+    if (copier.joinable()) copier.join();
+    e = cudaEventSynchronize(ev_meta);
+    size_t r0 = 0;
+    for (size_t k = 0; k < slabs.size() && e == cudaSuccess; ++k) {
+      const size_t r1 = slabs[k].first;
+      e = cudaEventSynchronize(slabs[k].second);
+      if (e != cudaSuccess) break;
+      pool->run([&](unsigned w, unsigned nw) {
+        size_t a, z;
+        split_range(r1 - r0, nw, w, &a, &z);
+        if (a < z) dequant_rows_host(q_host, qs_host, exact_pos.data(), xrows_host, r0 + a, r0 + z, h,
+                                     out->grad_weight.data);
+      });
+      r0 = r1;
+    }
+    if (e != cudaSuccess) return finish(cuda_fail(e, "device->host copy", err, err_len));
+  }
   out->chunk_plan = plan;
   return finish(ORDA_OK);
 }

@@ -178,10 +178,18 @@ void launch_finalize(const float* nll_s, const float* nll_t, const double* kl_ba
 // f32 -> bf16 (round to nearest even) into a padded row-major buffer.
 void launch_f32_to_bf16(const float* src, long long rows, long long cols, uint16_t* dst, long long ld,
                         cudaStream_t stream);
+// dst rows (fp32, ld elements apart) = the dense [rows, cols] bf16 src, exactly.
+void launch_bf16_rows_to_f32(const uint16_t* src, long long rows, long long cols, float* dst, long long ld,
+                             cudaStream_t stream);
 
 // INT8 row-wise quantisation of grad_W (in place dequantised result). Row r
 // of grad_w is row r + row_offset of the full matrix (the stochastic draw
 // index is (r + row_offset) * h + c).
+// dst[i, :] = src[idx[i], :] for i < n (fp32 rows of h elements; src ld).
+// The base pointers must be 16-byte aligned for the vector path.
+void launch_gather_rows(const float* src, long long ld, const int32_t* idx, long long n, long long h, float* dst,
+                        cudaStream_t stream);
+
 void launch_quant(float* grad_w, long long v, long long h, long long ld, const uint8_t* target_flags,
                   int stochastic, uint64_t seed, int8_t* q, float* scale, cudaStream_t stream,
                   long long row_offset = 0);

@@ -297,6 +297,29 @@ bool launch_slot_reduce_quant(const float* slots, int world, long long slice, lo
   return true;
 }
 
+// Copies rows idx[0..n) of src (ld elements apart) into the dense [n, h]
+// dst: the exact target rows of grad_W for the host-Mat entry's compressed
+// download. One CTA per row.
+__global__ void __launch_bounds__(QT) gather_rows_kernel(const float* __restrict__ src, long long ld,
+                                                         const int32_t* __restrict__ idx, long long h,
+                                                         float* __restrict__ dst) {
+  const long long i = blockIdx.x;
+  const float* srow = src + static_cast<long long>(idx[i]) * ld;
+  float* drow = dst + i * h;
+  if (h % 4 == 0 && ld % 4 == 0) {
+    for (long long c = threadIdx.x * 4; c < h; c += QT * 4)
+      *reinterpret_cast<float4*>(drow + c) = *reinterpret_cast<const float4*>(srow + c);
+  } else {
+    for (long long c = threadIdx.x; c < h; c += QT) drow[c] = srow[c];
+  }
+}
+
+void launch_gather_rows(const float* src, long long ld, const int32_t* idx, long long n, long long h, float* dst,
+                        cudaStream_t stream) {
+  if (n <= 0) return;
+  gather_rows_kernel<<<static_cast<unsigned>(n), QT, 0, stream>>>(src, ld, idx, h, dst);
+}
+
 void launch_quant(float* grad_w, long long v, long long h, long long ld, const uint8_t* target_flags,
                   int stochastic, uint64_t seed, int8_t* q, float* scale, cudaStream_t stream,
                   long long row_offset) {

@@ -27,6 +27,7 @@
 #include <cmath>
 #include <cstdint>
 
+#include "bf16_bits.h"
 #include "kernels.h"
 #include "ptx.cuh"
 
@@ -675,7 +676,19 @@ __global__ void f32_to_bf16_kernel(const float* src, long long rows, long long c
   for (long long idx = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; idx < total;
        idx += static_cast<long long>(gridDim.x) * blockDim.x) {
     const long long r = idx / cols, c = idx - r * cols;
-    dst[r * ld + c] = __bfloat16_as_ushort(__float2bfloat16_rn(src[idx]));
+    dst[r * ld + c] = f32_bits_to_bf16(__float_as_uint(src[idx]));
+  }
+}
+
+// dst rows (fp32, ld elements apart) = the dense [rows, cols] bf16 src,
+// exactly (a bf16 value is the high half of its fp32).
+__global__ void bf16_rows_to_f32_kernel(const uint16_t* src, long long rows, long long cols, float* dst,
+                                        long long ld) {
+  const long long total = rows * cols;
+  for (long long idx = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long r = idx / cols, c = idx - r * cols;
+    dst[r * ld + c] = __uint_as_float(static_cast<uint32_t>(src[idx]) << 16);
   }
 }
 
@@ -830,6 +843,15 @@ void launch_f32_to_bf16(const float* src, long long rows, long long cols, uint16
   long long blocks = (total + 255) / 256;
   if (blocks > 148 * 32) blocks = 148 * 32;
   f32_to_bf16_kernel<<<static_cast<int>(blocks), 256, 0, stream>>>(src, rows, cols, dst, ld);
+}
+
+void launch_bf16_rows_to_f32(const uint16_t* src, long long rows, long long cols, float* dst, long long ld,
+                             cudaStream_t stream) {
+  const long long total = rows * cols;
+  if (total <= 0) return;
+  long long blocks = (total + 255) / 256;
+  if (blocks > 148 * 32) blocks = 148 * 32;
+  bf16_rows_to_f32_kernel<<<static_cast<int>(blocks), 256, 0, stream>>>(src, rows, cols, dst, ld);
 }
 
 }  // namespace orda

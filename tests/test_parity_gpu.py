@@ -486,6 +486,80 @@ def test_host_entry_slab_pipeline_matches_oracle(ob, oracle, quantize):
     assert_parity(piped, oracle.distillation_loss(s, w, labs, t, opts, nthreads=NT), "pipelined")
 
 
+@pytest.mark.parametrize("mode,h,stochastic", [("Precomputed", 256, False), ("Tied", 250, True)])
+def test_host_entry_compressed_grad_w_download_is_bit_identical(ob, monkeypatch, mode, h, stochastic):
+    """With the INT8 round trip the host-Mat entry copies grad_W back as its
+    INT8 codes, row scales and exact target rows and forms q * s on the host;
+    the result equals the fp32 download (ORDA_HOST_DEQUANT=0) bit for bit,
+    with ignored and repeated labels, an odd H (scalar row gather) and a Tied
+    teacher whose CE term adds to grad_W."""
+    gen = torch.Generator().manual_seed(505)
+    bt, v = 192, 5000
+    s = randn_mat(ob, bt, h, gen)
+    w = randn_mat(ob, v, h, gen, 0.05)
+    labs = torch.randint(0, v, (bt,), generator=gen).tolist()
+    labs[5] = labs[6] = -100
+    labs[11] = labs[10]
+    if mode == "Tied":
+        t = ob.Teacher.Tied(randn_mat(ob, bt, h, gen))
+        extra = dict(teacher_ce_weight=0.5)
+    else:
+        t = ob.Teacher.Precomputed(ob.Mat.from_array((np.sqrt(2.0) * torch.randn(bt, v, generator=gen)).numpy()))
+        extra = {}
+    cfg = ob.KernelConfig(quantize_grad_weight=True, stochastic_rounding=stochastic,
+                          stochastic_seed=7 if stochastic else None)
+    opts = ob.LossOptions(kd_weight=0.4, temperature=1.5, config=cfg, **extra)
+    res = {}
+    for flag in ("1", "0"):
+        monkeypatch.setenv("ORDA_HOST_DEQUANT", flag)
+        res[flag] = ob.distillation_loss(s, w, labs, t, opts)
+    a, b = res["1"], res["0"]
+    assert np.array_equal(a.grad_weight.a.view(np.uint32), b.grad_weight.a.view(np.uint32))
+    assert np.array_equal(a.grad_student_hidden.a, b.grad_student_hidden.a)
+    assert (a.loss, a.student_ce, a.teacher_ce, a.kl) == (b.loss, b.student_ce, b.teacher_ce, b.kl)
+    # not vacuous: non-target rows lie on the INT8 grid of their row scale
+    gw = a.grad_weight.a.astype(np.float64)
+    rows = [r for r in range(v) if r not in set(labs)][:50]
+    for r in rows:
+        sc = max(np.abs(gw[r]).max(), 1e-30) / 127.0
+        assert np.allclose(gw[r] / sc, np.round(gw[r] / sc), atol=1e-3)
+
+
+@pytest.mark.parametrize("teacher", ["bf16_values", "fp32_values", "mixed"])
+def test_host_entry_bf16_uploads_are_bit_identical(ob, monkeypatch, teacher):
+    """The host-Mat entry rounds hidden states and weights to bf16 on the host
+    (the device's rounding, ties to even: W holds exact ties here) and sends
+    teacher-logit chunks of bf16 values as bf16, widened exactly on the
+    device; any other chunk, and every chunk after it, crosses as fp32. Each
+    case equals the same call with the device-side conversion
+    (ORDA_HOST_CONVERT=0) bit for bit. V = 70000 gives chunks of 479 rows,
+    so 1024 rows take three; "mixed" turns inexact from row 500 on (inside
+    the second chunk)."""
+    gen = torch.Generator().manual_seed(606)
+    bt, h, v = 1024, 128, 70000
+    s_ = randn_mat(ob, bt, h, gen)
+    wa = (0.05 * torch.randn(v, h, generator=gen)).numpy()
+    bits = wa.view(np.uint32)
+    bits[:64, :8] = (bits[:64, :8] & 0xFFFF0000) | 0x8000  # exact ties between two bf16 values
+    w = ob.Mat.from_array(wa)
+    tl = np.sqrt(2.0) * torch.randn(bt, v, generator=gen).numpy().astype(np.float32)
+    if teacher in ("bf16_values", "mixed"):
+        tb = tl.view(np.uint32)
+        r1 = bt if teacher == "bf16_values" else 500
+        tb[:r1] &= 0xFFFF0000
+    t = ob.Teacher.Precomputed(ob.Mat.from_array(tl))
+    labs = torch.randint(0, v, (bt,), generator=gen).tolist()
+    opts = ob.LossOptions(kd_weight=0.4, temperature=1.5, config=ob.KernelConfig(quantize_grad_weight=True))
+    res = {}
+    for flag in ("1", "0"):
+        monkeypatch.setenv("ORDA_HOST_CONVERT", flag)
+        res[flag] = ob.distillation_loss(s_, w, labs, t, opts)
+    a, b = res["1"], res["0"]
+    assert (a.loss, a.student_ce, a.teacher_ce, a.kl) == (b.loss, b.student_ce, b.teacher_ce, b.kl)
+    assert np.array_equal(a.grad_student_hidden.a.view(np.uint32), b.grad_student_hidden.a.view(np.uint32))
+    assert np.array_equal(a.grad_weight.a.view(np.uint32), b.grad_weight.a.view(np.uint32))
+
+
 # ------------------------------------------------------------ Profile::Fast
 
 # Stated tolerances of Profile::Fast (include/orda.h, OrdaProfile): the CE
