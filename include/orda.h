@@ -221,10 +221,16 @@ ORDA_API int orda_validate(const OrdaMatF32* student_hidden, const OrdaMatF32* w
  * ------------------------------------------------------------------------- */
 
 /* Computes loss, components and gradients on the B200 with the reference's
- * semantics. Inputs are f32 host matrices (pinned or pageable); they are
- * rounded to bf16 on the device (tensor-core operand type). Gradients come
- * back as library-allocated f32 host matrices; free them with
- * orda_output_free(). Runs on device 0 on an internal stream, synchronously. */
+ * semantics. Inputs are f32 host matrices (pinned or pageable); hidden states
+ * and weights are rounded to bf16 (tensor-core operand type), on the host
+ * before they are copied; Precomputed teacher logits keep their fp32 values
+ * (a chunk of them that holds bf16 values only is copied as bf16 and widened
+ * exactly on the device). Gradients come back as library-allocated f32 host
+ * matrices; free them with orda_output_free(). With quantize_grad_weight the
+ * dequantised grad_W is formed on the host from the INT8 codes, scales and
+ * exact target rows (the same float multiply as on the device). Runs on
+ * device 0 on internal streams, synchronously, with up to 16 host worker
+ * threads of its own during the call. */
 ORDA_API int orda_distillation_loss(const OrdaMatF32* student_hidden, const OrdaMatF32* weight, const int64_t* labels,
                            size_t n_labels, const OrdaTeacher* teacher, const OrdaLossOptions* opts,
                            OrdaOutput* out, char* err, size_t err_len);
