@@ -1612,7 +1612,20 @@ int orda_distillation_loss(const OrdaMatF32* student_hidden, const OrdaMatF32* w
   // so the values are bit-identical). ORDA_HOST_DEQUANT=0 copies the fp32
   // grad_W instead (a diagnostic switch). Target rows: non-ignored labels,
   // the rule of target_flags_kernel.
-  const bool host_deq = opts->config.quantize_grad_weight != 0 && host_dequant_enabled();
+  // host workers of the conversions and the dequantisation (one per core,
+  // at most 16: about 90 GB/s of fp32 converted on a 16-core host); without
+  // them the call copies fp32 both ways
+  const bool want_deq = opts->config.quantize_grad_weight != 0 && host_dequant_enabled();
+  const bool want_conv = host_convert_enabled();
+  std::unique_ptr<HostPool> pool;
+  if (want_deq || want_conv) {
+    try {
+      pool = std::make_unique<HostPool>(std::max(1u, std::min(16u, std::thread::hardware_concurrency())));
+    } catch (...) {
+      pool.reset();
+    }
+  }
+  const bool host_deq = want_deq && pool;
   std::vector<int32_t> exact_pos, exact_idx;
   if (host_deq) {
     std::vector<uint8_t> is_target(v, 0);
@@ -1650,7 +1663,7 @@ int orda_distillation_loss(const OrdaMatF32* student_hidden, const OrdaMatF32* w
   // Host conversion: a ring of kRing page-locked bf16 chunks of kChunk
   // elements feeds the copies; bf16 teacher-logit chunks land in a device
   // scratch chunk and are widened into the fp32 teacher rows.
-  const bool host_conv = host_convert_enabled();
+  const bool host_conv = want_conv && pool;
   constexpr size_t kChunk = size_t{32} << 20;  // elements (64 MiB of bf16)
   constexpr int kRing = 3;
   const size_t o_tscr = take(host_conv && pre ? std::max(kChunk, v) * 2 : 0);
@@ -1701,11 +1714,7 @@ int orda_distillation_loss(const OrdaMatF32* student_hidden, const OrdaMatF32* w
     pinned_release(xrows_host);
     for (int b = 0; b < kRing; ++b) pinned_release(ring_host[b]);
   };
-  // host workers of the conversions and the dequantisation (one per core,
-  // at most 16: about 90 GB/s of fp32 converted on a 16-core host)
-  std::unique_ptr<HostPool> pool;
-  if (ok_alloc && (host_conv || host_deq))
-    pool = std::make_unique<HostPool>(std::max(1u, std::min(16u, std::thread::hardware_concurrency())));
+
   if (!ok_alloc) {
     release_landing();
     pinned_release(sc_host);

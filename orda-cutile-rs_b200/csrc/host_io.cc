@@ -218,7 +218,18 @@ void dequant_rows_host(const int8_t* q, const float* scale, const int32_t* exact
 // ------------------------------------------------------------- pool
 
 HostPool::HostPool(unsigned n) : n_(n ? n : 1) {
-  for (unsigned w = 1; w < n_; ++w) threads_.emplace_back([this, w] { loop(w); });
+  try {
+    for (unsigned w = 1; w < n_; ++w) threads_.emplace_back([this, w] { loop(w); });
+  } catch (...) {
+    // a thread could not be started: stop the ones that were, then report
+    {
+      std::lock_guard<std::mutex> lk(mu_);
+      stop_ = true;
+    }
+    cv_.notify_all();
+    for (auto& t : threads_) t.join();
+    throw;
+  }
 }
 
 HostPool::~HostPool() {
