@@ -1052,8 +1052,8 @@ def e2e_host_entry(args, ob, hs, w, tl, labels, opts, D):
         gw_bytes = v * h * 4
     d2h = bt * h * 4 + gw_bytes + 16
     return {"value": bt / per, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-            "ms_per_step": per * 1e3, "api": "orda_distillation_loss (f32 host Mats, pinned inputs)",
-            "scope": "full", "grad_weight_download": ("int8 codes + row scales + exact target rows, dequantised "
+            "ms_per_step": per * 1e3, "calls_ms": [round(t * 1e3, 2) for t in times],
+            "api": "orda_distillation_loss (f32 host Mats, pinned inputs)", "scope": "full", "grad_weight_download": ("int8 codes + row scales + exact target rows, dequantised "
                                                       "on the host" if compressed else "fp32")}
 
 
@@ -1363,7 +1363,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--e2e-steps", type=int, default=2)
+    ap.add_argument("--e2e-steps", type=int, default=4)
     ap.add_argument("--c5-steps", type=int, default=10)
     ap.add_argument("--rows", type=int, default=CFG["bt"],
                     help="rows per GPU (default 8192, the metric's config; smaller values are for profiling only)")
