@@ -942,11 +942,14 @@ bool host_dequant_enabled() {
 }
 
 // The host-Mat entry's bf16 uploads: GEMM operands rounded on the host and
-// teacher-logit chunks that hold bf16 values sent as bf16 (on unless
-// ORDA_HOST_CONVERT=0, a diagnostic switch read on every call).
-bool host_convert_enabled() {
+// teacher-logit chunks that hold bf16 values sent as bf16, while the copy
+// engine is busy (1, the default); 0: fp32 copies only; 2: every chunk
+// through the host passes (a diagnostic switch read on every call, which the
+// tests use to cover the host conversion on small inputs).
+int host_convert_mode() {
   const char* v = std::getenv("ORDA_HOST_CONVERT");
-  return !(v && v[0] == '0');
+  if (!v || !v[0]) return 1;
+  return v[0] == '0' ? 0 : v[0] == '2' ? 2 : 1;
 }
 
 std::mutex g_default_mu;
@@ -1616,7 +1619,8 @@ int orda_distillation_loss(const OrdaMatF32* student_hidden, const OrdaMatF32* w
   // at most 16: about 90 GB/s of fp32 converted on a 16-core host); without
   // them the call copies fp32 both ways
   const bool want_deq = opts->config.quantize_grad_weight != 0 && host_dequant_enabled();
-  const bool want_conv = host_convert_enabled();
+  const int conv_mode = host_convert_mode();
+  const bool want_conv = conv_mode != 0;
   std::unique_ptr<HostPool> pool;
   if (want_deq || want_conv) {
     try {
@@ -1656,16 +1660,18 @@ int orda_distillation_loss(const OrdaMatF32* student_hidden, const OrdaMatF32* w
   const size_t o_ghs = take(bt * h * 4), o_gw = take(v * h * 4);
   const size_t o_ght = take(tgrad ? bt * ht * 4 : 0), o_gwt = take(tgrad && mode == ORDA_TEACHER_SEPARATE ? v * ht * 4 : 0);
   const size_t o_sc = take(4 * sizeof(float));
-  const size_t ring_bytes = std::max(kRingBytes, std::max(h, ht) * 4);
-  const size_t o_ring = take(ring_bytes);
-  const size_t o_q = take(host_deq ? v * h : 0), o_qs = take(host_deq ? v * 4 : 0);
-  const size_t o_xidx = take(n_exact * 4), o_xrows = take(n_exact * h * 4);
   // Host conversion: a ring of kRing page-locked bf16 chunks of kChunk
   // elements feeds the copies; bf16 teacher-logit chunks land in a device
-  // scratch chunk and are widened into the fp32 teacher rows.
+  // scratch chunk and are widened into the fp32 teacher rows. A chunk the
+  // host does not convert crosses as fp32 (GEMM operands through the device
+  // ring and the conversion kernel), so the ring holds a whole chunk.
   const bool host_conv = want_conv && pool;
   constexpr size_t kChunk = size_t{32} << 20;  // elements (64 MiB of bf16)
   constexpr int kRing = 3;
+  const size_t ring_bytes = std::max(std::max(kRingBytes, std::max(h, ht) * 4), host_conv ? kChunk * 4 : 0);
+  const size_t o_ring = take(ring_bytes);
+  const size_t o_q = take(host_deq ? v * h : 0), o_qs = take(host_deq ? v * 4 : 0);
+  const size_t o_xidx = take(n_exact * 4), o_xrows = take(n_exact * h * 4);
   const size_t o_tscr = take(host_conv && pre ? std::max(kChunk, v) * 2 : 0);
   if (ctx->stage_bytes < off) {
     cudaFree(ctx->stage);
@@ -1757,6 +1763,7 @@ int orda_distillation_loss(const OrdaMatF32* student_hidden, const OrdaMatF32* w
   cudaEvent_t ev_ring[kRing] = {nullptr, nullptr, nullptr};
   if (host_conv)
     for (int b = 0; b < kRing; ++b) ev_ring[b] = mk_event();
+  cudaEvent_t ev_queue = host_conv ? mk_event() : nullptr;  // the copier's last copy
   std::thread copier([&]() {
     cudaSetDevice(ctx->device);
     cudaError_t e = cudaMemcpyAsync(S + o_lab, labels, bt * 8, cudaMemcpyHostToDevice, cin);
@@ -1771,14 +1778,46 @@ int orda_distillation_loss(const OrdaMatF32* student_hidden, const OrdaMatF32* w
       return ring_host[*b];
     };
     // f32 host rows -> bf16 on the host -> device rows
+    // Host memory bandwidth, not only PCIe, bounds these copies: a chunk
+    // converted on the host costs 8 bytes of host memory traffic per element
+    // (read fp32, write bf16, the copy reads bf16) against 4 for an fp32
+    // copy, which moves twice the bytes over PCIe. So the copier converts
+    // while the copy engine is busy and sends the next chunk as fp32 when the
+    // engine has run dry: the split follows the host's speed.
+    bool queued = false;
+    auto engine_idle = [&]() -> bool {
+      if (conv_mode == 2) return false;
+      if (!queued) return true;
+      const cudaError_t q = cudaEventQuery(ev_queue);
+      if (q == cudaErrorNotReady) {
+        cudaGetLastError();  // not an error: the copy is still running
+        return false;
+      }
+      return true;
+    };
+    auto mark_queued = [&]() {
+      if (e == cudaSuccess) e = cudaEventRecord(ev_queue, cin);
+      queued = true;
+    };
     auto put_bf16_host = [&](const OrdaMatF32& m, size_t ld, size_t o) {
       const size_t per = std::max<size_t>(1, kChunk / std::max<size_t>(m.cols, 1));
       for (size_t r0 = 0; r0 < m.rows && e == cudaSuccess; r0 += per) {
         const size_t n = std::min(per, m.rows - r0), cnt = n * m.cols;
+        const float* src = m.data + r0 * m.cols;
+        if (engine_idle()) {
+          // fp32 through the device ring and the conversion kernel
+          e = cudaMemcpyAsync(ring, src, cnt * 4, cudaMemcpyHostToDevice, cin);
+          if (e == cudaSuccess) {
+            launch_f32_to_bf16(ring, static_cast<long long>(n), static_cast<long long>(m.cols),
+                               reinterpret_cast<uint16_t*>(S + o) + r0 * ld, static_cast<long long>(ld), cin);
+            e = cudaGetLastError();
+          }
+          mark_queued();
+          continue;
+        }
         int b;
         uint16_t* buf = next_chunk(&b);
         if (e != cudaSuccess) break;
-        const float* src = m.data + r0 * m.cols;
         pool->run([&](unsigned w, unsigned nw) {
           size_t a, z;
           split_range(cnt, nw, w, &a, &z);
@@ -1787,6 +1826,7 @@ int orda_distillation_loss(const OrdaMatF32* student_hidden, const OrdaMatF32* w
         e = cudaMemcpy2DAsync(S + o + r0 * ld * 2, ld * 2, buf, m.cols * 2, m.cols * 2, n, cudaMemcpyHostToDevice,
                               cin);
         if (e == cudaSuccess) e = cudaEventRecord(ev_ring[b], cin);
+        mark_queued();
       }
     };
     // f32 host rows -> ring -> bf16 device rows (one stream: each slab's copy
@@ -1825,6 +1865,12 @@ int orda_distillation_loss(const OrdaMatF32* student_hidden, const OrdaMatF32* w
         const size_t per = std::max<size_t>(1, kChunk / v);
         for (size_t c0 = r0; c0 < r0 + n && e == cudaSuccess && try_bf16; c0 += per) {
           const size_t m = std::min(per, r0 + n - c0), cnt = m * v;
+          if (engine_idle()) {
+            e = cudaMemcpy2DAsync(S + o_tl + c0 * ldtl * 4, ldtl * 4, teacher->logits.data + c0 * v, v * 4, v * 4, m,
+                                  cudaMemcpyHostToDevice, cin);
+            mark_queued();
+            continue;
+          }
           int b;
           uint16_t* buf = next_chunk(&b);
           if (e != cudaSuccess) return;
@@ -1840,6 +1886,7 @@ int orda_distillation_loss(const OrdaMatF32* student_hidden, const OrdaMatF32* w
             // this chunk and the rest of the rows as fp32
             e = cudaMemcpy2DAsync(S + o_tl + c0 * ldtl * 4, ldtl * 4, teacher->logits.data + c0 * v, v * 4, v * 4,
                                   r0 + n - c0, cudaMemcpyHostToDevice, cin);
+            mark_queued();
             return;
           }
           e = cudaMemcpyAsync(S + o_tscr, buf, cnt * 2, cudaMemcpyHostToDevice, cin);
@@ -1850,11 +1897,13 @@ int orda_distillation_loss(const OrdaMatF32* student_hidden, const OrdaMatF32* w
                                     static_cast<long long>(ldtl), cin);
             e = cudaGetLastError();
           }
+          mark_queued();
         }
         return;
       }
       e = cudaMemcpy2DAsync(S + o_tl + r0 * ldtl * 4, ldtl * 4, teacher->logits.data + r0 * v, v * 4, v * 4, n,
                             cudaMemcpyHostToDevice, cin);
+      if (host_conv) mark_queued();
     };
     for (size_t k = 0; k < ev_teacher.size(); ++k) {
       const size_t r0 = k * (group_rows ? group_rows : bt);

@@ -531,8 +531,10 @@ def test_host_entry_bf16_uploads_are_bit_identical(ob, monkeypatch, teacher):
     (the device's rounding, ties to even: W holds exact ties here) and sends
     teacher-logit chunks of bf16 values as bf16, widened exactly on the
     device; any other chunk, and every chunk after it, crosses as fp32. Each
-    case equals the same call with the device-side conversion
-    (ORDA_HOST_CONVERT=0) bit for bit. V = 70000 gives chunks of 479 rows,
+    case, with every chunk through the host passes (ORDA_HOST_CONVERT=2; by
+    default a chunk crosses as fp32 whenever the copy engine is idle), equals
+    the same call with the device-side conversion (ORDA_HOST_CONVERT=0) bit
+    for bit. V = 70000 gives chunks of 479 rows,
     so 1024 rows take three; "mixed" turns inexact from row 500 on (inside
     the second chunk)."""
     gen = torch.Generator().manual_seed(606)
@@ -551,13 +553,14 @@ def test_host_entry_bf16_uploads_are_bit_identical(ob, monkeypatch, teacher):
     labs = torch.randint(0, v, (bt,), generator=gen).tolist()
     opts = ob.LossOptions(kd_weight=0.4, temperature=1.5, config=ob.KernelConfig(quantize_grad_weight=True))
     res = {}
-    for flag in ("1", "0"):
+    for flag in ("2", "1", "0"):  # 2: every chunk through the host conversion; 1: the default split
         monkeypatch.setenv("ORDA_HOST_CONVERT", flag)
         res[flag] = ob.distillation_loss(s_, w, labs, t, opts)
-    a, b = res["1"], res["0"]
-    assert (a.loss, a.student_ce, a.teacher_ce, a.kl) == (b.loss, b.student_ce, b.teacher_ce, b.kl)
-    assert np.array_equal(a.grad_student_hidden.a.view(np.uint32), b.grad_student_hidden.a.view(np.uint32))
-    assert np.array_equal(a.grad_weight.a.view(np.uint32), b.grad_weight.a.view(np.uint32))
+    b = res["0"]
+    for a in (res["2"], res["1"]):
+        assert (a.loss, a.student_ce, a.teacher_ce, a.kl) == (b.loss, b.student_ce, b.teacher_ce, b.kl)
+        assert np.array_equal(a.grad_student_hidden.a.view(np.uint32), b.grad_student_hidden.a.view(np.uint32))
+        assert np.array_equal(a.grad_weight.a.view(np.uint32), b.grad_weight.a.view(np.uint32))
 
 
 # ------------------------------------------------------------ Profile::Fast
