@@ -307,13 +307,19 @@ __device__ __forceinline__ void stage_and_scatter(uint8_t* buf, int lane, const 
   const int sub = lane >> 3;  // row within a group of four
   const int c = lane & 7;     // 16-byte column piece
   const int col = col0 + c * 4;
+  // owner of the chunk's first row; with slices of at least 32 rows the 32
+  // rows of the chunk belong to it or to the next owner (one division per
+  // chunk instead of one per row)
+  const long long o0 = row0 / e.slot_slice;
+  const long long next0 = (o0 + 1) * e.slot_slice;
+  const bool wide_slice = e.slot_slice >= 32;
 #pragma unroll
   for (int it = 0; it < 8; ++it) {
     const int rr = it * 4 + sub;
     const long long g = static_cast<long long>(row0) + rr;
     if (g < p.M && col < p.N) {
       float4 v = *reinterpret_cast<const float4*>(buf + rr * 128 + ((c ^ (rr & 7)) << 4));
-      const long long o = g / e.slot_slice;
+      const long long o = g < next0 ? o0 : (wide_slice ? o0 + 1 : g / e.slot_slice);
       float* dst = e.slot[o] + (static_cast<long long>(e.slot_rank) * e.slot_slice + (g - o * e.slot_slice)) * e.slot_ld +
                    col;
       if (e.beta != 0.0f) {
