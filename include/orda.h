@@ -319,6 +319,14 @@ ORDA_API void orda_context_inject_alloc_failures(OrdaContext* ctx, int count);
  * the reference. */
 ORDA_API int orda_selftest_exp2(const float* x, float* y_fma, float* y_sfu, size_t n, void* stream, char* err,
                                 size_t err_len);
+/* Self-test of the host-side passes of the host-Mat entry (fp32 -> bf16
+ * rounding, the exact bf16 narrowing of teacher logits, the dequantisation
+ * of grad_W), on the host only: every instruction-set version this CPU runs
+ * (scalar, AVX2, AVX-512) against the scalar definitions, over rounding
+ * ties, NaN, infinities, subnormals and misaligned outputs. Returns ORDA_OK
+ * (err then names the versions checked) or ORDA_ERR_BACKEND with the first
+ * difference. Needs no GPU. No counterpart in the reference. */
+ORDA_API int orda_selftest_host_io(char* err, size_t err_len);
 
 /* Element type of a device matrix. Hidden states and weights are bf16 (the
  * tensor-core operand type); Precomputed teacher logits may be bf16 or f32. */

@@ -20,8 +20,13 @@
 
 #include <immintrin.h>
 
+#include <cmath>
+#include <cstdio>
 #include <cstring>
+#include <string>
+#include <vector>
 
+#include "../../include/orda.h"
 #include "bf16_bits.h"
 
 namespace orda {
@@ -181,8 +186,10 @@ Isa isa() {
 
 }  // namespace
 
-void f32_to_bf16_host(const float* src, size_t n, uint16_t* dst) {
-  switch (isa()) {
+namespace {
+
+void to_bf16_isa(Isa k, const float* src, size_t n, uint16_t* dst) {
+  switch (k) {
     case Isa::kAvx512: to_bf16_avx512(src, n, dst); break;
     case Isa::kAvx2: to_bf16_avx2(src, n, dst); break;
     default: to_bf16_scalar(src, n, dst);
@@ -190,9 +197,9 @@ void f32_to_bf16_host(const float* src, size_t n, uint16_t* dst) {
   _mm_sfence();  // the non-temporal stores are visible before the copy reads them
 }
 
-bool f32_to_bf16_if_exact(const float* src, size_t n, uint16_t* dst) {
+bool exact_isa(Isa k, const float* src, size_t n, uint16_t* dst) {
   bool ok;
-  switch (isa()) {
+  switch (k) {
     case Isa::kAvx512: ok = exact_avx512(src, n, dst); break;
     case Isa::kAvx2: ok = exact_avx2(src, n, dst); break;
     default: ok = exact_scalar(src, n, dst);
@@ -201,9 +208,8 @@ bool f32_to_bf16_if_exact(const float* src, size_t n, uint16_t* dst) {
   return ok;
 }
 
-void dequant_rows_host(const int8_t* q, const float* scale, const int32_t* exact_pos, const float* exact_rows,
-                       size_t r0, size_t r1, size_t h, float* out) {
-  const Isa k = isa();
+void dequant_isa(Isa k, const int8_t* q, const float* scale, const int32_t* exact_pos, const float* exact_rows,
+                 size_t r0, size_t r1, size_t h, float* out) {
   for (size_t r = r0; r < r1; ++r) {
     float* o = out + r * h;
     const int32_t e = exact_pos[r];
@@ -214,6 +220,99 @@ void dequant_rows_host(const int8_t* q, const float* scale, const int32_t* exact
   }
   _mm_sfence();
 }
+
+}  // namespace
+
+void f32_to_bf16_host(const float* src, size_t n, uint16_t* dst) { to_bf16_isa(isa(), src, n, dst); }
+
+bool f32_to_bf16_if_exact(const float* src, size_t n, uint16_t* dst) { return exact_isa(isa(), src, n, dst); }
+
+void dequant_rows_host(const int8_t* q, const float* scale, const int32_t* exact_pos, const float* exact_rows,
+                       size_t r0, size_t r1, size_t h, float* out) {
+  dequant_isa(isa(), q, scale, exact_pos, exact_rows, r0, r1, h, out);
+}
+
+// ------------------------------------------------------------ self-test
+
+namespace {
+
+uint32_t lcg(uint64_t* st) {
+  *st = *st * 6364136223846793005ull + 1442695040888963407ull;
+  return static_cast<uint32_t>(*st >> 32);
+}
+
+float from_bits(uint32_t b) {
+  float f;
+  std::memcpy(&f, &b, 4);
+  return f;
+}
+
+const char* isa_name(Isa k) { return k == Isa::kAvx512 ? "avx512" : k == Isa::kAvx2 ? "avx2" : "scalar"; }
+
+// Empty string when every check of ISA k agrees with the scalar definitions.
+std::string check_isa(Isa k) {
+  uint64_t st = 12345;
+  // fp32 -> bf16: special bit patterns, then random ones
+  std::vector<uint32_t> bits = {0x00000000u, 0x80000000u, 0x3F800000u, 0x3F808000u, 0x3F818000u, 0x3F807FFFu,
+                                0x3F808001u, 0x7F7FFFFFu, 0x7F7F7FFFu, 0xFF7FFFFFu, 0x7F800000u, 0xFF800000u,
+                                0x7FC00000u, 0x7F800001u, 0xFFC00001u, 0x7FFFFFFFu, 0x00000001u, 0x00008000u,
+                                0x00018000u, 0x807F8000u, 0x00800000u, 0x3F80FFFFu};
+  for (int i = 0; i < 70000; ++i) bits.push_back(lcg(&st));
+  std::vector<float> src(bits.size());
+  for (size_t i = 0; i < bits.size(); ++i) src[i] = from_bits(bits[i]);
+  for (size_t off : {size_t{0}, size_t{1}, size_t{3}}) {
+    for (size_t n : {bits.size() - off, size_t{33}, size_t{7}}) {
+      std::vector<uint16_t> out(n + 8, 0xABCD);
+      to_bf16_isa(k, src.data() + off, n, out.data() + off % 2);
+      for (size_t i = 0; i < n; ++i)
+        if (out[off % 2 + i] != f32_bits_to_bf16(bits[off + i])) return "f32->bf16 rounding differs";
+    }
+  }
+  // exactness: bf16 values pass, one low bit anywhere fails
+  std::vector<float> ex(1000);
+  for (size_t i = 0; i < ex.size(); ++i) ex[i] = from_bits(lcg(&st) & 0xFFFF0000u);
+  std::vector<uint16_t> hi(ex.size() + 8);
+  for (size_t off : {size_t{0}, size_t{1}}) {
+    if (!exact_isa(k, ex.data(), ex.size(), hi.data() + off)) return "bf16 values reported inexact";
+    for (size_t i = 0; i < ex.size(); ++i) {
+      uint32_t b;
+      std::memcpy(&b, &ex[i], 4);
+      if (hi[off + i] != static_cast<uint16_t>(b >> 16)) return "exact narrowing differs";
+    }
+    for (size_t pos : {size_t{0}, size_t{5}, size_t{500}, ex.size() - 1}) {
+      std::vector<float> bad(ex);
+      uint32_t b;
+      std::memcpy(&b, &bad[pos], 4);
+      bad[pos] = from_bits(b | 0x1u);
+      if (exact_isa(k, bad.data(), bad.size(), hi.data() + off)) return "inexact value not detected";
+    }
+  }
+  // dequantisation: q * s, exact rows copied, odd widths, misaligned output
+  for (size_t h : {size_t{256}, size_t{250}, size_t{17}}) {
+    const size_t rows = 40;
+    std::vector<int8_t> q(rows * h);
+    for (auto& x : q) x = static_cast<int8_t>(static_cast<int>(lcg(&st) % 255u) - 127);
+    std::vector<float> s(rows), xr;
+    std::vector<int32_t> pos(rows, -1);
+    for (size_t r = 0; r < rows; ++r) s[r] = std::ldexp(1.0f + static_cast<float>(lcg(&st) % 1000u) / 999.0f,
+                                                        -static_cast<int>(lcg(&st) % 60u));
+    for (size_t r = 0; r < rows; r += 7) {
+      pos[r] = static_cast<int32_t>(xr.size() / h);
+      for (size_t c = 0; c < h; ++c) xr.push_back(from_bits(lcg(&st) & 0xBFFFFFFFu));
+    }
+    std::vector<float> out(rows * h + 16);
+    float* o = out.data() + 1;
+    dequant_isa(k, q.data(), s.data(), pos.data(), xr.data(), 0, rows, h, o);
+    for (size_t r = 0; r < rows; ++r)
+      for (size_t c = 0; c < h; ++c) {
+        const float want = pos[r] >= 0 ? xr[static_cast<size_t>(pos[r]) * h + c] : static_cast<float>(q[r * h + c]) * s[r];
+        if (std::memcmp(&want, &o[r * h + c], 4) != 0) return "dequantisation differs";
+      }
+  }
+  return std::string();
+}
+
+}  // namespace
 
 // ------------------------------------------------------------- pool
 
@@ -273,3 +372,22 @@ void HostPool::loop(unsigned w) {
 }
 
 }  // namespace orda
+
+extern "C" ORDA_API int orda_selftest_host_io(char* err, size_t err_len) {
+  using namespace orda;
+  std::vector<Isa> isas = {Isa::kScalar};
+  __builtin_cpu_init();
+  if (__builtin_cpu_supports("avx2")) isas.push_back(Isa::kAvx2);
+  if (__builtin_cpu_supports("avx512f")) isas.push_back(Isa::kAvx512);
+  std::string names;
+  for (Isa k : isas) {
+    const std::string why = check_isa(k);
+    if (!why.empty()) {
+      if (err && err_len) std::snprintf(err, err_len, "%s: %s", isa_name(k), why.c_str());
+      return ORDA_ERR_BACKEND;
+    }
+    names += (names.empty() ? "" : ",") + std::string(isa_name(k));
+  }
+  if (err && err_len) std::snprintf(err, err_len, "checked: %s", names.c_str());
+  return ORDA_OK;
+}

@@ -204,6 +204,7 @@ SIGNATURES = {
     "orda_set_host_slab_bytes": (None, [C.c_size_t]),
     "orda_context_set_concurrency": (None, [C.c_void_p, C.c_int]),
     "orda_abi_layout": (C.c_size_t, [C.POINTER(C.POINTER(OrdaFieldLayout))]),
+    "orda_selftest_host_io": (C.c_int, [C.c_char_p, C.c_size_t]),
     "orda_selftest_exp2": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p, C.c_char_p,
                                      C.c_size_t]),
     "orda_context_create": (C.c_int, [C.c_int, C.POINTER(C.c_void_p), C.c_char_p, C.c_size_t]),

@@ -254,6 +254,7 @@ extern "C" {
     pub fn orda_context_selftest_bounded_wait(ctx: *mut OrdaContext, limit_us: u32, stream: *mut c_void,
                                               err: *mut c_char, err_len: usize) -> c_int;
     pub fn orda_context_inject_alloc_failures(ctx: *mut OrdaContext, count: c_int);
+    pub fn orda_selftest_host_io(err: *mut c_char, err_len: usize) -> c_int;
     pub fn orda_selftest_exp2(x: *const f32, y_fma: *mut f32, y_sfu: *mut f32, n: usize, stream: *mut c_void,
                               err: *mut c_char, err_len: usize) -> c_int;
 
