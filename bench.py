@@ -1027,31 +1027,23 @@ def e2e_host_entry(args, ob, hs, w, tl, labels, opts, D):
 
     call()  # warm-up (allocates the staging and page-locked buffers)
     call()  # a fresh host touches its memory for the first time during the first calls
-    times = []
+    times, moved = [], []
+    up, down = C.c_uint64(0), C.c_uint64(0)
     for _ in range(args.e2e_steps):
         t0 = time.perf_counter()
         call()
         times.append(time.perf_counter() - t0)
+        lib.orda_last_call_bytes(C.byref(up), C.byref(down))  # what the call actually copied
+        moved.append((up.value, down.value))
     per = statistics.mean(times)
     bt, h, v = hs.shape[0], CFG["h"], CFG["v"]
-    # bytes over PCIe: with host conversion (the default) h and W cross as
-    # bf16, and the fp32 teacher logits as bf16 when every value is a bf16
-    # value (true here: the workload's teacher logits are bf16); otherwise fp32
-    if os.environ.get("ORDA_HOST_CONVERT", "1")[:1] != "0":
-        tl_exact = not bool((tl_h.view(torch.int32) & 0xFFFF).any())
-        h2d = bt * h * 2 + v * h * 2 + bt * v * (2 if tl_exact else 4) + bt * 8
-    else:
-        h2d = bt * h * 4 + v * h * 4 + bt * v * 4 + bt * 8
-    # with the INT8 round trip grad_W comes back as INT8 codes, row scales
-    # and the exact target rows (one per distinct non-ignored label), and the
-    # library dequantises on the host (ORDA_HOST_DEQUANT=0: fp32 grad_W)
+    # bytes over PCIe, as the library counted them per call: h and W cross as
+    # bf16 or (when the copy engine would otherwise idle) fp32, the teacher
+    # logits as bf16 where they hold bf16 values, grad_W as INT8 codes + scales
+    # + exact target rows with the INT8 round trip; mean over the timed calls
+    h2d = int(round(statistics.mean(m[0] for m in moved)))
+    d2h = int(round(statistics.mean(m[1] for m in moved)))
     compressed = bool(opts.config.quantize_grad_weight) and os.environ.get("ORDA_HOST_DEQUANT", "1")[:1] != "0"
-    if compressed:
-        n_exact = len({int(x) for x in lab_h.tolist() if x != -100})
-        gw_bytes = v * h + v * 4 + n_exact * h * 4
-    else:
-        gw_bytes = v * h * 4
-    d2h = bt * h * 4 + gw_bytes + 16
     return {"value": bt / per, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
             "ms_per_step": per * 1e3, "calls_ms": [round(t * 1e3, 2) for t in times],
             "api": "orda_distillation_loss (f32 host Mats, pinned inputs)", "scope": "full", "grad_weight_download": ("int8 codes + row scales + exact target rows, dequantised "

@@ -245,6 +245,11 @@ ORDA_API void orda_output_free(OrdaOutput* out);
  * Process-wide; no counterpart in the reference (src/api.rs:188-422 has no
  * device copies). */
 ORDA_API void orda_set_host_slab_bytes(size_t bytes);
+/* Bytes the last successful orda_distillation_loss call of this process
+ * copied host->device and device->host (which chunks crossed as bf16 and
+ * whether grad_W came back compressed depend on the call and the host's
+ * speed). Either pointer may be NULL. No counterpart in the reference. */
+ORDA_API void orda_last_call_bytes(uint64_t* h2d, uint64_t* d2h);
 
 /* ---------------------------------------------------------------------------
  * Device entry (replaces the GPU launcher src/cuda/launch.rs:51-158, which

@@ -933,6 +933,8 @@ int check_status(OrdaContext* ctx, char* err, size_t len) {
 
 // Teacher-logit slab of the host entry's copy pipeline (bytes).
 std::atomic<size_t> g_host_slab_bytes{size_t{512} << 20};
+// bytes the last successful host-Mat call copied each way (orda_last_call_bytes)
+std::atomic<uint64_t> g_last_h2d{0}, g_last_d2h{0};
 
 // The host-Mat entry's compressed grad_W download (on unless
 // ORDA_HOST_DEQUANT=0, a diagnostic switch read on every call).
@@ -1764,9 +1766,12 @@ int orda_distillation_loss(const OrdaMatF32* student_hidden, const OrdaMatF32* w
   if (host_conv)
     for (int b = 0; b < kRing; ++b) ev_ring[b] = mk_event();
   cudaEvent_t ev_queue = host_conv ? mk_event() : nullptr;  // the copier's last copy
+  size_t up_copier = 0;                  // bytes the copier sends (read after it joins)
+  size_t up_main = 0, down_main = 0;     // bytes the calling thread copies
   std::thread copier([&]() {
     cudaSetDevice(ctx->device);
     cudaError_t e = cudaMemcpyAsync(S + o_lab, labels, bt * 8, cudaMemcpyHostToDevice, cin);
+    up_copier += bt * 8;
     // next page-locked ring chunk, once the copy that last read it is done
     int slot = 0;
     bool used[kRing] = {false, false, false};
@@ -1807,6 +1812,7 @@ int orda_distillation_loss(const OrdaMatF32* student_hidden, const OrdaMatF32* w
         if (engine_idle()) {
           // fp32 through the device ring and the conversion kernel
           e = cudaMemcpyAsync(ring, src, cnt * 4, cudaMemcpyHostToDevice, cin);
+          up_copier += cnt * 4;
           if (e == cudaSuccess) {
             launch_f32_to_bf16(ring, static_cast<long long>(n), static_cast<long long>(m.cols),
                                reinterpret_cast<uint16_t*>(S + o) + r0 * ld, static_cast<long long>(ld), cin);
@@ -1825,6 +1831,7 @@ int orda_distillation_loss(const OrdaMatF32* student_hidden, const OrdaMatF32* w
         });
         e = cudaMemcpy2DAsync(S + o + r0 * ld * 2, ld * 2, buf, m.cols * 2, m.cols * 2, n, cudaMemcpyHostToDevice,
                               cin);
+        up_copier += cnt * 2;
         if (e == cudaSuccess) e = cudaEventRecord(ev_ring[b], cin);
         mark_queued();
       }
@@ -1836,6 +1843,7 @@ int orda_distillation_loss(const OrdaMatF32* student_hidden, const OrdaMatF32* w
       for (size_t r0 = 0; r0 < m.rows && e == cudaSuccess; r0 += per) {
         const size_t n = std::min(per, m.rows - r0);
         e = cudaMemcpyAsync(ring, m.data + r0 * m.cols, n * m.cols * 4, cudaMemcpyHostToDevice, cin);
+        up_copier += n * m.cols * 4;
         if (e != cudaSuccess) break;
         launch_f32_to_bf16(ring, static_cast<long long>(n), static_cast<long long>(m.cols),
                            reinterpret_cast<uint16_t*>(S + o) + r0 * ld, static_cast<long long>(ld), cin);
@@ -1868,6 +1876,7 @@ int orda_distillation_loss(const OrdaMatF32* student_hidden, const OrdaMatF32* w
           if (engine_idle()) {
             e = cudaMemcpy2DAsync(S + o_tl + c0 * ldtl * 4, ldtl * 4, teacher->logits.data + c0 * v, v * 4, v * 4, m,
                                   cudaMemcpyHostToDevice, cin);
+            up_copier += m * v * 4;
             mark_queued();
             continue;
           }
@@ -1886,10 +1895,12 @@ int orda_distillation_loss(const OrdaMatF32* student_hidden, const OrdaMatF32* w
             // this chunk and the rest of the rows as fp32
             e = cudaMemcpy2DAsync(S + o_tl + c0 * ldtl * 4, ldtl * 4, teacher->logits.data + c0 * v, v * 4, v * 4,
                                   r0 + n - c0, cudaMemcpyHostToDevice, cin);
+            up_copier += (r0 + n - c0) * v * 4;
             mark_queued();
             return;
           }
           e = cudaMemcpyAsync(S + o_tscr, buf, cnt * 2, cudaMemcpyHostToDevice, cin);
+          up_copier += cnt * 2;
           if (e == cudaSuccess) e = cudaEventRecord(ev_ring[b], cin);
           if (e == cudaSuccess) {
             launch_bf16_rows_to_f32(reinterpret_cast<const uint16_t*>(S + o_tscr), static_cast<long long>(m),
@@ -1903,6 +1914,7 @@ int orda_distillation_loss(const OrdaMatF32* student_hidden, const OrdaMatF32* w
       }
       e = cudaMemcpy2DAsync(S + o_tl + r0 * ldtl * 4, ldtl * 4, teacher->logits.data + r0 * v, v * 4, v * 4, n,
                             cudaMemcpyHostToDevice, cin);
+      up_copier += n * v * 4;
       if (host_conv) mark_queued();
     };
     for (size_t k = 0; k < ev_teacher.size(); ++k) {
@@ -1944,6 +1956,8 @@ int orda_distillation_loss(const OrdaMatF32* student_hidden, const OrdaMatF32* w
       out->student_ce = sc_host[1];
       out->teacher_ce = sc_host[2];
       out->kl = sc_host[3];
+      g_last_h2d.store(up_copier + up_main);
+      g_last_d2h.store(down_main);
     } else {
       orda_output_free(out);
     }
@@ -1993,6 +2007,7 @@ int orda_distillation_loss(const OrdaMatF32* student_hidden, const OrdaMatF32* w
   if (cudaError_t e = cudaStreamWaitEvent(st, ev_inputs, 0); e != cudaSuccess) return finish(cuda_fail(e, "event wait", err, err_len));
   if (n_exact > 0) {
     cudaError_t e = cudaMemcpyAsync(S + o_xidx, exact_idx.data(), n_exact * 4, cudaMemcpyHostToDevice, st);
+    up_main += n_exact * 4;
     if (e != cudaSuccess) return finish(cuda_fail(e, "host->device copy", err, err_len));
   }
   HostPipe hp;
@@ -2014,9 +2029,12 @@ int orda_distillation_loss(const OrdaMatF32* student_hidden, const OrdaMatF32* w
     if (e == cudaSuccess)
       e = cudaMemcpyAsync(out->grad_student_hidden.data + g0 * h, dout.grad_student_hidden + g0 * h,
                           (g1 - g0) * h * 4, cudaMemcpyDeviceToHost, cout);
-    if (e == cudaSuccess && tgrad)
+    down_main += (g1 - g0) * h * 4;
+    if (e == cudaSuccess && tgrad) {
       e = cudaMemcpyAsync(out->grad_teacher_hidden.data + g0 * ht, dout.grad_teacher_hidden + g0 * ht,
                           (g1 - g0) * ht * 4, cudaMemcpyDeviceToHost, cout);
+      down_main += (g1 - g0) * ht * 4;
+    }
     return e == cudaSuccess ? ORDA_OK : cuda_fail(e, "device->host copy", err, err_len);
   };
   OrdaChunkPlan plan{};
@@ -2041,6 +2059,7 @@ int orda_distillation_loss(const OrdaMatF32* student_hidden, const OrdaMatF32* w
     if (e == cudaSuccess) e = cudaMemcpyAsync(qs_host, dout.grad_weight_scale, v * 4, cudaMemcpyDeviceToHost, cout);
     if (e == cudaSuccess && n_exact > 0)
       e = cudaMemcpyAsync(xrows_host, xrows_dev, n_exact * h * 4, cudaMemcpyDeviceToHost, cout);
+    down_main += v * 4 + n_exact * h * 4 + v * h;
     if (e == cudaSuccess) e = cudaEventRecord(ev_meta = mk_event(), cout);
     const size_t slab_rows = std::max<size_t>(1, (size_t{32} << 20) / std::max<size_t>(h, 1));
     for (size_t r0 = 0; r0 < v && e == cudaSuccess; r0 += slab_rows) {
@@ -2052,11 +2071,15 @@ int orda_distillation_loss(const OrdaMatF32* student_hidden, const OrdaMatF32* w
     }
   } else if (e == cudaSuccess) {
     e = cudaMemcpyAsync(out->grad_weight.data, dout.grad_weight, v * h * 4, cudaMemcpyDeviceToHost, cout);
+    down_main += v * h * 4;
   }
-  if (e == cudaSuccess && tgrad && mode == ORDA_TEACHER_SEPARATE)
+  if (e == cudaSuccess && tgrad && mode == ORDA_TEACHER_SEPARATE) {
     e = cudaMemcpyAsync(out->grad_teacher_weight.data, dout.grad_teacher_weight, v * ht * 4, cudaMemcpyDeviceToHost,
                         cout);
+    down_main += v * ht * 4;
+  }
   if (e == cudaSuccess) e = cudaMemcpyAsync(sc_host, dout.scalars, 4 * sizeof(float), cudaMemcpyDeviceToHost, cout);
+  down_main += 4 * sizeof(float);
   if (e != cudaSuccess) return finish(cuda_fail(e, "device->host copy", err, err_len));
   if (host_deq) {
     // the workers split each slab's rows once the slab has landed (the
@@ -2083,6 +2106,11 @@ int orda_distillation_loss(const OrdaMatF32* student_hidden, const OrdaMatF32* w
 }
 
 void orda_set_host_slab_bytes(size_t bytes) { g_host_slab_bytes.store(bytes ? bytes : (size_t{512} << 20)); }
+
+void orda_last_call_bytes(uint64_t* h2d, uint64_t* d2h) {
+  if (h2d) *h2d = g_last_h2d.load();
+  if (d2h) *d2h = g_last_d2h.load();
+}
 
 void orda_output_free(OrdaOutput* out) {
   if (!out) return;

@@ -202,6 +202,7 @@ SIGNATURES = {
     ),
     "orda_output_free": (None, [C.POINTER(OrdaOutput)]),
     "orda_set_host_slab_bytes": (None, [C.c_size_t]),
+    "orda_last_call_bytes": (None, [C.POINTER(C.c_uint64), C.POINTER(C.c_uint64)]),
     "orda_context_set_concurrency": (None, [C.c_void_p, C.c_int]),
     "orda_abi_layout": (C.c_size_t, [C.POINTER(C.POINTER(OrdaFieldLayout))]),
     "orda_selftest_host_io": (C.c_int, [C.c_char_p, C.c_size_t]),

@@ -239,6 +239,7 @@ extern "C" {
                                   out: *mut OrdaOutput, err: *mut c_char, err_len: usize) -> c_int;
     pub fn orda_output_free(out: *mut OrdaOutput);
     pub fn orda_set_host_slab_bytes(bytes: usize);
+    pub fn orda_last_call_bytes(h2d: *mut u64, d2h: *mut u64);
 
     pub fn orda_context_create(device: c_int, out: *mut *mut OrdaContext, err: *mut c_char, err_len: usize) -> c_int;
     pub fn orda_context_destroy(ctx: *mut OrdaContext);

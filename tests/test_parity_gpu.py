@@ -12,6 +12,7 @@ Stated tolerances:
 """
 from __future__ import annotations
 
+import ctypes as C
 import os
 
 import numpy as np
@@ -552,10 +553,22 @@ def test_host_entry_bf16_uploads_are_bit_identical(ob, monkeypatch, teacher):
     t = ob.Teacher.Precomputed(ob.Mat.from_array(tl))
     labs = torch.randint(0, v, (bt,), generator=gen).tolist()
     opts = ob.LossOptions(kd_weight=0.4, temperature=1.5, config=ob.KernelConfig(quantize_grad_weight=True))
-    res = {}
+    res, moved = {}, {}
+    lib = ob.load_library()
+    up, down = C.c_uint64(0), C.c_uint64(0)
     for flag in ("2", "1", "0"):  # 2: every chunk through the host conversion; 1: the default split
         monkeypatch.setenv("ORDA_HOST_CONVERT", flag)
         res[flag] = ob.distillation_loss(s_, w, labs, t, opts)
+        lib.orda_last_call_bytes(C.byref(up), C.byref(down))
+        moved[flag] = up.value
+    # bytes over PCIe as counted by the library: labels, the exact-row index
+    # of the compressed download, then h and W (bf16 or fp32) and the teacher
+    # logits (bf16 for the chunks of bf16 values before the first other one)
+    fixed = bt * 8 + 4 * len({x for x in labs if x != -100})
+    assert moved["0"] == fixed + (bt * h + v * h + bt * v) * 4
+    bf16_rows = {"bf16_values": bt, "fp32_values": 0, "mixed": 479}[teacher]
+    assert moved["2"] == fixed + (bt * h + v * h) * 2 + bf16_rows * v * 2 + (bt - bf16_rows) * v * 4
+    assert moved["2"] <= moved["1"] <= moved["0"]
     b = res["0"]
     for a in (res["2"], res["1"]):
         assert (a.loss, a.student_ce, a.teacher_ce, a.kl) == (b.loss, b.student_ce, b.teacher_ce, b.kl)
