@@ -545,7 +545,8 @@ def test_host_entry_bf16_uploads_are_bit_identical(ob, monkeypatch, teacher):
     bits = wa.view(np.uint32)
     bits[:64, :8] = (bits[:64, :8] & 0xFFFF0000) | 0x8000  # exact ties between two bf16 values
     w = ob.Mat.from_array(wa)
-    tl = np.sqrt(2.0) * torch.randn(bt, v, generator=gen).numpy().astype(np.float32)
+    tl = (np.sqrt(2.0) * torch.randn(bt, v, generator=gen)).numpy().astype(np.float32)
+    assert tl.dtype == np.float32  # the bit masking below works on fp32 words
     if teacher in ("bf16_values", "mixed"):
         tb = tl.view(np.uint32)
         r1 = bt if teacher == "bf16_values" else 500
